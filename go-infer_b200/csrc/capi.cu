@@ -1,0 +1,399 @@
+// capi.cu -- the C ABI of include/goinfer_cuda.h: device context, weight
+// buffers, host<->device staging and dispatch to the sm_100a kernels.
+//
+// The reference seam is pkg/metal/metal_bridge.h (+ metal_bridge_darwin.m):
+// a process-wide device/queue, weight buffers created once per tensor, and
+// int-returning GEMV/GEMM entry points that block unless a batch is open.
+// Here the process-wide state is one CUDA stream on one device plus the
+// scratch the stream-K GEMV needs; host-pointer calls stage x/y through a
+// device arena on that stream.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/goinfer_cuda.h"
+#include "gemm.cuh"
+#include "gemv.cuh"
+
+namespace gi {
+int quantize_host(int qtype, const float* src, int64_t rows, int64_t cols, uint8_t* dst,
+                  int threads);
+}
+
+namespace {
+
+thread_local std::string t_err;
+
+struct Buffer {
+  void* dptr = nullptr;
+  size_t bytes = 0;
+  int device = -1;
+};
+
+struct Pending {
+  float* host_y;
+  size_t off;  // in the pinned staging area
+  size_t bytes;
+};
+
+struct Ctx {
+  std::mutex mu;
+  bool ready = false;
+  int device = -1;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  gi::GemvScratch scratch;
+  int* err_host = nullptr;  // mapped pinned word the kernels set when a bounded wait gives up
+  uint8_t* arena = nullptr;  // device activations of host-pointer calls
+  size_t arena_cap = 0, arena_used = 0;
+  uint8_t* pinned = nullptr;  // D2H staging while a batch is open
+  size_t pinned_cap = 0, pinned_used = 0;
+  bool batch = false;
+  bool pdl = false;
+  std::vector<Pending> pending;
+};
+
+Ctx g;
+
+int fail(int code, const char* what, cudaError_t e = cudaSuccess) {
+  char buf[256];
+  if (e != cudaSuccess)
+    std::snprintf(buf, sizeof buf, "%s: %s", what, cudaGetErrorString(e));
+  else
+    std::snprintf(buf, sizeof buf, "%s", what);
+  t_err = buf;
+  return code;
+}
+
+#define GI_CUDA_TRY(call, what)                      \
+  do {                                               \
+    cudaError_t e_ = (call);                         \
+    if (e_ != cudaSuccess) return fail(-5, what, e_); \
+  } while (0)
+
+constexpr int kMaxTiles = 1 << 17;  // rows up to 2,097,152 per GEMV
+
+int init_locked(int device) {
+  if (g.ready) {
+    if (device >= 0 && device != g.device) return fail(-1, "gi_cuda_init: already bound to another device");
+    return cudaSetDevice(g.device) == cudaSuccess ? 0 : fail(-5, "cudaSetDevice");
+  }
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return fail(-1, "no CUDA device");
+  if (device < 0) {
+    const char* env = std::getenv("GOINFER_CUDA_DEVICE");
+    if (env && *env) device = std::atoi(env);
+    else GI_CUDA_TRY(cudaGetDevice(&device), "cudaGetDevice");
+  }
+  if (device < 0 || device >= n) return fail(-1, "gi_cuda_init: device ordinal out of range");
+  GI_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
+  cudaDeviceProp prop;
+  GI_CUDA_TRY(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major < 10) return fail(-1, "gi_cuda_init: the kernels are built for sm_100a");
+  g.sm_count = prop.multiProcessorCount;
+  GI_CUDA_TRY(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (gi::gemv_prepare_device() != 0 || gi::gemm_prepare_device() != 0)
+    return fail(-5, "kernel attribute set-up", cudaGetLastError());
+  g.scratch.max_warps = g.sm_count * 32;
+  g.scratch.max_tiles = kMaxTiles;
+  GI_CUDA_TRY(cudaMalloc(&g.scratch.partials, sizeof(float) * 32 * g.scratch.max_warps), "cudaMalloc scratch");
+  GI_CUDA_TRY(cudaMalloc(&g.scratch.counters, sizeof(unsigned) * kMaxTiles), "cudaMalloc counters");
+  GI_CUDA_TRY(cudaMemset(g.scratch.counters, 0, sizeof(unsigned) * kMaxTiles), "cudaMemset counters");
+  GI_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&g.err_host), sizeof(int), cudaHostAllocMapped),
+              "cudaHostAlloc error word");
+  *g.err_host = 0;
+  GI_CUDA_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&g.scratch.error), g.err_host, 0),
+              "cudaHostGetDevicePointer");
+  g.device = device;
+  g.ready = true;
+  return 0;
+}
+
+int ensure_ready() {
+  if (!g.ready) return fail(-1, "gi_cuda_init has not succeeded");
+  GI_CUDA_TRY(cudaSetDevice(g.device), "cudaSetDevice");
+  return 0;
+}
+
+// Device scratch for activations of host-pointer calls (bump allocator,
+// reset when the call or the batch completes).
+int arena_alloc(size_t bytes, void** out) {
+  bytes = (bytes + 255) & ~(size_t)255;
+  if (g.arena_used + bytes > g.arena_cap) {
+    if (g.arena_used != 0) return fail(-3, "activation arena exhausted inside a batch");
+    if (g.arena) cudaFree(g.arena);
+    g.arena = nullptr;
+    size_t cap = g.arena_cap ? g.arena_cap : (size_t)8 << 20;
+    while (cap < bytes) cap *= 2;
+    GI_CUDA_TRY(cudaMalloc(&g.arena, cap), "cudaMalloc arena");
+    g.arena_cap = cap;
+  }
+  *out = g.arena + g.arena_used;
+  g.arena_used += bytes;
+  return 0;
+}
+
+int pinned_alloc(size_t bytes, size_t* off) {
+  bytes = (bytes + 255) & ~(size_t)255;
+  if (g.pinned_used + bytes > g.pinned_cap) {
+    if (g.pinned_used != 0) return fail(-3, "pinned staging exhausted inside a batch");
+    if (g.pinned) cudaFreeHost(g.pinned);
+    g.pinned = nullptr;
+    size_t cap = g.pinned_cap ? g.pinned_cap : (size_t)8 << 20;
+    while (cap < bytes) cap *= 2;
+    GI_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&g.pinned), cap, cudaHostAllocDefault),
+                "cudaHostAlloc");
+    g.pinned_cap = cap;
+  }
+  *off = g.pinned_used;
+  g.pinned_used += bytes;
+  return 0;
+}
+
+// Finish the host-pointer call: outside a batch wait for the stream.
+// A kernel gave up a bounded wait (reported through the mapped error word).
+int check_device_error() {
+  if (g.err_host && *reinterpret_cast<volatile int*>(g.err_host)) {
+    *g.err_host = 0;
+    return fail(-6, "a device-side wait timed out");
+  }
+  return 0;
+}
+
+int complete_locked() {
+  if (g.batch) return 0;
+  GI_CUDA_TRY(cudaStreamSynchronize(g.stream), "kernel execution");
+  g.arena_used = 0;
+  return check_device_error();
+}
+
+gi::GemvLaunch launch_cfg(bool pdl) {
+  gi::GemvLaunch L;
+  L.sm_count = g.sm_count;
+  L.pdl = pdl;
+  return L;
+}
+
+int run_dev(int qtype, float* y, const float* x, const void* w, size_t w_bytes, int64_t batch,
+            int64_t rows, int64_t cols, cudaStream_t s, bool pdl) {
+  if (batch == 1) {
+    return gi::gemv_launch(qtype, y, x, w, w_bytes, rows, cols, g.scratch, launch_cfg(pdl), s);
+  }
+  return gi::gemm_launch(qtype, y, x, w, w_bytes, batch, rows, cols, g.scratch, launch_cfg(pdl), s);
+}
+
+// y/x on the host, weights on the device.
+int run_host_io(int qtype, float* y, const float* x, const void* wdev, size_t w_bytes,
+                int64_t batch, int64_t rows, int64_t cols) {
+  if (!y || !x) return fail(-4, "null y or x");
+  int rc = batch == 1 ? gi::gemv_check(qtype, rows, cols) : gi::gemm_check(qtype, batch, rows, cols);
+  if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : "unsupported shape");
+  void *xd, *yd;
+  if ((rc = arena_alloc(sizeof(float) * batch * cols, &xd))) return rc;
+  if ((rc = arena_alloc(sizeof(float) * batch * rows, &yd))) return rc;
+  GI_CUDA_TRY(cudaMemcpyAsync(xd, x, sizeof(float) * batch * cols, cudaMemcpyHostToDevice, g.stream),
+              "copy x to device");
+  rc = run_dev(qtype, static_cast<float*>(yd), static_cast<const float*>(xd), wdev, w_bytes, batch,
+               rows, cols, g.stream, false);
+  if (rc) return fail(rc, rc == -4 ? "unsupported shape or buffer too small" : "kernel launch failed",
+                      rc == -5 ? cudaGetLastError() : cudaSuccess);
+  const size_t yb = sizeof(float) * batch * rows;
+  if (g.batch) {
+    size_t off;
+    if ((rc = pinned_alloc(yb, &off))) return rc;
+    GI_CUDA_TRY(cudaMemcpyAsync(g.pinned + off, yd, yb, cudaMemcpyDeviceToHost, g.stream), "copy y to host");
+    g.pending.push_back({y, off, yb});
+    return 0;
+  }
+  GI_CUDA_TRY(cudaMemcpyAsync(y, yd, yb, cudaMemcpyDeviceToHost, g.stream), "copy y to host");
+  return complete_locked();
+}
+
+// Host weights: copy them for this call only (metal_gemv_q4_k wraps them
+// per call too, metal_bridge_darwin.m:3424-3437).
+int run_host_weights(int qtype, float* y, const float* x, const void* w, int64_t batch, int64_t rows,
+                     int64_t cols) {
+  if (!w) return fail(-1, "null weights");
+  const int64_t rb = gi::row_bytes(qtype, cols);
+  if (rb < 0) return fail(-2, "unsupported quant type");
+  const size_t wb = (size_t)(rb * rows);
+  void* wd = nullptr;
+  GI_CUDA_TRY(cudaMalloc(&wd, wb + 64), "cudaMalloc weights");
+  cudaError_t e = cudaMemcpyAsync(wd, w, wb, cudaMemcpyHostToDevice, g.stream);
+  int rc = e == cudaSuccess ? run_host_io(qtype, y, x, wd, wb, batch, rows, cols) : fail(-5, "copy weights", e);
+  if (g.batch) cudaStreamSynchronize(g.stream);  // the weights die with this call
+  cudaFree(wd);
+  return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gi_cuda_init(void) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  return init_locked(-1);
+}
+
+int gi_cuda_init_device(int device) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  return init_locked(device);
+}
+
+bool gi_cuda_is_available(void) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  return g.ready;
+}
+
+void gi_cuda_begin_batch(void) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (g.ready) g.batch = true;
+}
+
+void gi_cuda_end_batch(void) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (!g.ready || !g.batch) return;
+  g.batch = false;
+  cudaSetDevice(g.device);
+  const cudaError_t e = cudaStreamSynchronize(g.stream);
+  if (e != cudaSuccess) fail(-5, "batched kernels", e);
+  else
+    for (const Pending& p : g.pending) std::memcpy(p.host_y, g.pinned + p.off, p.bytes);
+  check_device_error();
+  g.pending.clear();
+  g.pinned_used = 0;
+  g.arena_used = 0;
+}
+
+gi_cuda_buffer_t gi_cuda_create_buffer(const void* ptr, size_t bytes) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (!ptr || bytes == 0 || ensure_ready()) return nullptr;
+  Buffer* b = new Buffer;
+  // 64 bytes of slack: kernels never read past `bytes`, the slack only keeps
+  // the allocation a multiple of the 16-byte vector width.
+  if (cudaMalloc(&b->dptr, bytes + 64) != cudaSuccess) {
+    fail(-3, "cudaMalloc buffer");
+    delete b;
+    return nullptr;
+  }
+  cudaMemsetAsync(static_cast<uint8_t*>(b->dptr) + bytes, 0, 64, g.stream);
+  if (cudaMemcpyAsync(b->dptr, ptr, bytes, cudaMemcpyHostToDevice, g.stream) != cudaSuccess ||
+      cudaStreamSynchronize(g.stream) != cudaSuccess) {
+    fail(-3, "copy buffer to device");
+    cudaFree(b->dptr);
+    delete b;
+    return nullptr;
+  }
+  b->bytes = bytes;
+  b->device = g.device;
+  return b;
+}
+
+void gi_cuda_release_buffer(gi_cuda_buffer_t buf) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (!buf) return;
+  Buffer* b = static_cast<Buffer*>(buf);
+  if (g.ready) {
+    cudaSetDevice(b->device);
+    cudaStreamSynchronize(g.stream);
+  }
+  cudaFree(b->dptr);
+  delete b;
+}
+
+const void* gi_cuda_buffer_device_ptr(gi_cuda_buffer_t buf) {
+  return buf ? static_cast<Buffer*>(buf)->dptr : nullptr;
+}
+
+size_t gi_cuda_buffer_bytes(gi_cuda_buffer_t buf) { return buf ? static_cast<Buffer*>(buf)->bytes : 0; }
+
+int gi_cuda_gemv_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t w_buf, uint32_t rows,
+                     uint32_t cols) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!w_buf) return fail(-1, "null weight buffer");
+  const Buffer* b = static_cast<const Buffer*>(w_buf);
+  return run_host_io(quant_type, y, x, b->dptr, b->bytes, 1, rows, cols);
+}
+
+int gi_cuda_gemm_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t w_buf,
+                     uint32_t batch_size, uint32_t rows, uint32_t cols) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!w_buf) return fail(-1, "null weight buffer");
+  if (batch_size == 0) return fail(-4, "batch_size must be >= 1");
+  const Buffer* b = static_cast<const Buffer*>(w_buf);
+  return run_host_io(quant_type, y, x, b->dptr, b->bytes, batch_size, rows, cols);
+}
+
+#define GI_HOST_GEMV(name, qt)                                                            \
+  int name(float* y, const float* x, const void* w, uint32_t rows, uint32_t cols) {        \
+    std::lock_guard<std::mutex> lk(g.mu);                                                  \
+    if (int rc = ensure_ready()) return rc;                                                \
+    return run_host_weights(qt, y, x, w, 1, rows, cols);                                   \
+  }
+GI_HOST_GEMV(gi_cuda_gemv_q8_0, GI_TYPE_Q8_0)
+GI_HOST_GEMV(gi_cuda_gemv_q4_k, GI_TYPE_Q4_K)
+GI_HOST_GEMV(gi_cuda_gemv_q6_k, GI_TYPE_Q6_K)
+
+#define GI_HOST_GEMM(name, qt)                                                                \
+  int name(float* y, const float* x, const void* w, uint32_t batch, uint32_t rows, uint32_t cols) { \
+    std::lock_guard<std::mutex> lk(g.mu);                                                      \
+    if (int rc = ensure_ready()) return rc;                                                    \
+    if (batch == 0) return fail(-4, "batch_size must be >= 1");                                \
+    return run_host_weights(qt, y, x, w, batch, rows, cols);                                   \
+  }
+GI_HOST_GEMM(gi_cuda_gemm_q8_0, GI_TYPE_Q8_0)
+GI_HOST_GEMM(gi_cuda_gemm_q4_k, GI_TYPE_Q4_K)
+GI_HOST_GEMM(gi_cuda_gemm_q6_k, GI_TYPE_Q6_K)
+
+int gi_cuda_gemv_dev(int quant_type, float* y, const float* x, const void* w, size_t w_bytes,
+                     uint32_t rows, uint32_t cols, void* stream) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!y || !x || !w) return fail(-4, "null device pointer");
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+  const int rc = run_dev(quant_type, y, x, w, w_bytes, 1, rows, cols, s, g.pdl);
+  if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : rc == -4 ? "unsupported shape" : "launch failed",
+                      rc == -5 ? cudaGetLastError() : cudaSuccess);
+  return 0;
+}
+
+int gi_cuda_gemm_dev(int quant_type, float* y, const float* x, const void* w, size_t w_bytes,
+                     uint32_t batch_size, uint32_t rows, uint32_t cols, void* stream) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!y || !x || !w) return fail(-4, "null device pointer");
+  if (batch_size == 0) return fail(-4, "batch_size must be >= 1");
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+  const int rc = run_dev(quant_type, y, x, w, w_bytes, batch_size, rows, cols, s, g.pdl);
+  if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : rc == -4 ? "unsupported shape" : "launch failed",
+                      rc == -5 ? cudaGetLastError() : cudaSuccess);
+  return 0;
+}
+
+int gi_cuda_set_pdl(int enable) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  g.pdl = enable != 0;
+  return 0;
+}
+
+const char* gi_cuda_last_error(void) { return t_err.c_str(); }
+
+int64_t gi_quant_row_bytes(int quant_type, int64_t cols) { return gi::row_bytes(quant_type, cols); }
+
+int gi_quantize(int quant_type, const float* src, int64_t rows, int64_t cols, void* dst, int threads) {
+  if (!src || !dst) return fail(-4, "null pointer");
+  if (threads <= 0) threads = (int)std::thread::hardware_concurrency();
+  const int rc = gi::quantize_host(quant_type, src, rows, cols, static_cast<uint8_t*>(dst), threads);
+  if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : "unsupported shape");
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,52 @@
+// gemv.cuh -- decode-time quantised GEMV (y = W x, batch 1) for sm_100a.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gi {
+
+// GGML type ids (pkg/gguf/types.go:25-52 of go-infer).
+enum : int { kTypeF32 = 0, kTypeQ8_0 = 8, kTypeQ4_K = 12, kTypeQ6_K = 14 };
+
+// Device scratch used by the stream-K Q4_K GEMV to combine row tiles that
+// straddle two CTAs: two 16-float partial slots per CTA and one arrival
+// counter per 16-row tile.  Counters must start at zero; every launch leaves
+// them at zero again.  `error` is set to 1 when a bounded device wait gives
+// up (never expected; the host reports GI_ERR_TIMEOUT).
+struct GemvScratch {
+  float* partials = nullptr;     // [max_warps][2][16] (max_warps bounds the CTA count)
+  unsigned* counters = nullptr;  // [max_tiles]
+  int* error = nullptr;
+  int max_warps = 0;
+  int max_tiles = 0;
+};
+
+struct GemvLaunch {
+  int sm_count = 148;
+  bool pdl = false;  // programmatic dependent launch (weights must not be
+                     // written by the preceding kernel)
+};
+
+// Per-device one-time set-up (kernel attributes); call with the device current.
+int gemv_prepare_device();
+
+// Bytes of one row of `cols` weights of `qtype` (gemv.go:99,135,171).
+int64_t row_bytes(int qtype, int64_t cols);
+
+// Shape rules: rows >= 1; cols a positive multiple of 256 (Q4_K, Q6_K) or
+// 32 (Q8_0); Q4_K cols <= 30464 (activation staging in shared memory).
+// Returns 0, -2 unsupported type, -4 bad shape, -5 CUDA launch error.
+int gemv_check(int qtype, int64_t rows, int64_t cols);
+
+// Scratch sizes the Q4_K launch needs for this shape (zero for other types).
+void gemv_scratch_need(int qtype, int64_t rows, int64_t cols, const GemvLaunch& L,
+                       int* warps, int* tiles);
+
+// y[rows] = W[rows x cols] * x[cols]; every pointer is device memory.
+// `w_bytes` bounds the weight reads (no access beyond w + w_bytes).
+int gemv_launch(int qtype, float* y, const float* x, const void* w, size_t w_bytes,
+                int64_t rows, int64_t cols, const GemvScratch& s, const GemvLaunch& L,
+                cudaStream_t stream);
+
+}  // namespace gi

@@ -1,0 +1,243 @@
+// quantize.cpp -- host quantisers that produce GGUF Q8_0 / Q4_K / Q6_K rows.
+//
+// Model-preparation tooling (the counterpart of go-infer's cmd/quantize),
+// not part of the GEMV path.  Q8_0 follows go-infer's own QuantizeQ8_0
+// (pkg/quant/quant.go:407-455) including its truncating fp16 conversion
+// (pkg/quant/fp16.go:38-69).  go-infer ships no Q4_K or Q6_K quantiser, so
+// those two are this library's own min/max fits written from the block
+// formats that DequantizeQ4_K / DequantizeQ6_K decode
+// (pkg/quant/quant.go:215-291).  Every step is a single IEEE float32
+// operation, so the result is deterministic across compilers.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "gemv.cuh"
+
+namespace gi {
+namespace {
+
+inline uint32_t f2u(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  return u;
+}
+inline float u2f(uint32_t u) {
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+// fp32 -> fp16 by truncation of the mantissa, as go-infer's FP32ToFP16.
+uint16_t f32_to_f16_trunc(float val) {
+  const uint32_t bits = f2u(val);
+  const uint32_t sign = (bits >> 16) & 0x8000u;
+  int exp = (int)((bits >> 23) & 0xFF);
+  uint32_t mant = bits & 0x007FFFFFu;
+  if (exp == 255) return (uint16_t)(sign | (mant ? 0x7E00u : 0x7C00u));
+  exp = exp - 127 + 15;
+  if (exp >= 31) return (uint16_t)(sign | 0x7C00u);
+  if (exp <= 0) {
+    if (exp < -10) return (uint16_t)sign;
+    mant = (mant | 0x00800000u) >> (1 - exp);
+    return (uint16_t)(sign | (mant >> 13));
+  }
+  return (uint16_t)(sign | ((uint32_t)exp << 10) | (mant >> 13));
+}
+
+// Exact fp16 -> fp32 for every finite value.
+float f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1F, mant = h & 0x3FFu;
+  if (exp == 0) {
+    if (mant == 0) return u2f(sign);
+    exp = 1;
+    while (!(mant & 0x400u)) {
+      mant <<= 1;
+      exp--;
+    }
+    mant &= 0x3FFu;
+    return u2f(sign | ((exp + 112) << 23) | (mant << 13));
+  }
+  if (exp == 0x1F) return u2f(sign | 0x7F800000u | (mant << 13));
+  return u2f(sign | ((exp + 112) << 23) | (mant << 13));
+}
+
+inline void put16(uint8_t* p, uint16_t v) {
+  p[0] = (uint8_t)(v & 0xFF);
+  p[1] = (uint8_t)(v >> 8);
+}
+
+// QuantizeQ8_0 for one row of `n` floats (n a multiple of 32).
+void q8_0_row(const float* src, int64_t n, uint8_t* out) {
+  for (int64_t b = 0; b < n / 32; ++b) {
+    const float* s = src + 32 * b;
+    float maxv = 0.f;
+    for (int i = 0; i < 32; ++i) {
+      const float v = std::fabs(s[i]);
+      if (v > maxv) maxv = v;
+    }
+    float scale = maxv / 127.0f;
+    uint16_t h = 0;
+    if (scale > 0) {
+      h = f32_to_f16_trunc(scale);
+      scale = f16_to_f32(h);
+    }
+    const float inv = scale > 0 ? 1.0f / scale : 0.f;
+    uint8_t* o = out + 34 * b;
+    put16(o, h);
+    for (int i = 0; i < 32; ++i) {
+      int8_t q = 0;
+      if (inv > 0) {
+        float v = s[i] * inv;
+        if (v > 127) v = 127;
+        else if (v < -128) v = -128;
+        q = (int8_t)std::round(v);
+      }
+      o[2 + i] = (uint8_t)q;
+    }
+  }
+}
+
+inline float clampf(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+// Q4_K super-block fit: per 32-weight sub-block j, w ~ d*sc_j*q - dmin*m_j
+// with q in [0,15] and 6-bit sc_j, m_j.  The offset m_j*dmin covers the
+// sub-block minimum (clipped at 0), the step d*sc_j its range / 15; d and
+// dmin put the largest step / offset at 63 and go through the truncating
+// fp16 conversion the repository uses for every block scale.
+void q4_k_block(const float* w, uint8_t* out) {
+  float step[8], off[8];
+  float max_step = 0.f, max_off = 0.f;
+  for (int j = 0; j < 8; ++j) {
+    float lo = 0.f, hi = w[32 * j];
+    for (int i = 0; i < 32; ++i) {
+      const float v = w[32 * j + i];
+      if (v < lo) lo = v;
+      if (v > hi) hi = v;
+    }
+    step[j] = (hi - lo) / 15.0f;
+    off[j] = -lo;
+    if (step[j] > max_step) max_step = step[j];
+    if (off[j] > max_off) max_off = off[j];
+  }
+  const uint16_t dh = f32_to_f16_trunc(max_step / 63.0f);
+  const uint16_t mh = f32_to_f16_trunc(max_off / 63.0f);
+  const float d = f16_to_f32(dh), dmin = f16_to_f32(mh);
+  uint8_t sc[8], mn[8];
+  for (int j = 0; j < 8; ++j) {
+    sc[j] = d > 0 ? (uint8_t)clampf(std::round(step[j] / d), 0.f, 63.f) : 0;
+    mn[j] = dmin > 0 ? (uint8_t)clampf(std::round(off[j] / dmin), 0.f, 63.f) : 0;
+  }
+  put16(out, dh);
+  put16(out + 2, mh);
+  uint8_t* scales = out + 4;
+  // Inverse of getScaleMin (pkg/quant/quant.go:228-235).
+  for (int j = 0; j < 4; ++j) {
+    scales[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+    scales[j + 4] = (uint8_t)((mn[j] & 63) | ((mn[j + 4] >> 4) << 6));
+    scales[j + 8] = (uint8_t)((sc[j + 4] & 0xF) | ((mn[j + 4] & 0xF) << 4));
+  }
+  uint8_t q[256];
+  for (int j = 0; j < 8; ++j) {
+    const float ds = d * (float)sc[j];
+    const float dm = dmin * (float)mn[j];
+    for (int i = 0; i < 32; ++i) {
+      float v = 0.f;
+      if (ds > 0) v = clampf(std::round((w[32 * j + i] + dm) / ds), 0.f, 15.f);
+      q[32 * j + i] = (uint8_t)v;
+    }
+  }
+  // Nibble order of DequantizeQ4_K (pkg/quant/quant.go:237-249).
+  uint8_t* qs = out + 16;
+  for (int c = 0; c < 4; ++c)
+    for (int l = 0; l < 32; ++l)
+      qs[32 * c + l] = (uint8_t)(q[64 * c + l] | (q[64 * c + 32 + l] << 4));
+}
+
+// Q6_K super-block fit: per 16-weight sub-block s, w ~ d*sc_s*q with
+// q in [-32,31] and int8 sc_s; step = max|w| / 31, d puts the largest step
+// at 127.  Layout of DequantizeQ6_K (pkg/quant/quant.go:263-286).
+void q6_k_block(const float* w, uint8_t* out) {
+  float step[16], max_step = 0.f;
+  for (int s = 0; s < 16; ++s) {
+    float amax = 0.f;
+    for (int i = 0; i < 16; ++i) {
+      const float v = std::fabs(w[16 * s + i]);
+      if (v > amax) amax = v;
+    }
+    step[s] = amax / 31.0f;
+    if (step[s] > max_step) max_step = step[s];
+  }
+  const uint16_t dh = f32_to_f16_trunc(max_step / 127.0f);
+  const float d = f16_to_f32(dh);
+  int8_t sc[16];
+  for (int s = 0; s < 16; ++s)
+    sc[s] = d > 0 ? (int8_t)clampf(std::round(step[s] / d), -128.f, 127.f) : 0;
+  uint8_t q[256];  // stored as q + 32
+  for (int s = 0; s < 16; ++s) {
+    const float ds = d * (float)sc[s];
+    for (int i = 0; i < 16; ++i) {
+      float v = 0.f;
+      if (ds > 0) v = clampf(std::round(w[16 * s + i] / ds), -32.f, 31.f);
+      q[16 * s + i] = (uint8_t)((int)v + 32);
+    }
+  }
+  uint8_t* ql = out;
+  uint8_t* qh = out + 128;
+  std::memset(out, 0, 210);
+  for (int n = 0; n < 2; ++n)
+    for (int l = 0; l < 32; ++l) {
+      const int b = 128 * n + l;
+      const uint8_t q1 = q[b], q2 = q[b + 32], q3 = q[b + 64], q4 = q[b + 96];
+      ql[64 * n + l] = (uint8_t)((q1 & 0xF) | ((q3 & 0xF) << 4));
+      ql[64 * n + l + 32] = (uint8_t)((q2 & 0xF) | ((q4 & 0xF) << 4));
+      qh[32 * n + l] = (uint8_t)((q1 >> 4) | ((q2 >> 4) << 2) | ((q3 >> 4) << 4) | ((q4 >> 4) << 6));
+    }
+  for (int s = 0; s < 16; ++s) out[192 + s] = (uint8_t)sc[s];
+  put16(out + 208, dh);
+}
+
+}  // namespace
+
+// Quantise rows x cols floats into `dst` (rows * row_bytes(qtype, cols)
+// bytes), splitting rows over `threads` host threads.
+int quantize_host(int qtype, const float* src, int64_t rows, int64_t cols, uint8_t* dst,
+                  int threads) {
+  const int64_t block = qtype == kTypeQ8_0 ? 32 : 256;
+  if (qtype != kTypeQ8_0 && qtype != kTypeQ4_K && qtype != kTypeQ6_K) return -2;
+  if (rows < 1 || cols < block || cols % block) return -4;
+  const int64_t rb = row_bytes(qtype, cols);
+  auto work = [&](int64_t r0, int64_t r1) {
+    for (int64_t r = r0; r < r1; ++r) {
+      const float* s = src + r * cols;
+      uint8_t* o = dst + r * rb;
+      if (qtype == kTypeQ8_0) {
+        q8_0_row(s, cols, o);
+      } else {
+        for (int64_t b = 0; b < cols / 256; ++b) {
+          if (qtype == kTypeQ4_K) q4_k_block(s + 256 * b, o + 144 * b);
+          else q6_k_block(s + 256 * b, o + 210 * b);
+        }
+      }
+    }
+  };
+  if (threads < 1) threads = 1;
+  if (threads > rows) threads = (int)rows;
+  if (threads == 1) {
+    work(0, rows);
+    return 0;
+  }
+  std::vector<std::thread> pool;
+  const int64_t chunk = (rows + threads - 1) / threads;
+  for (int i = 0; i < threads; ++i) {
+    const int64_t r0 = i * chunk, r1 = r0 + chunk < rows ? r0 + chunk : rows;
+    if (r0 < r1) pool.emplace_back(work, r0, r1);
+  }
+  for (auto& th : pool) th.join();
+  return 0;
+}
+
+}  // namespace gi

@@ -1,0 +1,141 @@
+/*
+ * goinfer_cuda.h -- C ABI of the B200 (sm_100a) engine for go-infer's
+ * quantised matrix-vector hot path.
+ *
+ * This is the CUDA counterpart of go-infer's GPU plugin seam
+ * pkg/metal/metal_bridge.h: the same entry points (gi_cuda_* for metal_*),
+ * the same argument meaning (GGML quant type ids, row-major raw GGUF weight
+ * blocks with rows = output features, fp32 activations, y[b*rows + r] /
+ * x[b*cols + k] for batches) and the same int status convention (0 = ok,
+ * negative = failure, which the Go wrapper turns into an error and the
+ * engine answers by falling back, pkg/engine/weights.go:251-289).  Every
+ * declaration names the reference declaration it replaces
+ * (file:line within abmarcum/go-infer).
+ *
+ * Plain C types only: no CUDA or torch types cross this boundary; streams
+ * are passed as void* (a cudaStream_t, NULL = the library's own stream).
+ *
+ * Threading: one process per GPU.  Calls on one device are serialised by
+ * an internal mutex (the pattern of CModelContext, c_bridge_cgo.go:19-82).
+ */
+#ifndef GOINFER_CUDA_H
+#define GOINFER_CUDA_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  -1..-3 keep metal_bridge_darwin.m's meaning (:3349,3361,
+ * 3377): unavailable / no buffer, unsupported quant type, buffer failure. */
+#define GI_OK 0
+#define GI_ERR_UNAVAILABLE (-1)
+#define GI_ERR_UNSUPPORTED_TYPE (-2)
+#define GI_ERR_BUFFER (-3)
+#define GI_ERR_SHAPE (-4)   /* cols not a multiple of the block, size too small, misaligned */
+#define GI_ERR_CUDA (-5)    /* CUDA runtime error; text in gi_cuda_last_error() */
+#define GI_ERR_TIMEOUT (-6) /* a bounded device-side wait gave up */
+
+/* GGML quant type ids, pkg/gguf/types.go:25-52. */
+#define GI_TYPE_F32 0
+#define GI_TYPE_Q8_0 8
+#define GI_TYPE_Q4_K 12
+#define GI_TYPE_Q6_K 14
+
+/* Replaces int metal_init(void), metal_bridge.h:13.  Selects the device in
+ * $GOINFER_CUDA_DEVICE, else the calling thread's current CUDA device;
+ * idempotent. */
+int gi_cuda_init(void);
+
+/* Like gi_cuda_init for an explicit device ordinal (no reference
+ * counterpart: Metal has one device). */
+int gi_cuda_init_device(int device);
+
+/* Replaces bool metal_is_available(void), metal_bridge.h:16. */
+bool gi_cuda_is_available(void);
+
+/* Replace void metal_begin_batch(void) / metal_end_batch(void),
+ * metal_bridge.h:19-20: between the two calls the host-pointer entry points
+ * enqueue without waiting; their y outputs are written at end_batch. */
+void gi_cuda_begin_batch(void);
+void gi_cuda_end_batch(void);
+
+/* Replaces metal_buffer_t / metal_create_buffer(const void*, size_t),
+ * metal_bridge.h:44-45.  Copies `bytes` host bytes into device memory once
+ * (Metal wraps unified memory without a copy); the handle stays valid
+ * until gi_cuda_release_buffer.  NULL on failure. */
+typedef void* gi_cuda_buffer_t;
+gi_cuda_buffer_t gi_cuda_create_buffer(const void* ptr, size_t bytes);
+
+/* Replaces void metal_release_buffer(metal_buffer_t), metal_bridge.h:46. */
+void gi_cuda_release_buffer(gi_cuda_buffer_t buf);
+
+/* Replaces int metal_gemv_buf(int quant_type, float* y, const float* x,
+ * metal_buffer_t w_buf, uint32_t rows, uint32_t cols), metal_bridge.h:49:
+ * y[rows] = W x with host y/x and a device-resident weight buffer.
+ * quant_type: GI_TYPE_Q8_0, GI_TYPE_Q4_K or GI_TYPE_Q6_K. */
+int gi_cuda_gemv_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t w_buf,
+                     uint32_t rows, uint32_t cols);
+
+/* Replaces int metal_gemm_buf(int quant_type, float* y, const float* x,
+ * metal_buffer_t w_buf, uint32_t batch_size, uint32_t rows, uint32_t cols),
+ * metal_bridge.h:50: Y[batch][rows] = X[batch][cols] W^T (prefill). */
+int gi_cuda_gemm_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t w_buf,
+                     uint32_t batch_size, uint32_t rows, uint32_t cols);
+
+/* Replace metal_gemv_q8_0 / metal_gemv_q4_k / metal_gemv_q6_k,
+ * metal_bridge.h:181-183: host y, x and host weight bytes (copied per call). */
+int gi_cuda_gemv_q8_0(float* y, const float* x, const void* w, uint32_t rows, uint32_t cols);
+int gi_cuda_gemv_q4_k(float* y, const float* x, const void* w, uint32_t rows, uint32_t cols);
+int gi_cuda_gemv_q6_k(float* y, const float* x, const void* w, uint32_t rows, uint32_t cols);
+
+/* Replace metal_gemm_q8_0 / metal_gemm_q4_k / metal_gemm_q6_k,
+ * metal_bridge.h:187-189. */
+int gi_cuda_gemm_q8_0(float* y, const float* x, const void* w, uint32_t batch_size, uint32_t rows,
+                      uint32_t cols);
+int gi_cuda_gemm_q4_k(float* y, const float* x, const void* w, uint32_t batch_size, uint32_t rows,
+                      uint32_t cols);
+int gi_cuda_gemm_q6_k(float* y, const float* x, const void* w, uint32_t batch_size, uint32_t rows,
+                      uint32_t cols);
+
+/* ---- Device-pointer entry points (the measured path; no reference
+ * counterpart, Metal's buffers are host-visible).  y, x and w are device
+ * pointers; x 16-byte aligned, Q4_K weights 16-byte aligned; w_bytes bounds
+ * every weight read.  Asynchronous on `stream` (NULL = library stream). */
+int gi_cuda_gemv_dev(int quant_type, float* y, const float* x, const void* w, size_t w_bytes,
+                     uint32_t rows, uint32_t cols, void* stream);
+int gi_cuda_gemm_dev(int quant_type, float* y, const float* x, const void* w, size_t w_bytes,
+                     uint32_t batch_size, uint32_t rows, uint32_t cols, void* stream);
+
+/* Device address / size of a buffer created by gi_cuda_create_buffer. */
+const void* gi_cuda_buffer_device_ptr(gi_cuda_buffer_t buf);
+size_t gi_cuda_buffer_bytes(gi_cuda_buffer_t buf);
+
+/* Launch kernels with programmatic dependent launch (1) or plainly (0,
+ * default).  With it on, a GEMV starts streaming its weights while the
+ * previous kernel on the stream drains; weights must then not be written by
+ * the kernel just before. */
+int gi_cuda_set_pdl(int enable);
+
+/* Text of the last failure on the calling thread ("" if none). */
+const char* gi_cuda_last_error(void);
+
+/* Bytes of one weight row, pkg/math/gemv.go:99,135,171; -1 for an
+ * unsupported type. */
+int64_t gi_quant_row_bytes(int quant_type, int64_t cols);
+
+/* Host quantiser (the counterpart of cmd/quantize/main.go:52-158): rows x
+ * cols fp32 -> GGUF blocks in dst (rows * gi_quant_row_bytes bytes).
+ * GI_TYPE_Q8_0 is go-infer's QuantizeQ8_0 (pkg/quant/quant.go:407-455);
+ * GI_TYPE_Q4_K / GI_TYPE_Q6_K are this library's own fits (go-infer has no
+ * K-quant quantiser).  threads <= 0 uses every host core. */
+int gi_quantize(int quant_type, const float* src, int64_t rows, int64_t cols, void* dst,
+                int threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GOINFER_CUDA_H */

@@ -1,0 +1,64 @@
+"""The C-ABI library without a GPU: it loads, exports exactly what
+include/goinfer_cuda.h declares, and answers with the status codes of the
+metal_bridge convention when no device is bound."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import goinfer_cuda as G
+from _util import ROOT
+
+HEADER = os.path.join(ROOT, "include", "goinfer_cuda.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(gi_\w+)\s*\(", text))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = G.load_library()
+    names = declared_functions()
+    assert names == set(G.EXPORTS)
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_header_compiles_as_c():
+    import subprocess, tempfile
+    with tempfile.TemporaryDirectory() as d:
+        src = os.path.join(d, "t.c")
+        open(src, "w").write('#include "goinfer_cuda.h"\nint main(void){return GI_TYPE_Q4_K == 12 ? 0 : 1;}\n')
+        subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.dirname(HEADER), src,
+                        "-o", os.path.join(d, "t")], check=True)
+
+
+def test_row_bytes_follow_gemv_go():
+    # pkg/math/gemv.go:99,135,171
+    assert G.row_bytes(G.TYPE_Q8_0, 4096) == 128 * 34
+    assert G.row_bytes(G.TYPE_Q4_K, 4096) == 16 * 144
+    assert G.row_bytes(G.TYPE_Q6_K, 11008) == 43 * 210
+    assert G.row_bytes(3, 4096) == -1
+
+
+@pytest.mark.skipif(os.path.exists("/dev/nvidia0"), reason="a GPU is present")
+def test_no_device_status_codes():
+    lib = G.load_library()
+    assert lib.gi_cuda_init() == G.ERR_UNAVAILABLE
+    assert not G.IsAvailable()
+    y = np.zeros(16, np.float32)
+    x = np.zeros(256, np.float32)
+    raw = np.zeros(16 * 144, np.uint8)
+    rc = lib.gi_cuda_gemv_q4_k(y.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                               x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                               ctypes.c_void_p(raw.ctypes.data), 16, 256)
+    assert rc == G.ERR_UNAVAILABLE
+    assert G.CreateBuffer(raw) is None  # nil handle, as metal.CreateBuffer
+    with pytest.raises(G.GoInferCudaError) as e:
+        G.MatMulQ4_K(y, x, raw, 16, 256)
+    assert e.value.code == G.ERR_UNAVAILABLE
+    assert "init" in lib.gi_cuda_last_error().decode()

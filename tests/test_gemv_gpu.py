@@ -1,0 +1,238 @@
+"""GPU parity of the decode GEMV against the CPU oracle, through the C ABI.
+
+Every case feeds the same raw GGUF bytes and fp32 activations to the CUDA
+library and to the restatement of go-infer's GEMVEngine.MatMul*
+(oracle/goinfer_ref.c) and requires per-element relative error <= 1e-3
+(denominator floored at 1e-2 * rms(ref), see tests/_util.py).  The tests
+mirror the reference's own GPU tests (pkg/metal/metal_test.go) where those
+exist.
+"""
+import struct
+
+import numpy as np
+import pytest
+
+import goinfer_cuda as G
+import oracle as O
+from _util import GOLDEN, assert_parity, rel_err, seeded_weights, seeded_x
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda():
+    G.Init(0)
+    assert G.IsAvailable()
+    yield
+
+
+def gpu_gemv(qt, raw, x, rows, cols):
+    buf = G.CreateBuffer(raw)
+    try:
+        y = np.full(rows, np.nan, np.float32)
+        G.MatMulBuf(qt, y, np.ascontiguousarray(x, np.float32), buf, rows, cols)
+        return y
+    finally:
+        G.ReleaseBuffer(buf)
+
+
+def f16(v):
+    return O.fp32_to_fp16(float(v))
+
+
+# ---------------------------------------------- reference GPU tests, mirrored
+
+def test_metal_gemv_q4_k_kat():
+    # pkg/metal/metal_test.go:127-164
+    raw = bytearray()
+    for _ in range(2):
+        raw += struct.pack("<HH", f16(1.0), f16(0.0)) + bytes([1] * 12) + bytes([0x22] * 128)
+    y = np.zeros(2, np.float32)
+    G.MatMulQ4_K(y, np.ones(256, np.float32), bytes(raw), 2, 256)
+    assert np.all(np.abs(y - 512.0) <= 1e-2)
+
+
+def test_metal_gemv_q8_0_kat():
+    # pkg/metal/metal_test.go:91-125
+    raw = bytearray()
+    for _ in range(4):
+        raw += struct.pack("<H", f16(0.25)) + bytes([4] * 32)
+    y = np.zeros(4, np.float32)
+    G.MatMulQ8_0(y, np.ones(32, np.float32), bytes(raw), 4, 32)
+    assert np.all(np.abs(y - 32.0) <= 1e-3)
+
+
+def test_q8_0_fused_dot_kat_through_gpu():
+    # pkg/quant/quant_test.go:55-83 on the GPU: 1 row, 2 blocks
+    raw = bytearray()
+    for _ in range(2):
+        raw += struct.pack("<H", f16(0.5)) + bytes((j - 16) & 0xFF for j in range(32))
+    x = np.arange(1, 65, dtype=np.float32)
+    y = np.zeros(1, np.float32)
+    G.MatMulQ8_0(y, x, bytes(raw), 1, 64)
+    ref = O.dot_vec(O.GGML_Q8_0, x, np.frombuffer(bytes(raw), np.uint8), 64)
+    assert abs(y[0] - ref) <= 1e-4 * max(1.0, abs(ref))
+
+
+# ------------------------------------------------------------ golden vectors
+
+def test_golden_vectors():
+    g = np.load(f"{GOLDEN}/gemv_golden.npz")
+    for name in sorted({k.split("__")[0] for k in g.files}):
+        qt, rows, cols = (int(v) for v in g[name + "__shape"])
+        y = gpu_gemv(qt, g[name + "__w"], g[name + "__x"], rows, cols)
+        assert_parity(y, g[name + "__y"], what=name)
+
+
+# ------------------------------------------------ seeded parity, config shapes
+
+CONFIG_SHAPES = [
+    ("config1 Q8_0 4096x4096", G.TYPE_Q8_0, 4096, 4096, 1, 2),
+    ("config2 Q4_K gate 11008x4096", G.TYPE_Q4_K, 11008, 4096, 3, 4),
+    ("config2 Q4_K down 4096x11008", G.TYPE_Q4_K, 4096, 11008, 5, 6),
+    ("lm_head Q6_K 32000x4096", G.TYPE_Q6_K, 32000, 4096, 10, 11),
+]
+
+
+@pytest.mark.parametrize("what,qt,rows,cols,ws,xs", CONFIG_SHAPES, ids=[c[0] for c in CONFIG_SHAPES])
+def test_config_shapes_match_oracle(what, qt, rows, cols, ws, xs):
+    w = seeded_weights(ws, rows, cols)
+    raw = G.quantize(qt, w)
+    x = seeded_x(xs, cols)
+    y = gpu_gemv(qt, raw, x, rows, cols)
+    ref = O.matmul(qt, x, raw, rows, cols)
+    worst = assert_parity(y, ref, what=what)
+    # the GPU sits as close to the exact product as the reference itself does
+    exact = O.matmul_f64(qt, x, raw, rows, cols)
+    scale = np.sqrt(np.mean(exact ** 2))
+    assert np.max(np.abs(y - exact)) <= 4 * np.max(np.abs(ref - exact)) + 1e-6 * scale
+    print(f"{what}: max rel err {worst:.2e}")
+
+
+@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
+@pytest.mark.parametrize("rows,cols", [(1, 256), (17, 256), (33, 512), (16, 4096), (100, 1280), (3, 11008)])
+def test_small_and_ragged_shapes(qt, rows, cols):
+    w = seeded_weights(rows * 7 + cols, rows, cols)
+    raw = G.quantize(qt, w)
+    x = seeded_x(cols + 1, cols)
+    y = gpu_gemv(qt, raw, x, rows, cols)
+    assert_parity(y, O.matmul(qt, x, raw, rows, cols), what=f"{qt} {rows}x{cols}")
+
+
+@pytest.mark.parametrize("rows,cols", [(32, 96), (7, 160), (50, 32)])
+def test_q8_0_rows_not_16_byte_aligned(rows, cols):
+    w = seeded_weights(rows + cols, rows, cols)
+    raw = G.quantize(G.TYPE_Q8_0, w)
+    x = seeded_x(3, cols)
+    y = gpu_gemv(G.TYPE_Q8_0, raw, x, rows, cols)
+    assert_parity(y, O.matmul(G.TYPE_Q8_0, x, raw, rows, cols))
+
+
+def test_70b_shapes_on_row_samples():
+    # 70B-shaped projections (d=8192, FFN 28672): check a random row subset
+    # against the oracle, and linearity of the whole output.
+    rng = np.random.default_rng(12)
+    for rows, cols in [(28672, 8192), (8192, 28672)]:
+        w = seeded_weights(rows + 1, rows, cols)
+        raw = G.quantize(G.TYPE_Q4_K, w)
+        rb = G.row_bytes(G.TYPE_Q4_K, cols)
+        x1, x2 = seeded_x(20, cols), seeded_x(21, cols)
+        buf = G.CreateBuffer(raw)
+        y1, y2, y12 = (np.zeros(rows, np.float32) for _ in range(3))
+        G.MatMulBuf(G.TYPE_Q4_K, y1, x1, buf, rows, cols)
+        G.MatMulBuf(G.TYPE_Q4_K, y2, x2, buf, rows, cols)
+        G.MatMulBuf(G.TYPE_Q4_K, y12, x1 + x2, buf, rows, cols)
+        G.ReleaseBuffer(buf)
+        pick = np.sort(rng.choice(rows, 256, replace=False))
+        sub = np.concatenate([raw[r * rb:(r + 1) * rb] for r in pick])
+        assert_parity(y1[pick], O.matmul(G.TYPE_Q4_K, x1, sub, len(pick), cols))
+        assert np.max(rel_err(y12, (y1.astype(np.float64) + y2))) < 1e-3
+
+
+def test_activation_scaling_extremes():
+    rows, cols = 64, 4096
+    raw = G.quantize(G.TYPE_Q4_K, seeded_weights(30, rows, cols))
+    for mag in (1e-30, 1e-6, 1.0, 3e3, 1e7):
+        x = seeded_x(31, cols) * np.float32(mag)
+        x[::97] *= 50  # outliers, as LLM activations have
+        y = gpu_gemv(G.TYPE_Q4_K, raw, x, rows, cols)
+        assert_parity(y, O.matmul(G.TYPE_Q4_K, x, raw, rows, cols), what=f"|x|~{mag}")
+    y = gpu_gemv(G.TYPE_Q4_K, raw, np.zeros(cols, np.float32), rows, cols)
+    assert np.all(y == 0)
+
+
+def test_deterministic_and_device_path_identical():
+    import torch
+    rows, cols = 4096, 11008
+    raw = G.quantize(G.TYPE_Q4_K, seeded_weights(5, rows, cols))
+    x = seeded_x(6, cols)
+    a = gpu_gemv(G.TYPE_Q4_K, raw, x, rows, cols)
+    b = gpu_gemv(G.TYPE_Q4_K, raw, x, rows, cols)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    wd = torch.from_numpy(raw).cuda()
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty(rows, dtype=torch.float32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for pdl in (False, True):
+        G.set_pdl(pdl)
+        G.gemv_dev(G.TYPE_Q4_K, yd.data_ptr(), xd.data_ptr(), wd.data_ptr(), raw.size, rows, cols, s)
+        torch.cuda.synchronize()
+        assert np.array_equal(yd.cpu().numpy().view(np.uint32), a.view(np.uint32))
+    G.set_pdl(False)
+
+
+def test_batch_mode_defers_outputs():
+    rows, cols = 256, 1024
+    raws = [G.quantize(qt, seeded_weights(40 + i, rows, cols)) for i, qt in
+            enumerate((G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0))]
+    bufs = [G.CreateBuffer(r) for r in raws]
+    xs = [seeded_x(50 + i, cols) for i in range(3)]
+    ys = [np.zeros(rows, np.float32) for _ in range(3)]
+    G.BeginBatch()
+    for qt, buf, x, y in zip((G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0), bufs, xs, ys):
+        G.MatMulBuf(qt, y, x, buf, rows, cols)
+    G.EndBatch()
+    for qt, raw, x, y in zip((G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0), raws, xs, ys):
+        assert_parity(y, O.matmul(qt, x, raw, rows, cols))
+    for b in bufs:
+        G.ReleaseBuffer(b)
+
+
+def test_weights_dispatch_mirror():
+    ws = G.Weights()
+    raw = G.quantize(G.TYPE_Q4_K, seeded_weights(60, 512, 4096))
+    ws.add("blk.0.ffn_gate.weight", G.TYPE_Q4_K, 512, 4096, raw)
+    x = seeded_x(61, 4096)
+    y = np.zeros(512, np.float32)
+    ws.MatMul(y, x, "blk.0.ffn_gate.weight", 512, 4096)
+    assert_parity(y, O.matmul(G.TYPE_Q4_K, x, raw, 512, 4096))
+    ws.Close()
+
+
+def test_error_codes():
+    raw = np.zeros(16 * 144, np.uint8)
+    buf = G.CreateBuffer(raw)
+    y = np.zeros(16, np.float32)
+    with pytest.raises(G.GoInferCudaError) as e:
+        G.MatMulBuf(G.TYPE_Q4_K, y, np.zeros(200, np.float32), buf, 16, 200)  # cols % 256 != 0
+    assert e.value.code == G.ERR_SHAPE
+    with pytest.raises(G.GoInferCudaError) as e:
+        G.MatMulBuf(3, y, np.zeros(256, np.float32), buf, 16, 256)  # not a supported type
+    assert e.value.code == G.ERR_UNSUPPORTED_TYPE
+    with pytest.raises(G.GoInferCudaError) as e:
+        G.MatMulBuf(G.TYPE_Q4_K, np.zeros(32, np.float32), np.zeros(256, np.float32), buf, 32, 256)
+    assert e.value.code == G.ERR_SHAPE  # buffer too small for 32 rows
+    G.ReleaseBuffer(buf)
+
+
+def test_prefill_batch_matches_per_token_oracle():
+    batch, rows, cols = 5, 96, 512
+    for qt in (G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0):
+        raw = G.quantize(qt, seeded_weights(70, rows, cols))
+        x = np.random.default_rng(71).normal(size=(batch, cols)).astype(np.float32)
+        buf = G.CreateBuffer(raw)
+        y = np.zeros(batch * rows, np.float32)
+        G.MatMulBatchBuf(qt, y, x.reshape(-1), buf, batch, rows, cols)
+        G.ReleaseBuffer(buf)
+        ref = O.matmul_batch(qt, x, raw, batch, rows, cols)
+        assert_parity(y, ref.reshape(-1), what=f"batch {qt}")
