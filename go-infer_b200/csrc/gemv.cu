@@ -8,13 +8,8 @@
 // Q4_K kernel: one small CTA per SM, each owning a contiguous run of 16-row
 // tiles.  Its 8 warps stream their units' raw super-blocks into per-warp
 // shared-memory rings with cp.async (up to 4 units ahead, the first ones
-// requested before the kernel waits on its predecessor), turn the 4-bit quants and 6-bit
-// sub-block scales into exact fp16 products q*sc with one HFMA2 per two
-// weights and multiply them on the tensor cores (mma.m16n8k16, fp32
-// accumulate) against the activation split into exact fp16 hi+lo halves.
-// The 6-bit mins ride along as a 17th MMA against per-half-sub-block
-// activation sums.  Tiles split between warps are summed in fixed warp
-// order through shared memory (deterministic).
+// requested before the kernel waits on its predecessor) and take exact
+// integer dot products on the int8 tensor cores (see namespace q4k).
 //
 // Q8_0 / Q6_K kernels: 4 rows per warp, fp32 CUDA-core dot products.  Their
 // 34- and 210-byte blocks are only 2-byte aligned, so each warp stages its
@@ -24,6 +19,15 @@
 #include "gemv.cuh"
 
 namespace gi {
+
+// Every kernel of the library runs with the same (maximum) shared-memory
+// carveout, so that kernels that follow each other under programmatic
+// dependent launch can share an SM without a carveout change draining it.
+template <typename K>
+cudaError_t set_max_shared_carveout(K kernel) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                              (int)cudaSharedmemCarveoutMaxShared);
+}
 
 int64_t row_bytes(int qtype, int64_t cols) {
   switch (qtype) {
@@ -42,20 +46,27 @@ namespace q4k {
 // in fixed warp order through shared memory (deterministic).  Each warp
 // streams its units through a private ring of shared-memory stages with
 // cp.async (16 bytes per lane, L1-bypassing, S units in flight, the first
-// ones issued before the kernel waits on its predecessor); every lane
-// stages exactly the quants it later reads, so a per-thread wait suffices
-// (plus one warp barrier for the row headers).  Keeping the prefetch out of
-// registers leaves the compiler room to interleave the decode/MMA chains.
+// ones requested before the kernel waits on its predecessor).
+//
+// Arithmetic: integer tensor cores.  The 4-bit quants enter an int8 MMA
+// (m16n8k32) unchanged except for one mask per 4 weights (low nibbles as
+// q, high nibbles as 16*q); the activations enter as four balanced base-256
+// limbs of a 30-bit fixed-point value per 256-column unit
+// (x = 2^-e * sum_n L_n 256^(3-n), |x| < 2^(30-e); exact for every value
+// within 7 binades of the unit's largest, absolute error <= 2^-31 of it
+// otherwise).  Every product and sum of a sub-block is therefore exact in
+// int32; the 6-bit sub-block scales are applied with integer multiply-adds,
+// and a unit's total leaves the integer domain once, through 4 int->float
+// conversions per lane.  The 6-bit mins ride on one fp16 MMA against the
+// per-sub-block activation sums (hi+lo fp16 split).
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kUnitVec = 68;      // uint4 of staged activations per 256 columns
-constexpr int kStageBytes = 2304;  // q: 4 x [32 lanes][16 B], headers: [16 rows][16 B]
+constexpr int kUnitX = 1104;       // staged activation bytes per unit (see stage_unit)
+constexpr int kStageBytes = 2304;  // qs: [16 rows][4 chunks, swizzled][32 B], headers: [16 rows][16 B]
 constexpr int kMaxCols = 45056;
 constexpr int kSmemMax = 227 * 1024;
 constexpr int kCoresidentSmem = 110 * 1024;  // fits two CTAs (this kernel and the next) per SM
-constexpr uint32_t kMagic = 0x64006400u;  // f16x2 (1024, 1024)
-constexpr uint32_t kMul = 0x2C003C00u;    // f16x2 (1, 1/16)
-constexpr uint32_t kAdd = 0xD400E400u;    // f16x2 (-1024, -64)
+constexpr uint32_t kMagic = 0x64006400u;     // f16x2 (1024, 1024)
 
 struct Params {
   const uint8_t* w;
@@ -66,76 +77,75 @@ struct Params {
   int x_off, slot_off;  // dynamic smem byte offsets (rings at 0)
 };
 
-struct Raw {
-  uint4 hA, qA0, qA1, hB, qB0, qB1;
-};
+// Byte k of each of four words, gathered into one word (byte i from w_i).
+GI_DEVINL uint32_t gather_byte(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t k) {
+  const uint32_t lo = prmt(w0, w1, k | ((4u + k) << 4));
+  const uint32_t hi = prmt(w2, w3, k | ((4u + k) << 4));
+  return prmt(lo, hi, 0x5410u);
+}
 
-// Activations for the MMAs, per 256-column unit (68 x 16 B):
-//   [i=0..7][g=0..1][t=0..3] 16 B: the B fragments of thread (g,t) for
-//     MMA pair i (g=0: hi halves, g=1: lo halves), in the k order the
-//     weight decode produces (see compute_unit);
-//   [64..67]: the min-MMA fragments, 8 B per (g-2, t): sums of x over the
-//     16-element half sub-blocks thread t covers, hi/lo split.
-// Each unit's activations are scaled by their own power of two 2^e (2^(e-4)
-// for the sums) so that max|x| < 2^15 keeps the fp16 halves exact; the
-// unit's 2^-e goes to s_inv[u] and into the epilogue multiplier.  One warp
-// stages a unit: lane (i, tt) loads the 8 values of its fragments; a warp
-// requests up to 4 units' values before converting any.
-GI_DEVINL void stage_unit(uint4* xs, float* s_inv, int u, float4 a, float4 b, int lane) {
-  const int i = lane >> 2, tt = lane & 3;
+// Activations of one unit (256 columns) in shared memory at xu:
+//   [0, 1024)    int8 limbs, [sub-block j][limb n][element l], limb 0 the
+//                most significant; sub-block j covers columns
+//                64*(j/2) + 32*(j%2) + l, as Q4_K's getScaleMin indexes them;
+//   [1024, 1088) min-MMA B fragments: for t = 0..3, 8 bytes:
+//                f16 (X_t hi, X_t lo, X_{t+4} hi, X_{t+4} lo), X_j the sum
+//                of sub-block j scaled by 2^em;
+//   [1088, 1096) float 2^-e, float 2^-em.
+// One warp stages a unit; lane L owns elements 8*(L%4) .. +7 of
+// sub-block L/4 (a: the first four, b: the next four).
+GI_DEVINL void stage_unit(uint8_t* xu, float4 a, float4 b, int lane) {
   float m = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
                   fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
   m = warp_max(m);
-  int e = 0;
-  if (m > 0.f && m <= 3.0e38f) e = min(100, max(-100, 14 - ilogbf(m)));
-  const float s = exp2i(e);
-  float ah[4], al[4], bh[4], bl[4];
-  split_hi_lo(a.x * s, ah[0], al[0]);
-  split_hi_lo(a.y * s, ah[1], al[1]);
-  split_hi_lo(a.z * s, ah[2], al[2]);
-  split_hi_lo(a.w * s, ah[3], al[3]);
-  split_hi_lo(b.x * s, bh[0], bl[0]);
-  split_hi_lo(b.y * s, bh[1], bl[1]);
-  split_hi_lo(b.z * s, bh[2], bl[2]);
-  split_hi_lo(b.w * s, bh[3], bl[3]);
-  uint4 hi, lo;
-  hi.x = pack_h2(ah[0], ah[2]);
-  hi.y = pack_h2(bh[0], bh[2]);
-  hi.z = pack_h2(ah[1], ah[3]);
-  hi.w = pack_h2(bh[1], bh[3]);
-  lo.x = pack_h2(al[0], al[2]);
-  lo.y = pack_h2(bl[0], bl[2]);
-  lo.z = pack_h2(al[1], al[3]);
-  lo.w = pack_h2(bl[1], bl[3]);
-  xs[u * kUnitVec + i * 8 + tt] = hi;
-  xs[u * kUnitVec + i * 8 + 4 + tt] = lo;
-  // Half-sub-block sums: this lane's 4 values, then over w (lane bits 2-3).
-  float sa = (a.x + a.y) + (a.z + a.w);
-  float sb = (b.x + b.y) + (b.z + b.w);
-  sa += __shfl_xor_sync(0xffffffffu, sa, 4);
-  sb += __shfl_xor_sync(0xffffffffu, sb, 4);
-  sa += __shfl_xor_sync(0xffffffffu, sa, 8);
-  sb += __shfl_xor_sync(0xffffffffu, sb, 8);
-  const float sa1 = __shfl_down_sync(0xffffffffu, sa, 16);  // v = 1 half sums
-  const float sb1 = __shfl_down_sync(0xffffffffu, sb, 16);
-  if (lane < 4) {
-    const float sm = exp2i(e - 4);
-    float Xh[4], Xl[4];
-    split_hi_lo(sa * sm, Xh[0], Xl[0]);
-    split_hi_lo(sb * sm, Xh[1], Xl[1]);
-    split_hi_lo(sa1 * sm, Xh[2], Xl[2]);
-    split_hi_lo(sb1 * sm, Xh[3], Xl[3]);
-    uint2* m2 = reinterpret_cast<uint2*>(xs + u * kUnitVec + 64);
-    m2[tt] = make_uint2(pack_h2(Xh[0], Xh[1]), pack_h2(Xh[2], Xh[3]));
-    m2[4 + tt] = make_uint2(pack_h2(Xl[0], Xl[1]), pack_h2(Xl[2], Xl[3]));
+  int e = 0, em = 0;
+  if (m > 0.f && m <= 3.0e38f) {
+    const int lg = ilogbf(m);
+    e = min(126, max(-126, 29 - lg));  // max |x| * 2^e < 2^30
+    em = min(126, max(-126, 9 - lg));  // max |X| <= 32 max |x|: X * 2^em < 2^15
   }
-  if (lane == 0) s_inv[u] = exp2i(-e);
+  const float s = exp2i(e);
+  // Balanced base-256 digits of v are the bytes of (v + 0x80808080) ^ 0x80808080.
+  uint32_t u[8];
+  u[0] = ((uint32_t)__float2int_rn(a.x * s) + 0x80808080u) ^ 0x80808080u;
+  u[1] = ((uint32_t)__float2int_rn(a.y * s) + 0x80808080u) ^ 0x80808080u;
+  u[2] = ((uint32_t)__float2int_rn(a.z * s) + 0x80808080u) ^ 0x80808080u;
+  u[3] = ((uint32_t)__float2int_rn(a.w * s) + 0x80808080u) ^ 0x80808080u;
+  u[4] = ((uint32_t)__float2int_rn(b.x * s) + 0x80808080u) ^ 0x80808080u;
+  u[5] = ((uint32_t)__float2int_rn(b.y * s) + 0x80808080u) ^ 0x80808080u;
+  u[6] = ((uint32_t)__float2int_rn(b.z * s) + 0x80808080u) ^ 0x80808080u;
+  u[7] = ((uint32_t)__float2int_rn(b.w * s) + 0x80808080u) ^ 0x80808080u;
+  const int j = lane >> 2, q = lane & 3;
+  const uint32_t base = smem_u32(xu) + j * 128 + 8 * q;
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    const uint32_t k = 3u - (uint32_t)n;  // limb n is byte 3-n
+    const uint32_t lo = gather_byte(u[0], u[1], u[2], u[3], k);
+    const uint32_t hi = gather_byte(u[4], u[5], u[6], u[7], k);
+    sts64(base + n * 32, (uint64_t)lo | ((uint64_t)hi << 32));
+  }
+  float sx = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
+  sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+  sx += __shfl_xor_sync(0xffffffffu, sx, 2);  // sub-block sum, in lanes 4j..4j+3
+  const float xs = sx * exp2i(em);
+  const float Xa = __shfl_sync(0xffffffffu, xs, 4 * q);       // X_q
+  const float Xb = __shfl_sync(0xffffffffu, xs, 16 + 4 * q);  // X_{q+4}
+  if (lane < 4) {
+    float ah, al, bh, bl;
+    split_hi_lo(Xa, ah, al);
+    split_hi_lo(Xb, bh, bl);
+    sts64(smem_u32(xu) + 1024 + 8 * lane, (uint64_t)pack_h2(ah, al) | ((uint64_t)pack_h2(bh, bl) << 32));
+  }
+  if (lane == 0) {
+    reinterpret_cast<float*>(xu + 1088)[0] = exp2i(-e);
+    reinterpret_cast<float*>(xu + 1088)[1] = exp2i(-em);
+  }
 }
 
-__device__ void stage_x(uint4* xs, float* s_inv, const float* __restrict__ x, int nku) {
+__device__ void stage_x(uint8_t* xs, const float* __restrict__ x, int nku) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int i = lane >> 2, tt = lane & 3;
-  const int off = 64 * ((tt >> 1) + 2 * (i >> 2)) + 16 * (tt & 1) + 4 * (i & 3);
+  const int j = lane >> 2, q = lane & 3;
+  const int off = 64 * (j >> 1) + 32 * (j & 1) + 8 * q;
   for (int u0 = warp; u0 < nku; u0 += 4 * kWarps) {
     float4 a[4], b[4];
 #pragma unroll
@@ -143,81 +153,86 @@ __device__ void stage_x(uint4* xs, float* s_inv, const float* __restrict__ x, in
       const int u = u0 + k * kWarps;
       if (u < nku) {
         a[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off));
-        b[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off + 32));
+        b[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off + 4));
       }
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int u = u0 + k * kWarps;
-      if (u < nku) stage_unit(xs, s_inv, u, a[k], b[k], lane);
+      if (u < nku) stage_unit(xs + u * kUnitX, a[k], b[k], lane);
     }
   }
   __syncthreads();
 }
 
-// Scales and mins of the four sub-blocks thread t covers, as exact f16x2:
-// (sc[p], sc[p+1]), (sc[p+4], sc[p+5]) and the same for the mins, with
-// p = 2*(t>>1).  This is getScaleMin (pkg/quant/quant.go:228-235) for two
-// sub-blocks at a time.
-GI_DEVINL void decode_scales(const uint4& h, uint32_t sh, uint32_t& sc0, uint32_t& sc1,
-                             uint32_t& mn0, uint32_t& mn1) {
-  const uint32_t a = h.y >> sh, b = h.z >> sh, c = h.w >> sh;
-  const uint32_t s01 = a & 0x3F3Fu, n01 = b & 0x3F3Fu;
-  const uint32_t s45 = (c & 0x0F0Fu) | ((a >> 2) & 0x3030u);
-  const uint32_t n45 = ((c >> 4) & 0x0F0Fu) | ((b >> 2) & 0x3030u);
-  sc0 = hsub2_u32(prmt(s01, 0x6464u, 0x5140u), kMagic);
-  sc1 = hsub2_u32(prmt(s45, 0x6464u, 0x5140u), kMagic);
-  mn0 = hsub2_u32(prmt(n01, 0x6464u, 0x5140u), kMagic);
-  mn1 = hsub2_u32(prmt(n45, 0x6464u, 0x5140u), kMagic);
-}
-
-// One unit: 16 rows (g, g+8 for this thread) x 256 columns.
-GI_DEVINL void compute_unit(const Raw& r, const uint4* __restrict__ xsu, int g, int t,
-                            uint32_t sh, uint32_t fshift, float fmul, float& yA, float& yB) {
-  uint32_t scA[2], scB[2], mnA[2], mnB[2];
-  decode_scales(r.hA, sh, scA[0], scA[1], mnA[0], mnA[1]);
-  decode_scales(r.hB, sh, scB[0], scB[1], mnB[0], mnB[1]);
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // one MMA chain per v
+// One unit: rows g and g+8 of a 16-row tile, 256 columns.  stage: the raw
+// super-blocks in shared memory; xu: the unit's staged activations.
+GI_DEVINL void compute_unit(uint32_t stage, uint32_t xu, int g, int t, uint32_t sh8, float W0, float W1,
+                            float& yA, float& yB) {
+  const uint4 hA = lds128(stage + 2048 + g * 16);
+  const uint4 hB = lds128(stage + 2048 + (g + 8) * 16);
+  // 6-bit scales sc0..sc7 as bytes (getScaleMin, pkg/quant/quant.go:228-235)
+  const uint32_t sA03 = hA.y & 0x3F3F3F3Fu, sB03 = hB.y & 0x3F3F3F3Fu;
+  const uint32_t sA47 = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
+  const uint32_t sB47 = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
+  int loA0 = 0, loA1 = 0, loB0 = 0, loB1 = 0, hiA0 = 0, hiA1 = 0, hiB0 = 0, hiB1 = 0;
+  const uint32_t rowA = stage + g * 128 + 8 * t, rowB = rowA + 8 * 128;
+  const uint32_t xb = xu + g * 32 + 8 * t;  // this lane's limb (g < 4) at sub-block 0
 #pragma unroll
-  for (int v = 0; v < 2; ++v) {
-    const uint32_t kA = hmul2_u32(scA[v], kMul), aA = hmul2_u32(scA[v], kAdd);
-    const uint32_t kB = hmul2_u32(scB[v], kMul), aB = hmul2_u32(scB[v], kAdd);
-    const uint32_t mlA = prmt(kA, kA, 0x1010u), mhA = prmt(kA, kA, 0x3232u);
-    const uint32_t alA = prmt(aA, aA, 0x1010u), ahA = prmt(aA, aA, 0x3232u);
-    const uint32_t mlB = prmt(kB, kB, 0x1010u), mhB = prmt(kB, kB, 0x3232u);
-    const uint32_t alB = prmt(aB, aB, 0x1010u), ahB = prmt(aB, aB, 0x3232u);
-    const uint4 qa = v ? r.qA1 : r.qA0;
-    const uint4 qb = v ? r.qB1 : r.qB0;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const uint32_t wa = (&qa.x)[w], wb = (&qb.x)[w];
-      uint4 bf = make_uint4(0u, 0u, 0u, 0u);
-      if (g < 2) bf = xsu[(4 * v + w) * 8 + g * 4 + t];
-      // bytes 0 and 2: low nibbles -> elements e0, e0+2; high -> e0+32, e0+34
-      const uint32_t p0a = hfma2_u32(and_or(wa, 0x000F000Fu, kMagic), mlA, alA);
-      const uint32_t p0b = hfma2_u32(and_or(wb, 0x000F000Fu, kMagic), mlB, alB);
-      const uint32_t p1a = hfma2_u32(and_or(wa, 0x00F000F0u, kMagic), mhA, ahA);
-      const uint32_t p1b = hfma2_u32(and_or(wb, 0x00F000F0u, kMagic), mhB, ahB);
-      mma_16816(acc[v], p0a, p0b, p1a, p1b, bf.x, bf.y);
-      // bytes 1 and 3: elements e0+1, e0+3, e0+33, e0+35
-      const uint32_t wa8 = wa >> 8, wb8 = wb >> 8;
-      const uint32_t p2a = hfma2_u32(and_or(wa8, 0x000F000Fu, kMagic), mlA, alA);
-      const uint32_t p2b = hfma2_u32(and_or(wb8, 0x000F000Fu, kMagic), mlB, alB);
-      const uint32_t p3a = hfma2_u32(and_or(wa8, 0x00F000F0u, kMagic), mhA, ahA);
-      const uint32_t p3b = hfma2_u32(and_or(wb8, 0x00F000F0u, kMagic), mhB, ahB);
-      mma_16816(acc[v], p2a, p2b, p3a, p3b, bf.z, bf.w);
+  for (int c = 0; c < 4; ++c) {
+    const uint32_t off = 32u * ((uint32_t)c ^ (uint32_t)(g & 3));
+    const uint64_t qa = lds64(rowA + off), qb = lds64(rowB + off);
+    const uint32_t a0 = (uint32_t)qa, a1 = (uint32_t)(qa >> 32);
+    const uint32_t b0 = (uint32_t)qb, b1 = (uint32_t)(qb >> 32);
+    uint64_t xl = 0, xh = 0;
+    if (g < 4) {
+      xl = lds64(xb + (2 * c) * 128);
+      xh = lds64(xb + (2 * c + 1) * 128);
     }
+    int dl[4] = {0, 0, 0, 0}, dh[4] = {0, 0, 0, 0};
+    imma_16832(dl, a0 & 0x0F0F0F0Fu, b0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, b1 & 0x0F0F0F0Fu, (uint32_t)xl,
+               (uint32_t)(xl >> 32));
+    imma_16832(dh, a0 & 0xF0F0F0F0u, b0 & 0xF0F0F0F0u, a1 & 0xF0F0F0F0u, b1 & 0xF0F0F0F0u, (uint32_t)xh,
+               (uint32_t)(xh >> 32));
+    const uint32_t scA = c < 2 ? sA03 : sA47, scB = c < 2 ? sB03 : sB47;
+    const int kl = (2 * c) & 3, kh = (2 * c + 1) & 3;
+    const int slA = (int)((scA >> (8 * kl)) & 0xFFu), shA = (int)((scA >> (8 * kh)) & 0xFFu);
+    const int slB = (int)((scB >> (8 * kl)) & 0xFFu), shB = (int)((scB >> (8 * kh)) & 0xFFu);
+    loA0 += dl[0] * slA;
+    loA1 += dl[1] * slA;
+    loB0 += dl[2] * slB;
+    loB1 += dl[3] * slB;
+    hiA0 += dh[0] * shA;
+    hiA1 += dh[1] * shA;
+    hiB0 += dh[2] * shB;
+    hiB1 += dh[3] * shB;
   }
-  uint2 bm = make_uint2(0u, 0u);
-  if (g == 2 || g == 3) bm = reinterpret_cast<const uint2*>(xsu + 64)[(g - 2) * 4 + t];
-  mma_16816(acc[0], mnA[0], mnB[0], mnA[1], mnB[1], bm.x, bm.y);
-  // Lane t=0 holds columns 0,1 (sum q*sc*x as hi+lo), lane t=1 columns 2,3
-  // (sum m*X); f = d for t=0 and -16*dmin for t=1 (the sums were staged at
-  // 2^-4 the activation scale).  Lanes t>=2 hold zero columns.
-  const float fA = __half2float(__ushort_as_half((unsigned short)(r.hA.x >> fshift))) * fmul;
-  const float fB = __half2float(__ushort_as_half((unsigned short)(r.hB.x >> fshift))) * fmul;  // fmul carries the unit's 2^-e
-  yA = fmaf(fA, (acc[0][0] + acc[0][1]) + (acc[1][0] + acc[1][1]), yA);
-  yB = fmaf(fB, (acc[0][2] + acc[0][3]) + (acc[1][2] + acc[1][3]), yB);
+  // Mins: A = m_t, m_{t+4} (duplicated for the hi/lo halves of X), B col 4.
+  const uint32_t zA = hA.z >> sh8, wA = hA.w >> sh8, zB = hB.z >> sh8, wB = hB.w >> sh8;
+  const uint32_t mA0 = zA & 63u, mA4 = ((wA >> 4) & 0xFu) | ((zA >> 2) & 0x30u);
+  const uint32_t mB0 = zB & 63u, mB4 = ((wB >> 4) & 0xFu) | ((zB >> 2) & 0x30u);
+  const uint32_t fA0 = hsub2_u32((mA0 * 0x10001u) | kMagic, kMagic);
+  const uint32_t fA4 = hsub2_u32((mA4 * 0x10001u) | kMagic, kMagic);
+  const uint32_t fB0 = hsub2_u32((mB0 * 0x10001u) | kMagic, kMagic);
+  const uint32_t fB4 = hsub2_u32((mB4 * 0x10001u) | kMagic, kMagic);
+  uint64_t bm = 0;
+  if (g == 4) bm = lds64(xu + 1024 + 8 * t);
+  float cm[4] = {0.f, 0.f, 0.f, 0.f};
+  mma_16816(cm, fA0, fB0, fA4, fB4, (uint32_t)bm, (uint32_t)(bm >> 32));
+  // The high nibbles entered the MMA as 16*q.
+  const int iA0 = loA0 * 16 + hiA0, iA1 = loA1 * 16 + hiA1;
+  const int iB0 = loB0 * 16 + hiB0, iB1 = loB1 * 16 + hiB1;
+  // Scale factors multiply in an order that keeps every intermediate a
+  // normal float (2^-e alone can be as small as 2^-126).
+  const uint64_t inv = lds64(xu + 1088);
+  const float inv_main = __uint_as_float((uint32_t)inv);
+  const float inv_min = __uint_as_float((uint32_t)(inv >> 32));
+  const float2 dA = __half22float2(*reinterpret_cast<const __half2*>(&hA.x));
+  const float2 dB = __half22float2(*reinterpret_cast<const __half2*>(&hB.x));
+  yA = fmaf(fmaf((float)iA0, W0, (float)iA1 * W1) * dA.x, inv_main, yA);
+  yB = fmaf(fmaf((float)iB0, W0, (float)iB1 * W1) * dB.x, inv_main, yB);
+  yA = fmaf((cm[0] + cm[1]) * -dA.y, inv_min, yA);
+  yB = fmaf((cm[2] + cm[3]) * -dB.y, inv_min, yB);
 }
 
 template <int S>
@@ -236,14 +251,15 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
   int u0, u1;
   range_of(warp, u0, u1);
   const uint32_t ring = smem_u32(smem) + warp * S * kStageBytes;
-  uint4* xs = reinterpret_cast<uint4*>(smem + p.x_off);
-  float* s_inv = reinterpret_cast<float*>(xs + p.nku * kUnitVec);
+  uint8_t* xs = smem + p.x_off;
+  const uint32_t xs_s = smem_u32(xs);
   float* slots = reinterpret_cast<float*>(smem + p.slot_off);  // [kWarps][2][16]
   const uint64_t pol = l2_evict_first_policy();
 
   // Producer state: (tile, ku) of the next unit to request.
   int ltile = u0 / p.nku, lku = u0 - ltile * p.nku;
   int next = u0;
+  const uint32_t swz = 32u * ((uint32_t)t ^ (uint32_t)(g & 3));  // where this lane's chunk t lands
   auto request = [&](int stage) {  // always commits one group (possibly empty)
     if (next < u1) {
       const int rA = min(ltile * 16 + g, p.rows - 1);
@@ -251,10 +267,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
       const uint8_t* a = p.w + (long long)rA * p.rowb + lku * 144;
       const uint8_t* b = p.w + (long long)rB * p.rowb + lku * 144;
       const uint32_t base = ring + stage * kStageBytes;
-      cp_async16_hint(base + lane * 16, a + 16 + 16 * t, pol);
-      cp_async16_hint(base + 512 + lane * 16, a + 80 + 16 * t, pol);
-      cp_async16_hint(base + 1024 + lane * 16, b + 16 + 16 * t, pol);
-      cp_async16_hint(base + 1536 + lane * 16, b + 80 + 16 * t, pol);
+      cp_async16_hint(base + g * 128 + swz, a + 16 + 32 * t, pol);
+      cp_async16_hint(base + g * 128 + swz + 16, a + 32 + 32 * t, pol);
+      cp_async16_hint(base + (g + 8) * 128 + swz, b + 16 + 32 * t, pol);
+      cp_async16_hint(base + (g + 8) * 128 + swz + 16, b + 32 + 32 * t, pol);
       if (t < 2) cp_async16_hint(base + 2048 + (g + 8 * t) * 16, t ? b : a, pol);
       if (++lku == p.nku) {
         lku = 0;
@@ -268,11 +284,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
 #pragma unroll
   for (int s = 0; s < S; ++s) request(s);
   griddep_wait();
-  stage_x(xs, s_inv, p.x, p.nku);
+  stage_x(xs, p.x, p.nku);
 
-  const uint32_t sh = (uint32_t)(t >> 1) * 16u;
-  const uint32_t fshift = t == 0 ? 0u : 16u;
-  const float fmul = t == 0 ? 1.f : -16.f;
+  const uint32_t sh8 = 8u * (uint32_t)t;
+  // Limb weights 256^(3-n) of this lane's two columns, divided by the 16
+  // the high nibbles (and so the combined sums) carry.
+  const float W0 = t == 0 ? 1048576.f : (t == 1 ? 16.f : 0.f);
+  const float W1 = t == 0 ? 4096.f : (t == 1 ? 0.0625f : 0.f);
   const int first_tile = u0 / p.nku;
   int ctile = first_tile, cku = u0 - first_tile * p.nku;
   float yA = 0.f, yB = 0.f;
@@ -280,15 +298,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
   for (int u = u0; u < u1; ++u) {
     cp_async_wait<S - 1>();
     __syncwarp();
-    const uint32_t base = ring + stage * kStageBytes;
-    Raw r;
-    r.qA0 = lds128(base + lane * 16);
-    r.qA1 = lds128(base + 512 + lane * 16);
-    r.qB0 = lds128(base + 1024 + lane * 16);
-    r.qB1 = lds128(base + 1536 + lane * 16);
-    r.hA = lds128(base + 2048 + g * 16);
-    r.hB = lds128(base + 2048 + (g + 8) * 16);
-    compute_unit(r, xs + cku * kUnitVec, g, t, sh, fshift, fmul * s_inv[cku], yA, yB);
+    compute_unit(ring + stage * kStageBytes, xs_s + cku * kUnitX, g, t, sh8, W0, W1, yA, yB);
     __syncwarp();
     request(stage);
     stage = stage + 1 == S ? 0 : stage + 1;
@@ -299,8 +309,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
       ++ctile;
     }
     if (tile_end || u == u1 - 1) {
-      const float vA = yA + __shfl_xor_sync(0xffffffffu, yA, 1);
-      const float vB = yB + __shfl_xor_sync(0xffffffffu, yB, 1);
+      float vA = yA + __shfl_xor_sync(0xffffffffu, yA, 1);
+      float vB = yB + __shfl_xor_sync(0xffffffffu, yB, 1);
+      vA += __shfl_xor_sync(0xffffffffu, vA, 2);
+      vB += __shfl_xor_sync(0xffffffffu, vB, 2);
       yA = 0.f;
       yB = 0.f;
       if (t == 0) {
@@ -345,7 +357,7 @@ Layout layout(int64_t rows, int64_t cols, const GemvLaunch& L) {
   const int nku = (int)(cols / 256);
   o.ntiles = (int)((rows + 15) / 16);
   o.ctas = o.ntiles < L.sm_count ? o.ntiles : L.sm_count;
-  const int xbytes = ((nku * (kUnitVec * 16 + 4)) + 15) & ~15;
+  const int xbytes = nku * kUnitX;
   const int fixed = xbytes + kWarps * 2 * 16 * 4;
   // As many stages as fit next to a co-resident CTA, at least 2.
   o.stages = 4;
@@ -395,6 +407,9 @@ int prepare() {
   cudaError_t e = cudaFuncSetAttribute(gemv_q4k_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_q4k_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_q4k_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  if (e == cudaSuccess) e = set_max_shared_carveout(gemv_q4k_kernel<4>);
+  if (e == cudaSuccess) e = set_max_shared_carveout(gemv_q4k_kernel<3>);
+  if (e == cudaSuccess) e = set_max_shared_carveout(gemv_q4k_kernel<2>);
   return e == cudaSuccess ? 0 : -5;
 }
 }  // namespace q4k
@@ -591,7 +606,12 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_q6k_kernel(
 }
 }  // namespace q6k
 
-int gemv_prepare_device() { return q4k::prepare(); }
+int gemv_prepare_device() {
+  if (q4k::prepare() != 0) return -5;
+  if (set_max_shared_carveout(q80::gemv_q80_kernel) != cudaSuccess) return -5;
+  if (set_max_shared_carveout(q6k::gemv_q6k_kernel) != cudaSuccess) return -5;
+  return 0;
+}
 
 int gemv_check(int qtype, int64_t rows, int64_t cols) {
   if (rows < 1 || cols < 1 || rows > (1LL << 30)) return -4;
