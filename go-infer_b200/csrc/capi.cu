@@ -378,6 +378,23 @@ int gi_cuda_gemm_dev(int quant_type, float* y, const float* x, const void* w, si
   return 0;
 }
 
+int gi_cuda_gemv_multi_dev(int quant_type, int nmat, float* const* y, const float* x, const void* const* w,
+                           const size_t* w_bytes, const uint32_t* rows, uint32_t cols, void* stream) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!y || !x || !w || !w_bytes || !rows || nmat < 1 || nmat > 3) return fail(-4, "bad multi-GEMV arguments");
+  int64_t r64[3];
+  for (int m = 0; m < nmat; ++m) {
+    if (!y[m] || !w[m]) return fail(-4, "null device pointer");
+    r64[m] = rows[m];
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+  const int rc = gi::gemv_multi_launch(quant_type, nmat, y, x, w, w_bytes, r64, cols, g.scratch, launch_cfg(g.pdl), s);
+  if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : rc == -4 ? "unsupported shape" : "launch failed",
+                      rc == -5 ? cudaGetLastError() : cudaSuccess);
+  return 0;
+}
+
 int gi_cuda_set_pdl(int enable) {
   std::lock_guard<std::mutex> lk(g.mu);
   g.pdl = enable != 0;

@@ -41,9 +41,9 @@ int64_t row_bytes(int qtype, int64_t cols) {
 namespace q4k {
 // Work decomposition: a unit is 16 rows x 256 columns (one super-block per
 // row, 2304 bytes).  Each CTA owns a contiguous run of whole 16-row tiles,
-// so no reduction crosses CTAs; its units (tile-major) are split into
-// contiguous ranges, one per warp, and tiles shared by two warps are summed
-// in fixed warp order through shared memory (deterministic).  Each warp
+// so no reduction crosses CTAs; its units (tile-major) are dealt to the
+// warps round-robin and every tile's per-warp partials are summed in fixed
+// warp order through shared memory (deterministic).  Each warp
 // streams its units through a private ring of shared-memory stages with
 // cp.async (16 bytes per lane, L1-bypassing, S units in flight, the first
 // ones requested before the kernel waits on its predecessor).
@@ -68,14 +68,21 @@ constexpr int kSmemMax = 227 * 1024;
 constexpr int kCoresidentSmem = 110 * 1024;  // fits two CTAs (this kernel and the next) per SM
 constexpr uint32_t kMagic = 0x64006400u;     // f16x2 (1024, 1024)
 
+constexpr int kMaxMats = 3;  // matrices sharing one activation vector per launch
+
 struct Params {
-  const uint8_t* w;
+  const uint8_t* w[kMaxMats];
+  float* y[kMaxMats];
+  int rows[kMaxMats];
+  int tstart[kMaxMats + 1];  // first global 16-row tile of each matrix (prefix sums)
   const float* x;
-  float* y;
   long long rowb;
-  int rows, nku, ntiles, ctas;
+  int nku, ntiles, ctas;
   int x_off, slot_off;  // dynamic smem byte offsets (rings at 0)
 };
+
+// Matrix of global tile T (tiles of matrix m are [tstart[m], tstart[m+1])).
+GI_DEVINL int mat_of(const Params& p, int T) { return (T >= p.tstart[1]) + (T >= p.tstart[2]); }
 
 // Byte k of each of four words, gathered into one word (byte i from w_i).
 GI_DEVINL uint32_t gather_byte(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t k) {
@@ -243,40 +250,43 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
   const int g = lane >> 2, t = lane & 3;
   const int c = blockIdx.x;
   const int T0 = (int)((long long)p.ntiles * c / p.ctas), T1 = (int)((long long)p.ntiles * (c + 1) / p.ctas);
-  const int c0 = T0 * p.nku, n = (T1 - T0) * p.nku;  // the CTA's units [c0, c0 + n)
-  auto range_of = [&](int w, int& a, int& b) {
-    a = c0 + (int)((long long)n * w / kWarps);
-    b = c0 + (int)((long long)n * (w + 1) / kWarps);
-  };
-  int u0, u1;
-  range_of(warp, u0, u1);
+  const int ntl = T1 - T0, n = ntl * p.nku;  // the CTA's units, tile-major
   const uint32_t ring = smem_u32(smem) + warp * S * kStageBytes;
   uint8_t* xs = smem + p.x_off;
   const uint32_t xs_s = smem_u32(xs);
-  float* slots = reinterpret_cast<float*>(smem + p.slot_off);  // [kWarps][2][16]
+  float* slots = reinterpret_cast<float*>(smem + p.slot_off);  // [ntl][kWarps][16]
   const uint64_t pol = l2_evict_first_policy();
+  for (int i = threadIdx.x; i < ntl * kWarps * 16; i += kThreads) slots[i] = 0.f;
 
-  // Producer state: (tile, ku) of the next unit to request.
-  int ltile = u0 / p.nku, lku = u0 - ltile * p.nku;
-  int next = u0;
+  // Warp w takes the CTA's units w, w + kWarps, ...: at any moment the warps
+  // stream neighbouring super-blocks of the same 16 rows (one long run of
+  // bytes per row), which keeps DRAM pages open.
+  int ltile = warp / p.nku, lku = warp - (warp / p.nku) * p.nku;  // next unit to request
+  int next = warp;
   const uint32_t swz = 32u * ((uint32_t)t ^ (uint32_t)(g & 3));  // where this lane's chunk t lands
+  auto advance = [&](int& tile, int& ku) {
+    ku += kWarps;
+    while (ku >= p.nku) {
+      ku -= p.nku;
+      ++tile;
+    }
+  };
   auto request = [&](int stage) {  // always commits one group (possibly empty)
-    if (next < u1) {
-      const int rA = min(ltile * 16 + g, p.rows - 1);
-      const int rB = min(ltile * 16 + g + 8, p.rows - 1);
-      const uint8_t* a = p.w + (long long)rA * p.rowb + lku * 144;
-      const uint8_t* b = p.w + (long long)rB * p.rowb + lku * 144;
+    if (next < n) {
+      const int T = T0 + ltile, m = mat_of(p, T);
+      const int r0 = (T - p.tstart[m]) * 16, rl = p.rows[m] - 1;
+      const int rA = min(r0 + g, rl);
+      const int rB = min(r0 + g + 8, rl);
+      const uint8_t* a = p.w[m] + (long long)rA * p.rowb + lku * 144;
+      const uint8_t* b = p.w[m] + (long long)rB * p.rowb + lku * 144;
       const uint32_t base = ring + stage * kStageBytes;
       cp_async16_hint(base + g * 128 + swz, a + 16 + 32 * t, pol);
       cp_async16_hint(base + g * 128 + swz + 16, a + 32 + 32 * t, pol);
       cp_async16_hint(base + (g + 8) * 128 + swz, b + 16 + 32 * t, pol);
       cp_async16_hint(base + (g + 8) * 128 + swz + 16, b + 32 + 32 * t, pol);
       if (t < 2) cp_async16_hint(base + 2048 + (g + 8 * t) * 16, t ? b : a, pol);
-      if (++lku == p.nku) {
-        lku = 0;
-        ++ltile;
-      }
-      ++next;
+      advance(ltile, lku);
+      next += kWarps;
     }
     cp_async_commit();
   };
@@ -284,18 +294,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
 #pragma unroll
   for (int s = 0; s < S; ++s) request(s);
   griddep_wait();
-  stage_x(xs, p.x, p.nku);
+  stage_x(xs, p.x, p.nku);  // ends with a CTA barrier (also orders the slot zeroing)
 
   const uint32_t sh8 = 8u * (uint32_t)t;
   // Limb weights 256^(3-n) of this lane's two columns, divided by the 16
   // the high nibbles (and so the combined sums) carry.
   const float W0 = t == 0 ? 1048576.f : (t == 1 ? 16.f : 0.f);
   const float W1 = t == 0 ? 4096.f : (t == 1 ? 0.0625f : 0.f);
-  const int first_tile = u0 / p.nku;
-  int ctile = first_tile, cku = u0 - first_tile * p.nku;
+  int ctile = warp / p.nku, cku = warp - (warp / p.nku) * p.nku;
   float yA = 0.f, yB = 0.f;
   int stage = 0;
-  for (int u = u0; u < u1; ++u) {
+  for (int i = warp; i < n; i += kWarps) {
     cp_async_wait<S - 1>();
     __syncwarp();
     compute_unit(ring + stage * kStageBytes, xs_s + cku * kUnitX, g, t, sh8, W0, W1, yA, yB);
@@ -303,12 +312,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
     request(stage);
     stage = stage + 1 == S ? 0 : stage + 1;
     const int tile = ctile;
-    const bool tile_end = cku == p.nku - 1;
-    if (++cku == p.nku) {
-      cku = 0;
-      ++ctile;
-    }
-    if (tile_end || u == u1 - 1) {
+    advance(ctile, cku);
+    if (ctile != tile || i + kWarps >= n) {  // this warp is done with `tile`
       float vA = yA + __shfl_xor_sync(0xffffffffu, yA, 1);
       float vB = yB + __shfl_xor_sync(0xffffffffu, yB, 1);
       vA += __shfl_xor_sync(0xffffffffu, vA, 2);
@@ -316,35 +321,24 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
       yA = 0.f;
       yB = 0.f;
       if (t == 0) {
-        const int tu0 = tile * p.nku;
-        if (tu0 >= u0 && tu0 + p.nku <= u1) {  // this warp owns the whole tile
-          const int rA = tile * 16 + g;
-          if (rA < p.rows) p.y[rA] = vA;
-          if (rA + 8 < p.rows) p.y[rA + 8] = vB;
-        } else {
-          float* sl = slots + (warp * 2 + (tile == first_tile ? 0 : 1)) * 16;
-          sl[g] = vA;
-          sl[g + 8] = vB;
-        }
+        float* sl = slots + (tile * kWarps + warp) * 16;
+        sl[g] = vA;
+        sl[g + 8] = vB;
       }
     }
   }
   cp_async_wait<0>();
   __syncthreads();
-  // Tiles split between warps of this CTA: sum their partials in warp order.
-  for (int T = T0 + warp; T < T1; T += kWarps) {
-    const int tu0 = T * p.nku, tu1 = tu0 + p.nku;
-    float sum = 0.f;
-    bool owned = false;
-    for (int w = 0; w < kWarps; ++w) {
-      int a, b;
-      range_of(w, a, b);
-      if (a >= b || a >= tu1 || b <= tu0) continue;
-      if (a <= tu0 && b >= tu1) owned = true;
-      if (lane < 16) sum += slots[(w * 2 + (T == a / p.nku ? 0 : 1)) * 16 + lane];
+  // Each tile's partials, summed in fixed warp order (deterministic).
+  for (int tl = warp; tl < ntl; tl += kWarps) {
+    if (lane < 16) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) sum += slots[(tl * kWarps + w) * 16 + lane];
+      const int T = T0 + tl, m = mat_of(p, T);
+      const int row = (T - p.tstart[m]) * 16 + lane;
+      if (row < p.rows[m]) p.y[m][row] = sum;
     }
-    const int row = T * 16 + lane;
-    if (!owned && lane < 16 && row < p.rows) p.y[row] = sum;
   }
 }
 
@@ -352,33 +346,41 @@ struct Layout {
   int ctas, ntiles, stages, x_off, slot_off, smem;
 };
 
-Layout layout(int64_t rows, int64_t cols, const GemvLaunch& L) {
+Layout layout(int64_t ntiles, int64_t cols, const GemvLaunch& L) {
   Layout o;
   const int nku = (int)(cols / 256);
-  o.ntiles = (int)((rows + 15) / 16);
+  o.ntiles = (int)ntiles;
   o.ctas = o.ntiles < L.sm_count ? o.ntiles : L.sm_count;
+  const int max_tiles = (o.ntiles + o.ctas - 1) / o.ctas;
   const int xbytes = nku * kUnitX;
-  const int fixed = xbytes + kWarps * 2 * 16 * 4;
+  const int slot_bytes = max_tiles * kWarps * 16 * 4;
+  const int fixed = xbytes + slot_bytes;
   // As many stages as fit next to a co-resident CTA, at least 2.
   o.stages = 4;
   while (o.stages > 2 && fixed + kWarps * o.stages * kStageBytes > kCoresidentSmem) --o.stages;
   o.x_off = kWarps * o.stages * kStageBytes;
   o.slot_off = o.x_off + xbytes;
-  o.smem = o.slot_off + kWarps * 2 * 16 * 4;
+  o.smem = o.slot_off + slot_bytes;
   return o;
 }
 
-int launch(float* y, const float* x, const void* w, int64_t rows, int64_t cols, const GemvScratch& s,
+int launch(int nmat, float* const* y, const float* x, const void* const* w, const int64_t* rows, int64_t cols,
            const GemvLaunch& L, cudaStream_t stream) {
-  (void)s;
-  const Layout o = layout(rows, cols, L);
-  if (o.smem > kSmemMax) return -4;
+  if (nmat < 1 || nmat > kMaxMats) return -4;
   Params p;
-  p.w = static_cast<const uint8_t*>(w);
+  p.tstart[0] = 0;
+  for (int m = 0; m < kMaxMats; ++m) {
+    const bool on = m < nmat;
+    p.w[m] = on ? static_cast<const uint8_t*>(w[m]) : nullptr;
+    p.y[m] = on ? y[m] : nullptr;
+    p.rows[m] = on ? (int)rows[m] : 0;
+    p.tstart[m + 1] = p.tstart[m] + (on ? (int)((rows[m] + 15) / 16) : 0);
+  }
+  // unused slots repeat the total so mat_of never selects them
+  const Layout o = layout(p.tstart[kMaxMats], cols, L);
+  if (o.smem > kSmemMax) return -4;
   p.x = x;
-  p.y = y;
   p.rowb = row_bytes(kTypeQ4_K, cols);
-  p.rows = (int)rows;
   p.nku = (int)(cols / 256);
   p.ntiles = o.ntiles;
   p.ctas = o.ctas;
@@ -395,7 +397,7 @@ int launch(float* y, const float* x, const void* w, int64_t rows, int64_t cols, 
   cfg.attrs = attr;
   cfg.numAttrs = L.pdl ? 1 : 0;
   cudaError_t e;
-  switch (o.stages) {
+  switch (o.stages) {  // tile counts past nmat equal the total: mat_of stays < nmat
     case 4: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<4>, p); break;
     case 3: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<3>, p); break;
     default: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<2>, p); break;
@@ -666,7 +668,7 @@ int gemv_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
   switch (qtype) {
     case kTypeQ4_K:
       if ((reinterpret_cast<uintptr_t>(w) & 15) != 0) return -4;
-      return q4k::launch(y, x, w, rows, cols, s, L, stream);
+      return q4k::launch(1, &y, x, &w, &rows, cols, L, stream);
     case kTypeQ8_0:
       return launch_rowwarp(q80::gemv_q80_kernel, rows, L, stream, y, x, wb, wb + w_bytes,
                             (long long)rb, (int)rows, (int)(cols / 32));
@@ -676,6 +678,28 @@ int gemv_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
     default:
       return -2;
   }
+}
+
+int gemv_multi_launch(int qtype, int nmat, float* const* y, const float* x, const void* const* w,
+                      const size_t* w_bytes, const int64_t* rows, int64_t cols, const GemvScratch& s,
+                      const GemvLaunch& L, cudaStream_t stream) {
+  if (nmat < 1 || nmat > q4k::kMaxMats) return -4;
+  for (int m = 0; m < nmat; ++m) {
+    const int rc = gemv_check(qtype, rows[m], cols);
+    if (rc) return rc;
+    if (w_bytes[m] < (size_t)(row_bytes(qtype, cols) * rows[m])) return -4;
+  }
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return -4;
+  if (qtype == kTypeQ4_K) {
+    for (int m = 0; m < nmat; ++m)
+      if ((reinterpret_cast<uintptr_t>(w[m]) & 15) != 0) return -4;
+    return q4k::launch(nmat, y, x, w, rows, cols, L, stream);
+  }
+  for (int m = 0; m < nmat; ++m) {  // the CUDA-core kernels take one matrix per launch
+    const int rc = gemv_launch(qtype, y[m], x, w[m], w_bytes[m], rows[m], cols, s, L, stream);
+    if (rc) return rc;
+  }
+  return 0;
 }
 
 }  // namespace gi

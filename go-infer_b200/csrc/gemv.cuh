@@ -49,4 +49,11 @@ int gemv_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
                 int64_t rows, int64_t cols, const GemvScratch& s, const GemvLaunch& L,
                 cudaStream_t stream);
 
+// Several matrices of the same type and width against one activation
+// vector in one launch (gate and up, or Q, K and V): y[m] = W[m] x for
+// m < nmat <= 3.  Q4_K stages x once for all of them.
+int gemv_multi_launch(int qtype, int nmat, float* const* y, const float* x, const void* const* w,
+                      const size_t* w_bytes, const int64_t* rows, int64_t cols, const GemvScratch& s,
+                      const GemvLaunch& L, cudaStream_t stream);
+
 }  // namespace gi

@@ -110,6 +110,15 @@ int gi_cuda_gemv_dev(int quant_type, float* y, const float* x, const void* w, si
 int gi_cuda_gemm_dev(int quant_type, float* y, const float* x, const void* w, size_t w_bytes,
                      uint32_t batch_size, uint32_t rows, uint32_t cols, void* stream);
 
+/* Up to 3 matrices of one type and width against one activation vector in
+ * one launch: y[m] = W[m] x for m < nmat (Q, K and V of a layer, or gate
+ * and up).  The decode counterpart of the fused gate/up entry point
+ * metal_gemm_fused_gate_up_buf (metal_bridge.h:51); Q4_K stages x once for
+ * all matrices.  Device pointers; arrays of nmat entries. */
+int gi_cuda_gemv_multi_dev(int quant_type, int nmat, float* const* y, const float* x,
+                           const void* const* w, const size_t* w_bytes, const uint32_t* rows,
+                           uint32_t cols, void* stream);
+
 /* Device address / size of a buffer created by gi_cuda_create_buffer. */
 const void* gi_cuda_buffer_device_ptr(gi_cuda_buffer_t buf);
 size_t gi_cuda_buffer_bytes(gi_cuda_buffer_t buf);

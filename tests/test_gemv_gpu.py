@@ -181,6 +181,26 @@ def test_deterministic_and_device_path_identical():
     G.set_pdl(False)
 
 
+@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
+def test_multi_matrix_gemv_matches_single(qt):
+    import torch
+    cols = 4096
+    shapes = [4096, 1024, 1040]  # Q, K, V of a GQA layer; the last one ragged
+    raws = [G.quantize(qt, seeded_weights(80 + i, r, cols)) for i, r in enumerate(shapes)]
+    x = seeded_x(83, cols)
+    ws = [torch.from_numpy(r).cuda() for r in raws]
+    xd = torch.from_numpy(x).cuda()
+    ys = [torch.full((r,), float("nan"), device="cuda") for r in shapes]
+    s = torch.cuda.current_stream().cuda_stream
+    G.gemv_multi_dev(qt, [y.data_ptr() for y in ys], xd.data_ptr(), [w.data_ptr() for w in ws],
+                     [r.size for r in raws], shapes, cols, s)
+    torch.cuda.synchronize()
+    for raw, y, r in zip(raws, ys, shapes):
+        assert_parity(y.cpu().numpy(), O.matmul(qt, x, raw, r, cols), what=f"multi {qt} {r}")
+        single = gpu_gemv(qt, raw, x, r, cols)
+        assert np.array_equal(single.view(np.uint32), y.cpu().numpy().view(np.uint32))
+
+
 def test_batch_mode_defers_outputs():
     rows, cols = 256, 1024
     raws = [G.quantize(qt, seeded_weights(40 + i, rows, cols)) for i, qt in
