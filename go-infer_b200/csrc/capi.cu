@@ -49,6 +49,7 @@ struct Ctx {
   int sm_count = 0;
   cudaStream_t stream = nullptr;
   gi::GemvScratch scratch;
+  gi::GemmWorkspace gemm_ws;  // staged activations of the tensor-core prefill path
   int* err_host = nullptr;  // mapped pinned word the kernels set when a bounded wait gives up
   uint8_t* arena = nullptr;  // device activations of host-pointer calls
   size_t arena_cap = 0, arena_used = 0;
@@ -180,12 +181,29 @@ gi::GemvLaunch launch_cfg(bool pdl) {
   return L;
 }
 
+// Grow the prefill workspace to `need` bytes.  Growing waits for the device
+// (work queued earlier may still read the old workspace), so a caller that
+// captures CUDA graphs makes one call of its largest shape before capturing.
+int ensure_gemm_ws(size_t need) {
+  if (need <= g.gemm_ws.bytes) return 0;
+  GI_CUDA_TRY(cudaDeviceSynchronize(), "synchronize before growing the prefill workspace");
+  if (g.gemm_ws.ptr) cudaFree(g.gemm_ws.ptr);
+  g.gemm_ws = gi::GemmWorkspace();
+  size_t cap = (size_t)16 << 20;
+  while (cap < need) cap *= 2;
+  GI_CUDA_TRY(cudaMalloc(&g.gemm_ws.ptr, cap), "cudaMalloc prefill workspace");
+  g.gemm_ws.bytes = cap;
+  return 0;
+}
+
 int run_dev(int qtype, float* y, const float* x, const void* w, size_t w_bytes, int64_t batch,
             int64_t rows, int64_t cols, cudaStream_t s, bool pdl) {
   if (batch == 1) {
     return gi::gemv_launch(qtype, y, x, w, w_bytes, rows, cols, g.scratch, launch_cfg(pdl), s);
   }
-  return gi::gemm_launch(qtype, y, x, w, w_bytes, batch, rows, cols, g.scratch, launch_cfg(pdl), s);
+  const int rc = ensure_gemm_ws(gi::gemm_workspace_need(qtype, batch, rows, cols));
+  if (rc) return rc;
+  return gi::gemm_launch(qtype, y, x, w, w_bytes, batch, rows, cols, g.scratch, g.gemm_ws, launch_cfg(pdl), s);
 }
 
 // y/x on the host, weights on the device.
@@ -195,8 +213,10 @@ int run_host_io(int qtype, float* y, const float* x, const void* wdev, size_t w_
   int rc = batch == 1 ? gi::gemv_check(qtype, rows, cols) : gi::gemm_check(qtype, batch, rows, cols);
   if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : "unsupported shape");
   void *xd, *yd;
-  if ((rc = arena_alloc(sizeof(float) * batch * cols, &xd))) return rc;
-  if ((rc = arena_alloc(sizeof(float) * batch * rows, &yd))) return rc;
+  // One reservation for x and y: the arena can only grow while it is empty.
+  const size_t xbytes = ((sizeof(float) * batch * cols) + 255) & ~(size_t)255;
+  if ((rc = arena_alloc(xbytes + sizeof(float) * batch * rows, &xd))) return rc;
+  yd = static_cast<uint8_t*>(xd) + xbytes;
   GI_CUDA_TRY(cudaMemcpyAsync(xd, x, sizeof(float) * batch * cols, cudaMemcpyHostToDevice, g.stream),
               "copy x to device");
   rc = run_dev(qtype, static_cast<float*>(yd), static_cast<const float*>(xd), wdev, w_bytes, batch,
