@@ -254,6 +254,36 @@ int run_host_weights(int qtype, float* y, const float* x, const void* w, int64_t
 
 }  // namespace
 
+// Fixed device scratch of gi_cuda_gemm_dev_noalloc: the prefill workspace
+// (staged fp16 activation tiles, sub-block sums, per-token scales) lives in
+// this module-scope array instead of memory allocated at call time.  Nothing
+// in it needs to start at zero: the staging kernel writes every byte the
+// GEMM reads, padding included.  One array per device context, shared by
+// every call on that device: calls that overlap in time (other streams,
+// other threads) race on it.
+constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Address of g_noalloc_scratch on the bound device, looked up once per
+// device with that device current (the first call does this set-up).
+int noalloc_scratch(void** out) {
+  if (g.device < 0 || g.device >= kMaxDevices) return fail(-1, "device ordinal out of range");
+  if (!g_noalloc_addr[g.device]) {
+    void* p = nullptr;
+    GI_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_addr[g.device] = p;
+  }
+  *out = g_noalloc_addr[g.device];
+  return 0;
+}
+
+}  // namespace
+
 extern "C" {
 
 int gi_cuda_init(void) {
@@ -393,6 +423,33 @@ int gi_cuda_gemm_dev(int quant_type, float* y, const float* x, const void* w, si
   if (batch_size == 0) return fail(-4, "batch_size must be >= 1");
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : g.stream;
   const int rc = run_dev(quant_type, y, x, w, w_bytes, batch_size, rows, cols, s, g.pdl);
+  if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : rc == -4 ? "unsupported shape" : "launch failed",
+                      rc == -5 ? cudaGetLastError() : cudaSuccess);
+  return 0;
+}
+
+int gi_cuda_gemm_dev_noalloc(int quant_type, float* y, const float* x, const void* w, size_t w_bytes,
+                             uint32_t batch_size, uint32_t rows, uint32_t cols, void* stream) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!y || !x || !w) return fail(-4, "null device pointer");
+  if (batch_size == 0) return fail(-4, "batch_size must be >= 1");
+  int rc = gi::gemm_check(quant_type, batch_size, rows, cols);
+  if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : "unsupported shape");
+  const size_t need = gi::gemm_workspace_need(quant_type, batch_size, rows, cols);
+  if (need > kNoAllocScratchBytes) {
+    char buf[200];
+    std::snprintf(buf, sizeof buf,
+                  "gi_cuda_gemm_dev_noalloc: %u tokens x %u columns need %zu bytes of scratch, more than the "
+                  "%zu-byte static buffer",
+                  batch_size, cols, need, kNoAllocScratchBytes);
+    return fail(-4, buf);
+  }
+  gi::GemmWorkspace ws;
+  if ((rc = noalloc_scratch(&ws.ptr))) return rc;
+  ws.bytes = kNoAllocScratchBytes;
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+  rc = gi::gemm_launch(quant_type, y, x, w, w_bytes, batch_size, rows, cols, g.scratch, ws, launch_cfg(g.pdl), s);
   if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : rc == -4 ? "unsupported shape" : "launch failed",
                       rc == -5 ? cudaGetLastError() : cudaSuccess);
   return 0;

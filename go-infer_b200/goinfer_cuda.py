@@ -47,7 +47,7 @@ EXPORTS = (
     "gi_cuda_end_batch", "gi_cuda_create_buffer", "gi_cuda_release_buffer", "gi_cuda_gemv_buf",
     "gi_cuda_gemm_buf", "gi_cuda_gemv_q8_0", "gi_cuda_gemv_q4_k", "gi_cuda_gemv_q6_k",
     "gi_cuda_gemm_q8_0", "gi_cuda_gemm_q4_k", "gi_cuda_gemm_q6_k", "gi_cuda_gemv_dev",
-    "gi_cuda_gemm_dev", "gi_cuda_gemv_multi_dev", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl",
+    "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl",
     "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize",
 )
 
@@ -90,6 +90,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "gi_cuda_gemm_q6_k": ([f32p, f32p, vp, u32, u32, u32], i32),
         "gi_cuda_gemv_dev": ([i32, vp, vp, vp, sz, u32, u32, vp], i32),
         "gi_cuda_gemm_dev": ([i32, vp, vp, vp, sz, u32, u32, u32, vp], i32),
+        "gi_cuda_gemm_dev_noalloc": ([i32, vp, vp, vp, sz, u32, u32, u32, vp], i32),
         "gi_cuda_gemv_multi_dev": ([i32, i32, vp, vp, vp, vp, vp, u32, vp], i32),
         "gi_cuda_buffer_device_ptr": ([vp], vp),
         "gi_cuda_buffer_bytes": ([vp], sz),
@@ -238,6 +239,13 @@ def gemm_dev(quant_type: int, y_ptr: int, x_ptr: int, w_ptr: int, w_bytes: int, 
              cols: int, stream: int = 0) -> None:
     _err("gi_cuda_gemm_dev", load_library().gi_cuda_gemm_dev(quant_type, y_ptr, x_ptr, w_ptr, w_bytes,
                                                               batch, rows, cols, stream or None))
+
+
+def gemm_dev_noalloc(quant_type: int, y_ptr: int, x_ptr: int, w_ptr: int, w_bytes: int, batch: int, rows: int,
+                     cols: int, stream: int = 0) -> None:
+    """gemm_dev with the library's fixed 16 MiB scratch: allocates nothing."""
+    _err("gi_cuda_gemm_dev_noalloc", load_library().gi_cuda_gemm_dev_noalloc(
+        quant_type, y_ptr, x_ptr, w_ptr, w_bytes, batch, rows, cols, stream or None))
 
 
 def gemv_multi_dev(quant_type: int, ys: list[int], x_ptr: int, ws: list[int], w_bytes: list[int],

@@ -110,6 +110,18 @@ int gi_cuda_gemv_dev(int quant_type, float* y, const float* x, const void* w, si
 int gi_cuda_gemm_dev(int quant_type, float* y, const float* x, const void* w, size_t w_bytes,
                      uint32_t batch_size, uint32_t rows, uint32_t cols, void* stream);
 
+/* gi_cuda_gemm_dev without any allocation (no counterpart in the reference).
+ * The prefill workspace is a fixed 16 MiB device array inside the library
+ * instead of memory grown at call time, so a call never allocates or
+ * synchronises the device.  Limit: the staged activations of the call must
+ * fit: 4 bytes (Q6_K) or 4.125 bytes (Q4_K) per column per token, tokens
+ * rounded up to a multiple of 128; 512 tokens x 4096 columns fit.  Larger
+ * calls return GI_ERR_SHAPE (batches under 16 and Q8_0 need no scratch).  The first call on a device looks up the array's
+ * address (make it before any stream capture); the array is shared by all
+ * calls on the device, so calls that overlap in time race on it. */
+int gi_cuda_gemm_dev_noalloc(int quant_type, float* y, const float* x, const void* w, size_t w_bytes,
+                             uint32_t batch_size, uint32_t rows, uint32_t cols, void* stream);
+
 /* Up to 3 matrices of one type and width against one activation vector in
  * one launch: y[m] = W[m] x for m < nmat (Q, K and V of a layer, or gate
  * and up).  The decode counterpart of the fused gate/up entry point
