@@ -20,10 +20,12 @@
 #include "../../include/goinfer_cuda.h"
 #include "gemm.cuh"
 #include "gemv.cuh"
+#include "model.cuh"
 
 namespace gi {
 int quantize_host(int qtype, const float* src, int64_t rows, int64_t cols, uint8_t* dst,
                   int threads);
+int quantize_seeded(int qtype, uint64_t seed, float stddev, int64_t rows, int64_t cols, uint8_t* dst, int threads);
 }
 
 namespace {
@@ -252,6 +254,83 @@ int run_host_weights(int qtype, float* y, const float* x, const void* w, int64_t
   return rc;
 }
 
+// ---- whole-model decode -----------------------------------------------------
+
+// Sizes recorded by gi_cuda_alloc_buffers and the model that
+// gi_cuda_forward_transformer runs on them.
+struct Mirror {
+  bool set = false;
+  uint32_t dim = 0, hidden = 0, kv_dim = 0, vocab = 0, layers = 0, max_seq = 0;
+  gi::DecodeModel* m = nullptr;
+  int n_heads = 0, n_kv_heads = 0, head_dim = 0;
+  float eps = 0.f, theta = 0.f, scale = 0.f;
+};
+Mirror g_mirror;
+
+struct ModelHandle {
+  gi::DecodeModel m;
+  uint32_t* pinned = nullptr;  // prompt tokens staged for the per-step copies
+  size_t pinned_cap = 0;
+  gi::StepState* pinned_state = nullptr;
+  ~ModelHandle() {
+    if (pinned) cudaFreeHost(pinned);
+    if (pinned_state) cudaFreeHost(pinned_state);
+  }
+};
+
+const Buffer* as_buffer(gi_cuda_buffer_t b) { return static_cast<const Buffer*>(b); }
+
+// A weight matrix of `rows` x `cols`: present, of a supported type, large enough.
+int mat_ref(gi_cuda_buffer_t b, int qtype, int64_t rows, int64_t cols, gi::MatRef* out, const char* what) {
+  const Buffer* B = as_buffer(b);
+  if (!B || !B->dptr) return fail(-3, what);
+  const int64_t rb = gi::row_bytes(qtype, cols);
+  if (rb < 0) return fail(-2, what);
+  if (B->bytes < (size_t)(rb * rows)) return fail(-4, what);
+  out->w = B->dptr;
+  out->bytes = B->bytes;
+  out->qtype = qtype;
+  return 0;
+}
+
+int vec_ref(gi_cuda_buffer_t b, int64_t n, const float** out, bool optional, const char* what) {
+  const Buffer* B = as_buffer(b);
+  if (!B || !B->dptr) {
+    if (optional) {
+      *out = nullptr;
+      return 0;
+    }
+    return fail(-3, what);
+  }
+  if (B->bytes < sizeof(float) * (size_t)n) return fail(-4, what);
+  *out = static_cast<const float*>(B->dptr);
+  return 0;
+}
+
+int layer_refs(const gi_cuda_layer_weights_t* lw, uint32_t n_layers, int64_t dim, int64_t q_dim, int64_t kv_dim,
+               int64_t hidden, std::vector<gi::LayerRef>* out) {
+  if (!lw) return fail(-4, "null layer table");
+  out->resize(n_layers);
+  for (uint32_t l = 0; l < n_layers; ++l) {
+    const gi_cuda_layer_weights_t& w = lw[l];
+    gi::LayerRef& r = (*out)[l];
+    int rc = 0;
+    if ((rc = mat_ref(w.wq, w.wq_type, q_dim, dim, &r.wq, "layer wq"))) return rc;
+    if ((rc = mat_ref(w.wk, w.wk_type, kv_dim, dim, &r.wk, "layer wk"))) return rc;
+    if ((rc = mat_ref(w.wv, w.wv_type, kv_dim, dim, &r.wv, "layer wv"))) return rc;
+    if ((rc = mat_ref(w.wo, w.wo_type, dim, q_dim, &r.wo, "layer wo"))) return rc;
+    if ((rc = mat_ref(w.ffn_gate, w.ffn_gate_type, hidden, dim, &r.gate, "layer ffn_gate"))) return rc;
+    if ((rc = mat_ref(w.ffn_up, w.ffn_up_type, hidden, dim, &r.up, "layer ffn_up"))) return rc;
+    if ((rc = mat_ref(w.ffn_down, w.ffn_down_type, dim, hidden, &r.down, "layer ffn_down"))) return rc;
+    if ((rc = vec_ref(w.attn_norm, dim, &r.attn_norm, false, "layer attn_norm"))) return rc;
+    if ((rc = vec_ref(w.ffn_norm, dim, &r.ffn_norm, false, "layer ffn_norm"))) return rc;
+    if ((rc = vec_ref(w.bq, q_dim, &r.bq, true, "layer bq"))) return rc;
+    if ((rc = vec_ref(w.bk, kv_dim, &r.bk, true, "layer bk"))) return rc;
+    if ((rc = vec_ref(w.bv, kv_dim, &r.bv, true, "layer bv"))) return rc;
+  }
+  return 0;
+}
+
 }  // namespace
 
 // Fixed device scratch of gi_cuda_gemm_dev_noalloc: the prefill workspace
@@ -455,6 +534,233 @@ int gi_cuda_gemm_dev_noalloc(int quant_type, float* y, const float* x, const voi
   return 0;
 }
 
+int gi_cuda_alloc_buffers(uint32_t dim, uint32_t hidden_dim, uint32_t kv_dim, uint32_t vocab_size,
+                          uint32_t num_layers, uint32_t max_seq) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!dim || !hidden_dim || !kv_dim || !vocab_size || !num_layers || !max_seq) return fail(-4, "zero size");
+  delete g_mirror.m;
+  g_mirror = Mirror();
+  g_mirror.set = true;
+  g_mirror.dim = dim;
+  g_mirror.hidden = hidden_dim;
+  g_mirror.kv_dim = kv_dim;
+  g_mirror.vocab = vocab_size;
+  g_mirror.layers = num_layers;
+  g_mirror.max_seq = max_seq;
+  return 0;
+}
+
+int gi_cuda_forward_transformer(const float* initial_x, float* out_logits, uint32_t* out_token,
+                                const gi_cuda_layer_weights_t* layers, gi_cuda_buffer_t output_norm_buf,
+                                gi_cuda_buffer_t output_weight_buf, int output_weight_type, uint32_t num_layers,
+                                uint32_t dim, uint32_t hidden_dim, uint32_t kv_dim, uint32_t vocab_size,
+                                uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim, uint32_t pos,
+                                uint32_t slot, uint32_t max_seq, uint32_t active_context, float norm_eps,
+                                float rope_theta, float attn_scale) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  Mirror& M = g_mirror;
+  if (!M.set) return fail(-1, "gi_cuda_alloc_buffers has not been called");
+  if (dim != M.dim || hidden_dim != M.hidden || kv_dim != M.kv_dim || vocab_size != M.vocab ||
+      num_layers != M.layers || max_seq != M.max_seq)
+    return fail(-4, "sizes differ from gi_cuda_alloc_buffers");
+  if (!initial_x) return fail(-4, "null initial_x");
+  if (!num_heads || !num_kv_heads || num_kv_heads * head_dim != kv_dim || num_heads % num_kv_heads)
+    return fail(-4, "inconsistent head layout");
+  if (slot >= max_seq || active_context < 1 || active_context > max_seq) return fail(-4, "bad slot or context");
+  constexpr uint32_t kMirrorMaxPos = 32768;
+  if (pos >= kMirrorMaxPos) return fail(-4, "position beyond the RoPE table (32768)");
+  std::vector<gi::LayerRef> refs;
+  const int64_t q_dim = (int64_t)num_heads * head_dim;
+  if (int rc = layer_refs(layers, num_layers, dim, q_dim, kv_dim, hidden_dim, &refs)) return rc;
+  gi::MatRef out_ref, embd_ref;
+  const float* onorm = nullptr;
+  if (int rc = mat_ref(output_weight_buf, output_weight_type, vocab_size, dim, &out_ref, "output weight")) return rc;
+  if (int rc = vec_ref(output_norm_buf, dim, &onorm, false, "output norm")) return rc;
+  if (!M.m || M.n_heads != (int)num_heads || M.n_kv_heads != (int)num_kv_heads || M.head_dim != (int)head_dim ||
+      M.eps != norm_eps || M.theta != rope_theta || M.scale != attn_scale) {
+    delete M.m;
+    M.m = new gi::DecodeModel();
+    gi::ModelCfg c;
+    c.n_layers = (int)num_layers;
+    c.dim = (int)dim;
+    c.hidden = (int)hidden_dim;
+    c.n_heads = (int)num_heads;
+    c.n_kv_heads = (int)num_kv_heads;
+    c.head_dim = (int)head_dim;
+    c.vocab = (int)vocab_size;
+    c.max_seq = (int)max_seq;
+    c.max_pos = (int)kMirrorMaxPos;
+    c.eps = norm_eps;
+    c.rope_theta = rope_theta;
+    c.attn_scale = attn_scale;
+    const int rc = M.m->init(c, refs.data(), embd_ref, onorm, out_ref, g.sm_count, g.scratch.error);
+    if (rc) {
+      delete M.m;
+      M.m = nullptr;
+      return fail(rc, "forward buffers");
+    }
+    M.n_heads = (int)num_heads;
+    M.n_kv_heads = (int)num_kv_heads;
+    M.head_dim = (int)head_dim;
+    M.eps = norm_eps;
+    M.theta = rope_theta;
+    M.scale = attn_scale;
+  } else {
+    M.m->bind(refs.data(), embd_ref, onorm, out_ref);
+  }
+  gi::DecodeModel& m = *M.m;
+  gi::StepState st = {};
+  st.pos = pos;
+  st.slot = slot;
+  st.active = active_context;
+  GI_CUDA_TRY(cudaMemcpyAsync(m.x(), initial_x, sizeof(float) * dim, cudaMemcpyHostToDevice, g.stream), "copy x");
+  GI_CUDA_TRY(cudaMemcpyAsync(m.state(), &st, sizeof st, cudaMemcpyHostToDevice, g.stream), "copy state");
+  int rc = m.enqueue_step(g.stream, false, g.pdl);
+  if (rc) return fail(rc, "forward step launch", rc == -5 ? cudaGetLastError() : cudaSuccess);
+  if (out_logits)
+    GI_CUDA_TRY(cudaMemcpyAsync(out_logits, m.logits(), sizeof(float) * vocab_size, cudaMemcpyDeviceToHost, g.stream),
+                "copy logits");
+  if (out_token)
+    GI_CUDA_TRY(cudaMemcpyAsync(out_token, m.tokens_out(), sizeof(uint32_t), cudaMemcpyDeviceToHost, g.stream),
+                "copy token");
+  GI_CUDA_TRY(cudaStreamSynchronize(g.stream), "forward step");
+  return check_device_error();
+}
+
+gi_cuda_model_t gi_cuda_model_create(const gi_cuda_model_desc_t* d) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (ensure_ready()) return nullptr;
+  if (!d || !d->num_layers || !d->dim || !d->num_heads || !d->num_kv_heads || !d->head_dim || !d->vocab_size ||
+      !d->hidden_dim || !d->max_seq || d->num_heads % d->num_kv_heads) {
+    fail(-4, "gi_cuda_model_create: bad description");
+    return nullptr;
+  }
+  const int64_t q_dim = (int64_t)d->num_heads * d->head_dim, kv_dim = (int64_t)d->num_kv_heads * d->head_dim;
+  std::vector<gi::LayerRef> refs;
+  if (layer_refs(d->layers, d->num_layers, d->dim, q_dim, kv_dim, d->hidden_dim, &refs)) return nullptr;
+  gi::MatRef out_ref, embd_ref;
+  const float* onorm = nullptr;
+  if (mat_ref(d->output_weight, d->output_weight_type, d->vocab_size, d->dim, &out_ref, "output weight") ||
+      mat_ref(d->token_embd, d->token_embd_type, d->vocab_size, d->dim, &embd_ref, "token embedding") ||
+      vec_ref(d->output_norm, d->dim, &onorm, false, "output norm"))
+    return nullptr;
+  gi::ModelCfg c;
+  c.n_layers = (int)d->num_layers;
+  c.dim = (int)d->dim;
+  c.hidden = (int)d->hidden_dim;
+  c.n_heads = (int)d->num_heads;
+  c.n_kv_heads = (int)d->num_kv_heads;
+  c.head_dim = (int)d->head_dim;
+  c.vocab = (int)d->vocab_size;
+  c.max_seq = (int)d->max_seq;
+  c.max_pos = d->max_pos ? (int)d->max_pos : 32768;
+  c.eps = d->norm_eps;
+  c.rope_theta = d->rope_theta;
+  c.attn_scale = gi::attn_scale_for((int)d->head_dim);
+  ModelHandle* h = new ModelHandle();
+  const int rc = h->m.init(c, refs.data(), embd_ref, onorm, out_ref, g.sm_count, g.scratch.error);
+  if (rc) {
+    delete h;
+    fail(rc, "gi_cuda_model_create: device buffers");
+    return nullptr;
+  }
+  if (cudaHostAlloc(reinterpret_cast<void**>(&h->pinned_state), sizeof(gi::StepState), cudaHostAllocDefault) !=
+      cudaSuccess) {
+    delete h;
+    fail(-5, "gi_cuda_model_create: pinned state");
+    return nullptr;
+  }
+  return h;
+}
+
+void gi_cuda_model_destroy(gi_cuda_model_t model) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (!model || ensure_ready()) return;
+  cudaStreamSynchronize(g.stream);
+  delete static_cast<ModelHandle*>(model);
+}
+
+int gi_cuda_model_reset(gi_cuda_model_t model) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!model) return fail(-4, "null model");
+  static_cast<ModelHandle*>(model)->m.reset_cache(g.stream);
+  GI_CUDA_TRY(cudaStreamSynchronize(g.stream), "reset");
+  return 0;
+}
+
+int gi_cuda_model_generate(gi_cuda_model_t model, const int32_t* tokens, uint32_t n_tokens, uint32_t start_pos,
+                           uint32_t n_gen, uint32_t* out_tokens, float* out_logits, float* decode_ms) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!model || !tokens || !out_tokens || n_tokens < 1 || n_gen < 1) return fail(-4, "bad generate arguments");
+  ModelHandle* h = static_cast<ModelHandle*>(model);
+  gi::DecodeModel& m = h->m;
+  const gi::ModelCfg& c = m.cfg();
+  const uint64_t steps = (uint64_t)n_tokens + n_gen - 1;
+  if ((uint64_t)start_pos + steps > (uint64_t)c.max_pos) return fail(-4, "positions beyond the RoPE table");
+  if (steps > (uint64_t)m.max_out()) return fail(-4, "too many steps for one call");
+  for (uint32_t i = 0; i < n_tokens; ++i)
+    if (tokens[i] < 0 || tokens[i] >= c.vocab) return fail(-4, "token id out of range");
+  if (!m.graph) {
+    cudaGraph_t graph = nullptr;
+    GI_CUDA_TRY(cudaStreamBeginCapture(g.stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    const int rc = m.enqueue_step(g.stream, true, true);
+    const cudaError_t ce = cudaStreamEndCapture(g.stream, &graph);
+    if (rc || ce != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      return fail(rc ? rc : -5, "capturing the decode step", ce);
+    }
+    const cudaError_t ie = cudaGraphInstantiate(&m.graph, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) {
+      m.graph = nullptr;
+      return fail(-5, "instantiating the decode step", ie);
+    }
+  }
+  if (h->pinned_cap < n_tokens) {
+    if (h->pinned) cudaFreeHost(h->pinned);
+    h->pinned = nullptr;
+    h->pinned_cap = 0;
+    GI_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&h->pinned), sizeof(uint32_t) * n_tokens, cudaHostAllocDefault),
+                "pinned prompt");
+    h->pinned_cap = n_tokens;
+  }
+  std::memcpy(h->pinned, tokens, sizeof(uint32_t) * n_tokens);
+  gi::StepState* st = h->pinned_state;
+  *st = gi::StepState();
+  st->token = (uint32_t)tokens[0];
+  st->pos = start_pos;
+  st->slot = start_pos % (uint32_t)c.max_seq;
+  st->active = start_pos + 1 < (uint32_t)c.max_seq ? start_pos + 1 : (uint32_t)c.max_seq;
+  GI_CUDA_TRY(cudaMemcpyAsync(m.state(), st, sizeof *st, cudaMemcpyHostToDevice, g.stream), "copy state");
+  for (uint32_t i = 0; i < n_tokens; ++i) {
+    if (i > 0)  // the argmax just wrote st.token: the prompt overrides it
+      GI_CUDA_TRY(cudaMemcpyAsync(&m.state()->token, h->pinned + i, sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                  g.stream),
+                  "copy prompt token");
+    GI_CUDA_TRY(cudaGraphLaunch(m.graph, g.stream), "decode step");
+  }
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  GI_CUDA_TRY(cudaEventCreate(&e0), "event");
+  GI_CUDA_TRY(cudaEventCreate(&e1), "event");
+  cudaEventRecord(e0, g.stream);
+  for (uint32_t i = 1; i < n_gen; ++i) GI_CUDA_TRY(cudaGraphLaunch(m.graph, g.stream), "decode step");
+  cudaEventRecord(e1, g.stream);
+  cudaError_t e = cudaMemcpyAsync(out_tokens, m.tokens_out() + (n_tokens - 1), sizeof(uint32_t) * n_gen,
+                                  cudaMemcpyDeviceToHost, g.stream);
+  if (e == cudaSuccess && out_logits)
+    e = cudaMemcpyAsync(out_logits, m.logits(), sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, g.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
+  if (e == cudaSuccess && decode_ms) cudaEventElapsedTime(decode_ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (e != cudaSuccess) return fail(-5, "generate", e);
+  return check_device_error();
+}
+
 int gi_cuda_gemv_multi_dev(int quant_type, int nmat, float* const* y, const float* x, const void* const* w,
                            const size_t* w_bytes, const uint32_t* rows, uint32_t cols, void* stream) {
   std::lock_guard<std::mutex> lk(g.mu);
@@ -481,6 +787,15 @@ int gi_cuda_set_pdl(int enable) {
 const char* gi_cuda_last_error(void) { return t_err.c_str(); }
 
 int64_t gi_quant_row_bytes(int quant_type, int64_t cols) { return gi::row_bytes(quant_type, cols); }
+
+int gi_quantize_seeded(int quant_type, uint64_t seed, float stddev, int64_t rows, int64_t cols, void* dst,
+                       int threads) {
+  if (!dst) return fail(-4, "null pointer");
+  if (threads <= 0) threads = (int)std::thread::hardware_concurrency();
+  const int rc = gi::quantize_seeded(quant_type, seed, stddev, rows, cols, static_cast<uint8_t*>(dst), threads);
+  if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : "unsupported shape");
+  return 0;
+}
 
 int gi_quantize(int quant_type, const float* src, int64_t rows, int64_t cols, void* dst, int threads) {
   if (!src || !dst) return fail(-4, "null pointer");

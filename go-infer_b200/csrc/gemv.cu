@@ -34,6 +34,7 @@ int64_t row_bytes(int qtype, int64_t cols) {
     case kTypeQ8_0: return (cols / 32) * 34;
     case kTypeQ4_K: return (cols / 256) * 144;
     case kTypeQ6_K: return (cols / 256) * 210;
+    case kTypeF32: return cols * 4;
     default: return -1;
   }
 }
@@ -64,7 +65,7 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kUnitX = 1104;       // staged activation bytes per unit (see stage_unit)
 constexpr int kStageBytes = 2304;  // qs: [16 rows][4 chunks, swizzled][32 B], headers: [16 rows][16 B]
 constexpr int kMaxCols = 45056;
-constexpr int kSmemMax = 227 * 1024;
+constexpr int kSmemMax = 227 * 1024 - 256;  // dynamic; the rest is static (the RMSNorm reduction)
 constexpr int kCoresidentSmem = 110 * 1024;  // fits two CTAs (this kernel and the next) per SM
 constexpr uint32_t kMagic = 0x64006400u;     // f16x2 (1024, 1024)
 
@@ -76,13 +77,27 @@ struct Params {
   int rows[kMaxMats];
   int tstart[kMaxMats + 1];  // first global 16-row tile of each matrix (prefix sums)
   const float* x;
+  const float* x2;  // RMSNorm weight (xmode kXNorm)
+  float eps;
+  int xmode, ymode;
   long long rowb;
   int nku, ntiles, ctas;
   int x_off, slot_off;  // dynamic smem byte offsets (rings at 0)
 };
 
-// Matrix of global tile T (tiles of matrix m are [tstart[m], tstart[m+1])).
-GI_DEVINL int mat_of(const Params& p, int T) { return (T >= p.tstart[1]) + (T >= p.tstart[2]); }
+// Matrix m and its local 16-row tile lt of global tile T: matrices one
+// after another (tiles of matrix m are [tstart[m], tstart[m+1])), or in
+// kYSwiGLU mode gate and up tiles interleaved (gate tile i = 2i, up = 2i+1)
+// so that one CTA holds both halves of every row it finishes.
+GI_DEVINL void tile_of(const Params& p, int T, int& m, int& lt) {
+  if (p.ymode == kYSwiGLU) {
+    m = T & 1;
+    lt = T >> 1;
+  } else {
+    m = (T >= p.tstart[1]) + (T >= p.tstart[2]);
+    lt = T - p.tstart[m];
+  }
+}
 
 // Byte k of each of four words, gathered into one word (byte i from w_i).
 GI_DEVINL uint32_t gather_byte(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t k) {
@@ -149,10 +164,42 @@ GI_DEVINL void stage_unit(uint8_t* xu, float4 a, float4 b, int lane) {
   }
 }
 
-__device__ void stage_x(uint8_t* xs, const float* __restrict__ x, int nku) {
+GI_DEVINL float4 mul3(float4 a, float s, float4 w) {  // (a * s) * w, one rounding each
+  return make_float4(__fmul_rn(__fmul_rn(a.x, s), w.x), __fmul_rn(__fmul_rn(a.y, s), w.y),
+                     __fmul_rn(__fmul_rn(a.z, s), w.z), __fmul_rn(__fmul_rn(a.w, s), w.w));
+}
+
+// Stage the activation vector: p.x, or in kXNorm mode RMSNorm(p.x) * p.x2
+// (pkg/math/kernels.go:9-19: float32 sum of squares, scale
+// float32(1 / sqrt(float64(mean + eps))), out = x * scale * w), computed by
+// every CTA from the same data in the same order.
+__device__ void stage_x(uint8_t* xs, const Params& p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int j = lane >> 2, q = lane & 3;
   const int off = 64 * (j >> 1) + 32 * (j & 1) + 8 * q;
+  const int nku = p.nku;
+  const float* __restrict__ x = p.x;
+  float scale = 1.f;
+  if (p.xmode == kXNorm) {
+    __shared__ float red[kWarps];
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    float s = 0.f;
+    for (int i = threadIdx.x; i < nku * 64; i += kThreads) {
+      const float4 v = __ldg(x4 + i);
+      s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+      s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+      s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+      s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+    }
+    s = warp_sum(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) tot = __fadd_rn(tot, red[w]);
+    const float mean = __fdiv_rn(tot, (float)(nku * 256));
+    scale = (float)(1.0 / sqrt((double)__fadd_rn(mean, p.eps)));
+  }
   for (int u0 = warp; u0 < nku; u0 += 4 * kWarps) {
     float4 a[4], b[4];
 #pragma unroll
@@ -161,6 +208,10 @@ __device__ void stage_x(uint8_t* xs, const float* __restrict__ x, int nku) {
       if (u < nku) {
         a[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off));
         b[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off + 4));
+        if (p.xmode == kXNorm) {
+          a[k] = mul3(a[k], scale, __ldg(reinterpret_cast<const float4*>(p.x2 + u * 256 + off)));
+          b[k] = mul3(b[k], scale, __ldg(reinterpret_cast<const float4*>(p.x2 + u * 256 + off + 4)));
+        }
       }
     }
 #pragma unroll
@@ -249,7 +300,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int c = blockIdx.x;
-  const int T0 = (int)((long long)p.ntiles * c / p.ctas), T1 = (int)((long long)p.ntiles * (c + 1) / p.ctas);
+  // CTA c owns tiles [T0, T1); in kYSwiGLU mode whole (gate, up) pairs.
+  const int gran = p.ymode == kYSwiGLU ? 2 : 1, nun = p.ntiles / gran;
+  const int T0 = gran * (int)((long long)nun * c / p.ctas), T1 = gran * (int)((long long)nun * (c + 1) / p.ctas);
   const int ntl = T1 - T0, n = ntl * p.nku;  // the CTA's units, tile-major
   const uint32_t ring = smem_u32(smem) + warp * S * kStageBytes;
   uint8_t* xs = smem + p.x_off;
@@ -273,8 +326,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
   };
   auto request = [&](int stage) {  // always commits one group (possibly empty)
     if (next < n) {
-      const int T = T0 + ltile, m = mat_of(p, T);
-      const int r0 = (T - p.tstart[m]) * 16, rl = p.rows[m] - 1;
+      int m, lt;
+      tile_of(p, T0 + ltile, m, lt);
+      const int r0 = lt * 16, rl = p.rows[m] - 1;
       const int rA = min(r0 + g, rl);
       const int rB = min(r0 + g + 8, rl);
       const uint8_t* a = p.w[m] + (long long)rA * p.rowb + lku * 144;
@@ -294,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
 #pragma unroll
   for (int s = 0; s < S; ++s) request(s);
   griddep_wait();
-  stage_x(xs, p.x, p.nku);  // ends with a CTA barrier (also orders the slot zeroing)
+  stage_x(xs, p);  // ends with a CTA barrier (also orders the slot zeroing)
 
   const uint32_t sh8 = 8u * (uint32_t)t;
   // Limb weights 256^(3-n) of this lane's two columns, divided by the 16
@@ -335,9 +389,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
       float sum = 0.f;
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) sum += slots[(tl * kWarps + w) * 16 + lane];
-      const int T = T0 + tl, m = mat_of(p, T);
-      const int row = (T - p.tstart[m]) * 16 + lane;
-      if (row < p.rows[m]) p.y[m][row] = sum;
+      int m, lt;
+      tile_of(p, T0 + tl, m, lt);
+      const int row = lt * 16 + lane;
+      if (p.ymode == kYSwiGLU) {
+        // gate tile (even) pairs with the next (up) tile: SwiGLU
+        // (kernels.go:39-46), silu = g / (1 + float32(exp(float64(-g)))).
+        if ((tl & 1) == 0 && row < p.rows[0]) {
+          float up = 0.f;
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w) up += slots[((tl + 1) * kWarps + w) * 16 + lane];
+          const float silu = __fdiv_rn(sum, __fadd_rn(1.0f, (float)exp(-(double)sum)));
+          p.y[0][row] = __fmul_rn(silu, up);
+        }
+      } else if (row < p.rows[m]) {
+        p.y[m][row] = p.ymode == kYAdd ? __fadd_rn(p.y[m][row], sum) : sum;  // residual: y += W x
+      }
     }
   }
 }
@@ -346,12 +413,13 @@ struct Layout {
   int ctas, ntiles, stages, x_off, slot_off, smem;
 };
 
-Layout layout(int64_t ntiles, int64_t cols, const GemvLaunch& L) {
+Layout layout(int64_t ntiles, int64_t cols, const GemvLaunch& L, int gran = 1) {
   Layout o;
   const int nku = (int)(cols / 256);
   o.ntiles = (int)ntiles;
-  o.ctas = o.ntiles < L.sm_count ? o.ntiles : L.sm_count;
-  const int max_tiles = (o.ntiles + o.ctas - 1) / o.ctas;
+  const int nun = o.ntiles / gran;
+  o.ctas = nun < L.sm_count ? nun : L.sm_count;
+  const int max_tiles = gran * ((nun + o.ctas - 1) / o.ctas);
   const int xbytes = nku * kUnitX;
   const int slot_bytes = max_tiles * kWarps * 16 * 4;
   const int fixed = xbytes + slot_bytes;
@@ -365,8 +433,9 @@ Layout layout(int64_t ntiles, int64_t cols, const GemvLaunch& L) {
 }
 
 int launch(int nmat, float* const* y, const float* x, const void* const* w, const int64_t* rows, int64_t cols,
-           const GemvLaunch& L, cudaStream_t stream) {
+           const GemvLaunch& L, cudaStream_t stream, const GemvFuse& f = GemvFuse()) {
   if (nmat < 1 || nmat > kMaxMats) return -4;
+  if (f.ymode == kYSwiGLU && (nmat != 2 || rows[0] != rows[1])) return -4;
   Params p;
   p.tstart[0] = 0;
   for (int m = 0; m < kMaxMats; ++m) {
@@ -376,10 +445,15 @@ int launch(int nmat, float* const* y, const float* x, const void* const* w, cons
     p.rows[m] = on ? (int)rows[m] : 0;
     p.tstart[m + 1] = p.tstart[m] + (on ? (int)((rows[m] + 15) / 16) : 0);
   }
-  // unused slots repeat the total so mat_of never selects them
-  const Layout o = layout(p.tstart[kMaxMats], cols, L);
+  // unused slots repeat the total so tile_of never selects them
+  const int gran = f.ymode == kYSwiGLU ? 2 : 1;
+  const Layout o = layout(p.tstart[kMaxMats], cols, L, gran);
   if (o.smem > kSmemMax) return -4;
   p.x = x;
+  p.x2 = f.x2;
+  p.eps = f.eps;
+  p.xmode = f.xmode;
+  p.ymode = f.ymode;
   p.rowb = row_bytes(kTypeQ4_K, cols);
   p.nku = (int)(cols / 256);
   p.ntiles = o.ntiles;
@@ -624,10 +698,36 @@ int gemv_check(int qtype, int64_t rows, int64_t cols) {
       return cols % 256 == 0 ? 0 : -4;
     case kTypeQ8_0:
       return cols % 32 == 0 ? 0 : -4;
+    case kTypeF32:
+      return cols % 4 == 0 ? 0 : -4;
     default:
       return -2;
   }
 }
+
+namespace f32 {
+// float32 rows (GEMVEngine.MatMulF32, pkg/math/gemv.go:27-60): one warp per
+// row, 16-byte loads, warp-shuffle sum.
+__global__ void __launch_bounds__(256) gemv_f32_kernel(float* __restrict__ y, const float* __restrict__ x,
+                                                       const float* __restrict__ w, int rows, int cols) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int row = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* wr = reinterpret_cast<const float4*>(w + (size_t)row * cols);
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  float s = 0.f;
+  for (int i = lane; i < cols / 4; i += 32) {
+    const float4 a = __ldg(wr + i), b = __ldg(x4 + i);
+    s = fmaf(a.x, b.x, s);
+    s = fmaf(a.y, b.y, s);
+    s = fmaf(a.z, b.z, s);
+    s = fmaf(a.w, b.w, s);
+  }
+  s = warp_sum(s);
+  if (lane == 0) y[row] = s;
+}
+}  // namespace f32
 
 void gemv_scratch_need(int qtype, int64_t rows, int64_t cols, const GemvLaunch& L, int* warps,
                        int* tiles) {
@@ -675,9 +775,39 @@ int gemv_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
     case kTypeQ6_K:
       return launch_rowwarp(q6k::gemv_q6k_kernel, rows, L, stream, y, x, wb, wb + w_bytes,
                             (long long)rb, (int)rows, (int)(cols / 256));
+    case kTypeF32: {
+      if ((reinterpret_cast<uintptr_t>(w) & 15) != 0) return -4;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)((rows + 7) / 8));
+      cfg.blockDim = dim3(256);
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = L.pdl ? 1 : 0;
+      return cudaLaunchKernelEx(&cfg, f32::gemv_f32_kernel, y, x, reinterpret_cast<const float*>(w), (int)rows,
+                                (int)cols) == cudaSuccess
+                 ? 0
+                 : -5;
+    }
     default:
       return -2;
   }
+}
+
+int gemv_q4k_fused(int nmat, float* const* y, const float* x, const void* const* w, const size_t* w_bytes,
+                   const int64_t* rows, int64_t cols, const GemvFuse& f, const GemvLaunch& L, cudaStream_t stream) {
+  if (nmat < 1 || nmat > q4k::kMaxMats) return -4;
+  for (int m = 0; m < nmat; ++m) {
+    const int rc = gemv_check(kTypeQ4_K, rows[m], cols);
+    if (rc) return rc;
+    if (w_bytes[m] < (size_t)(row_bytes(kTypeQ4_K, cols) * rows[m])) return -4;
+    if ((reinterpret_cast<uintptr_t>(w[m]) & 15) != 0) return -4;
+  }
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return -4;
+  if (f.xmode == kXNorm && (!f.x2 || (reinterpret_cast<uintptr_t>(f.x2) & 15) != 0)) return -4;
+  return q4k::launch(nmat, y, x, w, rows, cols, L, stream, f);
 }
 
 int gemv_multi_launch(int qtype, int nmat, float* const* y, const float* x, const void* const* w,

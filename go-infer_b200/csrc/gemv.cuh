@@ -22,6 +22,16 @@ struct GemvScratch {
   int max_tiles = 0;
 };
 
+// Fusions of the Q4_K GEMV used by the decode step (internal).
+enum : int { kXPlain = 0, kXNorm = 1 };              // staged x, or RMSNorm(x) * x2 (weight)
+enum : int { kYStore = 0, kYAdd = 1, kYSwiGLU = 2 };  // y = Wx, y += Wx, or silu(W0 x) * (W1 x)
+struct GemvFuse {
+  int xmode = kXPlain;
+  const float* x2 = nullptr;
+  float eps = 0.f;
+  int ymode = kYStore;
+};
+
 struct GemvLaunch {
   int sm_count = 148;
   bool pdl = false;  // programmatic dependent launch (weights must not be
@@ -34,8 +44,9 @@ int gemv_prepare_device();
 // Bytes of one row of `cols` weights of `qtype` (gemv.go:99,135,171).
 int64_t row_bytes(int qtype, int64_t cols);
 
-// Shape rules: rows >= 1; cols a positive multiple of 256 (Q4_K, Q6_K) or
-// 32 (Q8_0); Q4_K cols <= 30464 (activation staging in shared memory).
+// Shape rules: rows >= 1; cols a positive multiple of 256 (Q4_K, Q6_K), 32
+// (Q8_0) or 4 (F32 rows); Q4_K cols <= 45056 (activation staging in shared
+// memory).
 // Returns 0, -2 unsupported type, -4 bad shape, -5 CUDA launch error.
 int gemv_check(int qtype, int64_t rows, int64_t cols);
 
@@ -55,5 +66,11 @@ int gemv_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
 int gemv_multi_launch(int qtype, int nmat, float* const* y, const float* x, const void* const* w,
                       const size_t* w_bytes, const int64_t* rows, int64_t cols, const GemvScratch& s,
                       const GemvLaunch& L, cudaStream_t stream);
+
+// Q4_K only: gemv_multi_launch with the prologue / epilogue fusions above.
+// kYSwiGLU takes nmat == 2 matrices of equal rows (gate, up) and writes the
+// SwiGLU product into y[0].
+int gemv_q4k_fused(int nmat, float* const* y, const float* x, const void* const* w, const size_t* w_bytes,
+                   const int64_t* rows, int64_t cols, const GemvFuse& f, const GemvLaunch& L, cudaStream_t stream);
 
 }  // namespace gi

@@ -1,0 +1,570 @@
+// model.cu -- device-resident Llama decode step: the CPU branch of
+// Engine.Forward (pkg/engine/forward.go:140-297) and the greedy pick of
+// ForwardSample (forward.go:394-405), on the device, one token per call of
+// enqueue_step (captured once into a CUDA graph and replayed per token).
+//
+// The element-wise kernels repeat the reference's float32 operation order
+// (one rounding per Go operation, __f*_rn so nothing is contracted into an
+// FMA) and its float64 detours (sqrt in RMSNorm, exp in SwiGLU/softmax, the
+// RoPE angles, precomputed on the host in double).  Reductions that the
+// reference does sequentially (the RMSNorm sum of squares, softmax sums, the
+// attention weighted sum) are parallel here: they differ from the
+// reference by float32 rounding only, as the GEMVs do.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "model.cuh"
+
+namespace gi {
+namespace {
+
+constexpr int kAttChunk = 32;  // KV positions per attention CTA
+
+// Launch with programmatic dependent launch when `pdl` (every kernel here
+// waits for its predecessor before touching its outputs).
+template <typename... KArgs, typename... Args>
+cudaError_t launch(bool pdl, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void (*k)(KArgs...),
+                   Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
+GI_DEVINL float f16_bits_to_f32(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
+
+// ---- embedding: one row of the token table (weights.go:132-234) ----------
+// Q4_K: float32(q)*d1 - m1 with d1 = sc*d, m1 = m*dmin (quant.go:228-248);
+// Q6_K: d * float32(sc) * float32(q) (quant.go:277-282); Q8_0:
+// float32(q) * d (quant.go:205-207); F32: a copy.
+__global__ void embed_kernel(const StepState* __restrict__ st, const uint8_t* __restrict__ tbl, int qtype,
+                             int dim, size_t rowb, float* __restrict__ x) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= dim) return;
+  const uint8_t* row = tbl + (size_t)st->token * rowb;
+  float out;
+  if (qtype == kTypeQ4_K) {
+    const uint8_t* b = row + (size_t)(e >> 8) * 144;
+    const int r = e & 255, c = r >> 6, l = r & 63;
+    const int j = 2 * c + (l >> 5);
+    const uint8_t* sc = b + 4;
+    const float d = f16_bits_to_f32(b[0] | (b[1] << 8)), dmin = f16_bits_to_f32(b[2] | (b[3] << 8));
+    uint32_t s6, m6;
+    if (j < 4) {
+      s6 = sc[j] & 63;
+      m6 = sc[j + 4] & 63;
+    } else {
+      s6 = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+      m6 = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    const uint8_t qb = b[16 + 32 * c + (l & 31)];
+    const uint32_t q = l < 32 ? (qb & 0xF) : (qb >> 4);
+    const float d1 = __fmul_rn((float)s6, d), m1 = __fmul_rn((float)m6, dmin);
+    out = __fsub_rn(__fmul_rn((float)q, d1), m1);
+  } else if (qtype == kTypeQ6_K) {
+    const uint8_t* b = row + (size_t)(e >> 8) * 210;
+    const int r = e & 255, n = r >> 7, g = (r >> 5) & 3, l = r & 31;
+    const uint8_t qlb = b[n * 64 + (g & 1) * 32 + l];
+    const uint32_t lo = (g >> 1) ? (qlb >> 4) : (qlb & 0xF);
+    const uint32_t hi = (b[128 + n * 32 + l] >> (2 * g)) & 3;
+    const int q = (int)(lo | (hi << 4)) - 32;
+    const float sc = (float)(int8_t)b[192 + n * 8 + 2 * g + (l >> 4)];
+    const float d = f16_bits_to_f32(b[208] | (b[209] << 8));
+    out = __fmul_rn(__fmul_rn(d, sc), (float)q);
+  } else if (qtype == kTypeQ8_0) {
+    const uint8_t* b = row + (size_t)(e >> 5) * 34;
+    out = __fmul_rn((float)(int8_t)b[2 + (e & 31)], f16_bits_to_f32(b[0] | (b[1] << 8)));
+  } else {
+    out = reinterpret_cast<const float*>(row)[e];
+  }
+  x[e] = out;
+}
+
+// ---- RMSNorm (pkg/math/kernels.go:9-19) ------------------------------------
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                       float* __restrict__ out, int n, float eps) {
+  __shared__ float red[32];
+  griddep_wait();
+  griddep_launch_dependents();
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s = __fadd_rn(s, __fmul_rn(x[i], x[i]));
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float mean = __fdiv_rn(red[0], (float)n);
+  const float scale = (float)(1.0 / sqrt((double)__fadd_rn(mean, eps)));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], scale), w[i]);
+}
+
+// ---- biases (forward.go:207-223) --------------------------------------------
+__global__ void add_kernel(float* __restrict__ y, const float* __restrict__ b, int n) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __fadd_rn(y[i], b[i]);
+}
+
+// ---- RoPE (kernels.go:22-36) on q and k, then the KV-cache write ------------
+// (forward.go:226-238).  rope[pos][i] = (cos, sin) of pos / theta^(2i/hd),
+// computed in double on the host and rounded to float32 as the reference does.
+__global__ void rope_kv_kernel(const StepState* __restrict__ st, float* __restrict__ q, const float* __restrict__ k,
+                               const float* __restrict__ v, const float2* __restrict__ rope, float* __restrict__ kc,
+                               float* __restrict__ vc, int n_heads, int n_kv_heads, int hd, int kv_dim,
+                               uint32_t max_pos, int* error) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int half = hd >> 1;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t pos = st->pos, slot = st->slot;
+  if (pos >= max_pos) {  // past the RoPE table: report, touch nothing
+    if (i == 0) atomicExch(error, 1);
+    return;
+  }
+  const int nq = n_heads * half, nk = n_kv_heads * half;
+  float* krow = kc + (size_t)slot * kv_dim;
+  float* vrow = vc + (size_t)slot * kv_dim;
+  if (i < nq + nk) {
+    const bool isq = i < nq;
+    const int p = isq ? i : i - nq;
+    const int h = p / half, j = p % half;
+    const float2 cs = rope[(size_t)pos * half + j];
+    const float* src = isq ? q : k;
+    const float v0 = src[h * hd + j], v1 = src[h * hd + j + half];
+    const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+    const float r1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+    if (isq) {
+      q[h * hd + j] = r0;
+      q[h * hd + j + half] = r1;
+    } else {
+      krow[h * hd + j] = r0;
+      krow[h * hd + j + half] = r1;
+    }
+  } else if (i < nq + nk + kv_dim) {
+    const int e = i - nq - nk;
+    vrow[e] = v[e];
+  }
+}
+
+// ---- attention with GQA (forward.go:241-266), split over KV positions -------
+// CTA (kv head g, chunk c) handles the kv_mul query heads of g against
+// positions [32c, 32c + 32) of the active context: it stages the chunk's K
+// and V rows and the queries in shared memory (all loads in flight at once),
+// then writes, per query head, (max, sum of exp, unnormalised output) for
+// attn_combine_kernel.  Scores use the float64 exp of kernels.go:60.
+__global__ void __launch_bounds__(256) attn_partial_kernel(const StepState* __restrict__ st,
+                                                           const float* __restrict__ q, const float* __restrict__ kc,
+                                                           const float* __restrict__ vc, float* __restrict__ part,
+                                                           int kv_mul, int hd, int kv_dim, int splits, float scale) {
+  extern __shared__ __align__(16) float sm[];
+  griddep_wait();
+  griddep_launch_dependents();
+  const int g = blockIdx.x, c = blockIdx.y;
+  const int active = (int)st->active;
+  const int t0 = c * kAttChunk;
+  const int nt = max(0, min(kAttChunk, active - t0));
+  const int hd4 = hd >> 2;
+  float* qs = sm;                          // [kv_mul][hd]
+  float* ks = qs + kv_mul * hd;            // [kAttChunk][hd]
+  float* vs = ks + kAttChunk * hd;         // [kAttChunk][hd]
+  float* sc = vs + kAttChunk * hd;         // [kv_mul][kAttChunk]
+  float* mx = sc + kv_mul * kAttChunk;     // [kv_mul][2]
+  float4* qs4 = reinterpret_cast<float4*>(qs);
+  float4* ks4 = reinterpret_cast<float4*>(ks);
+  float4* vs4 = reinterpret_cast<float4*>(vs);
+  const float4* q4 = reinterpret_cast<const float4*>(q + (size_t)g * kv_mul * hd);
+  for (int i = threadIdx.x; i < kv_mul * hd4; i += blockDim.x) qs4[i] = __ldg(q4 + i);
+  for (int i = threadIdx.x; i < nt * hd4; i += blockDim.x) {
+    const int t = i / hd4, d4 = i - t * hd4;
+    const size_t off = ((size_t)(t0 + t) * kv_dim + (size_t)g * hd) / 4 + d4;
+    ks4[i] = __ldg(reinterpret_cast<const float4*>(kc) + off);
+    vs4[i] = __ldg(reinterpret_cast<const float4*>(vc) + off);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int p = warp; p < kv_mul * nt; p += nw) {  // one warp per (head, position)
+    const int h = p / nt, t = p - h * nt;
+    float s = 0.f;
+    for (int d = lane; d < hd; d += 32) s = fmaf(qs[h * hd + d], ks[t * hd + d], s);
+    s = warp_sum(s);
+    if (lane == 0) sc[h * kAttChunk + t] = __fmul_rn(s, scale);
+  }
+  __syncthreads();
+  for (int h = warp; h < kv_mul; h += nw) {  // local softmax statistics per head
+    float m = -INFINITY;
+    for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[h * kAttChunk + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < nt; t += 32) {
+      const float e = (float)exp((double)__fsub_rn(sc[h * kAttChunk + t], m));
+      sc[h * kAttChunk + t] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      mx[2 * h] = m;
+      mx[2 * h + 1] = l;
+    }
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < kv_mul * hd; o += blockDim.x) {  // thread per (head, d)
+    const int h = o / hd, d = o - h * hd;
+    float a0 = 0.f, a1 = 0.f;
+    int t = 0;
+    for (; t + 1 < nt; t += 2) {
+      a0 = fmaf(sc[h * kAttChunk + t], vs[t * hd + d], a0);
+      a1 = fmaf(sc[h * kAttChunk + t + 1], vs[(t + 1) * hd + d], a1);
+    }
+    if (t < nt) a0 = fmaf(sc[h * kAttChunk + t], vs[t * hd + d], a0);
+    float* pp = part + ((size_t)(g * kv_mul + h) * splits + c) * (hd + 2);
+    pp[2 + d] = a0 + a1;
+    if (d == 0) {
+      pp[0] = nt > 0 ? mx[2 * h] : -INFINITY;
+      pp[1] = nt > 0 ? mx[2 * h + 1] : 0.f;
+    }
+  }
+}
+
+__global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ att, int hd, int splits) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int h = blockIdx.x, d = threadIdx.x;
+  const float* ph = part + (size_t)h * splits * (hd + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, ph[s * (hd + 2)]);
+  float L = 0.f, acc = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float m = ph[s * (hd + 2)];
+    if (m == -INFINITY) continue;
+    const float f = (float)exp((double)(m - M));
+    L = fmaf(ph[s * (hd + 2) + 1], f, L);
+    acc = fmaf(ph[s * (hd + 2) + 2 + d], f, acc);
+  }
+  if (d < hd) att[(size_t)h * hd + d] = L > 0.f ? acc / L : 0.f;
+}
+
+// ---- residual add (forward.go:271-273, 285-287) ------------------------------
+__global__ void residual_kernel(float* __restrict__ x, const float* __restrict__ p, int n) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) x[i] = __fadd_rn(x[i], p[i]);
+}
+
+// ---- SwiGLU (kernels.go:39-46) ---------------------------------------------
+__global__ void swiglu_kernel(float* __restrict__ gate, const float* __restrict__ up, int n) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float g = gate[i];
+  const float silu = __fdiv_rn(g, __fadd_rn(1.0f, (float)exp(-(double)g)));
+  gate[i] = __fmul_rn(silu, up[i]);
+}
+
+// ---- greedy pick (forward.go:397-404: the first maximum wins) and the
+// position advance of the generation loop ------------------------------------
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int n, StepState* st,
+                                                      uint32_t* __restrict__ out, int max_out, int max_seq) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  griddep_wait();
+  griddep_launch_dependents();
+  float v = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float l = logits[i];
+    if (idx == 0x7fffffff || l > v) {  // strictly greater: the first maximum stays
+      v = l;
+      idx = i;
+    }
+  }
+  // combine (value, index): larger value wins, equal values keep the lower index
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) {
+      v = ov;
+      idx = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    bv[threadIdx.x >> 5] = v;
+    bi[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    v = threadIdx.x < nw ? bv[threadIdx.x] : -INFINITY;
+    idx = threadIdx.x < nw ? bi[threadIdx.x] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ov > v || (ov == v && oi < idx)) {
+        v = ov;
+        idx = oi;
+      }
+    }
+    if (threadIdx.x == 0) {
+      if (idx == 0x7fffffff) idx = 0;
+      if ((int)st->n_out < max_out) out[st->n_out] = (uint32_t)idx;
+      st->n_out += 1;
+      st->token = (uint32_t)idx;
+      const uint32_t pos = st->pos + 1;
+      st->pos = pos;
+      st->slot = pos % (uint32_t)max_seq;
+      st->active = pos + 1 < (uint32_t)max_seq ? pos + 1 : (uint32_t)max_seq;
+    }
+  }
+}
+
+size_t attn_smem_bytes(int kv_mul, int hd) {
+  return sizeof(float) * ((size_t)kv_mul * hd + 2 * (size_t)kAttChunk * hd + (size_t)kv_mul * kAttChunk + 2 * kv_mul);
+}
+
+template <typename T>
+int dev_alloc(T** p, size_t n, size_t* total) {
+  if (cudaMalloc(reinterpret_cast<void**>(p), sizeof(T) * (n ? n : 1)) != cudaSuccess) return -5;
+  *total += sizeof(T) * (n ? n : 1);
+  return 0;
+}
+
+}  // namespace
+
+float attn_scale_for(int head_dim) {
+  const double x = (double)head_dim;
+  double z = 0.0;
+  if (x > 0) {
+    z = x / 2;
+    for (int i = 0; i < 10; i++) z = (z + x / z) / 2;
+  }
+  return (float)(1.0 / z);
+}
+
+DecodeModel::~DecodeModel() {
+  if (graph) cudaGraphExecDestroy(graph);
+  for (void* p : {(void*)x_, (void*)xb_, (void*)q_, (void*)k_, (void*)v_, (void*)att_, (void*)proj_, (void*)gate_,
+                  (void*)up_, (void*)logits_, (void*)kcache_, (void*)vcache_, (void*)part_, (void*)rope_, (void*)st_,
+                  (void*)tokens_out_})
+    if (p) cudaFree(p);
+  delete[] layers_;
+}
+
+int DecodeModel::init(const ModelCfg& cfg, const LayerRef* layers, const MatRef& tok_embd, const float* out_norm,
+                      const MatRef& out, int sm_count, int* error_word) {
+  cfg_ = cfg;
+  if (cfg.n_layers < 1 || cfg.dim < 1 || cfg.n_heads < 1 || cfg.n_kv_heads < 1 || cfg.head_dim < 2 ||
+      cfg.head_dim % 2 || cfg.head_dim > 1024 || cfg.n_heads % cfg.n_kv_heads || cfg.max_seq < 1 ||
+      cfg.max_pos < 1 || cfg.vocab < 1 || cfg.hidden < 1)
+    return -4;
+  const int kv_mul = cfg.n_heads / cfg.n_kv_heads;
+  if (cfg.head_dim % 4) return -4;  // float4 staging of K / V rows
+  const size_t att_smem = attn_smem_bytes(kv_mul, cfg.head_dim);
+  if (att_smem > 200 * 1024) return -4;
+  if (att_smem > 48 * 1024 &&
+      cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)att_smem) !=
+          cudaSuccess)
+    return -5;
+  n_layers_ = cfg.n_layers;
+  layers_ = new LayerRef[n_layers_];
+  for (int l = 0; l < n_layers_; ++l) layers_[l] = layers[l];
+  tok_embd_ = tok_embd;
+  out_ = out;
+  out_norm_ = out_norm;
+  sm_count_ = sm_count;
+  scratch_.error = error_word;
+  const int q_dim = cfg.n_heads * cfg.head_dim, kv_dim = cfg.n_kv_heads * cfg.head_dim;
+  att_splits_ = (cfg.max_seq + kAttChunk - 1) / kAttChunk;
+  max_out_ = 1 << 16;
+  size_t t = 0;
+  int rc = 0;
+  rc |= dev_alloc(&x_, cfg.dim, &t);
+  rc |= dev_alloc(&xb_, cfg.dim, &t);
+  rc |= dev_alloc(&q_, q_dim, &t);
+  rc |= dev_alloc(&k_, kv_dim, &t);
+  rc |= dev_alloc(&v_, kv_dim, &t);
+  rc |= dev_alloc(&att_, q_dim, &t);
+  rc |= dev_alloc(&proj_, cfg.dim, &t);
+  rc |= dev_alloc(&gate_, cfg.hidden, &t);
+  rc |= dev_alloc(&up_, cfg.hidden, &t);
+  rc |= dev_alloc(&logits_, cfg.vocab, &t);
+  rc |= dev_alloc(&kcache_, (size_t)cfg.n_layers * cfg.max_seq * kv_dim, &t);
+  rc |= dev_alloc(&vcache_, (size_t)cfg.n_layers * cfg.max_seq * kv_dim, &t);
+  rc |= dev_alloc(&part_, (size_t)cfg.n_heads * att_splits_ * (cfg.head_dim + 2), &t);
+  rc |= dev_alloc(&rope_, (size_t)cfg.max_pos * (cfg.head_dim / 2), &t);
+  rc |= dev_alloc(&st_, 1, &t);
+  rc |= dev_alloc(&tokens_out_, max_out_, &t);
+  if (rc) return -5;
+  dev_bytes_ = t;
+  // RoPE angles in double, rounded to float32 (kernels.go:25-29).
+  const int half = cfg.head_dim / 2;
+  std::vector<float2> tab((size_t)cfg.max_pos * half);
+  for (int i = 0; i < half; ++i) {
+    const double freq = 1.0 / std::pow((double)cfg.rope_theta, (double)(2 * i) / (double)cfg.head_dim);
+    for (int p = 0; p < cfg.max_pos; ++p) {
+      const double val = (double)p * freq;
+      tab[(size_t)p * half + i] = make_float2((float)std::cos(val), (float)std::sin(val));
+    }
+  }
+  if (cudaMemcpy(rope_, tab.data(), sizeof(float2) * tab.size(), cudaMemcpyHostToDevice) != cudaSuccess) return -5;
+  if (cudaMemset(kcache_, 0, sizeof(float) * (size_t)cfg.n_layers * cfg.max_seq * kv_dim) != cudaSuccess ||
+      cudaMemset(vcache_, 0, sizeof(float) * (size_t)cfg.n_layers * cfg.max_seq * kv_dim) != cudaSuccess ||
+      cudaMemset(st_, 0, sizeof(StepState)) != cudaSuccess)
+    return -5;
+  return 0;
+}
+
+void DecodeModel::bind(const LayerRef* layers, const MatRef& tok_embd, const float* out_norm, const MatRef& out) {
+  for (int l = 0; l < n_layers_; ++l) layers_[l] = layers[l];
+  tok_embd_ = tok_embd;
+  out_norm_ = out_norm;
+  out_ = out;
+}
+
+void DecodeModel::reset_cache(cudaStream_t s) {
+  const size_t kv = (size_t)cfg_.n_layers * cfg_.max_seq * cfg_.n_kv_heads * cfg_.head_dim;
+  cudaMemsetAsync(kcache_, 0, sizeof(float) * kv, s);
+  cudaMemsetAsync(vcache_, 0, sizeof(float) * kv, s);
+}
+
+int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
+  const ModelCfg& c = cfg_;
+  const int hd = c.head_dim, q_dim = c.n_heads * hd, kv_dim = c.n_kv_heads * hd;
+  const int kv_mul = c.n_heads / c.n_kv_heads;
+  GemvLaunch L;
+  L.sm_count = sm_count_;
+  L.pdl = pdl;
+  auto blocks = [](int n, int b) { return dim3((unsigned)((n + b - 1) / b)); };
+  cudaError_t e = cudaSuccess;
+  int rc = 0;
+  if (embed) {
+    const int64_t rb = tok_embd_.qtype == kTypeF32 ? (int64_t)c.dim * 4 : row_bytes(tok_embd_.qtype, c.dim);
+    if (rb <= 0) return -2;
+    e = launch(pdl, blocks(c.dim, 256), dim3(256), 0, s, embed_kernel, (const StepState*)st_,
+               (const uint8_t*)tok_embd_.w, tok_embd_.qtype, c.dim, (size_t)rb, x_);
+    if (e != cudaSuccess) return -5;
+  }
+  const size_t layer_kv = (size_t)c.max_seq * kv_dim;
+  const size_t att_smem = attn_smem_bytes(kv_mul, hd);
+  for (int l = 0; l < n_layers_; ++l) {
+    const LayerRef& Ly = layers_[l];
+    float* kc = kcache_ + l * layer_kv;
+    float* vc = vcache_ + l * layer_kv;
+    // RMSNorm + Q, K, V.  Q4_K: one launch, the norm folded into the GEMV's
+    // activation staging.
+    if (Ly.wq.qtype == kTypeQ4_K && Ly.wk.qtype == kTypeQ4_K && Ly.wv.qtype == kTypeQ4_K) {
+      float* ys[3] = {q_, k_, v_};
+      const void* ws[3] = {Ly.wq.w, Ly.wk.w, Ly.wv.w};
+      const size_t wb[3] = {Ly.wq.bytes, Ly.wk.bytes, Ly.wv.bytes};
+      const int64_t rows[3] = {q_dim, kv_dim, kv_dim};
+      GemvFuse f;
+      f.xmode = kXNorm;
+      f.x2 = Ly.attn_norm;
+      f.eps = c.eps;
+      rc = gemv_q4k_fused(3, ys, x_, ws, wb, rows, c.dim, f, L, s);
+    } else {
+      e = launch(pdl, dim3(1), dim3(1024), 0, s, rmsnorm_kernel, (const float*)x_, Ly.attn_norm, xb_, c.dim, c.eps);
+      if (e != cudaSuccess) return -5;
+      rc = gemv_launch(Ly.wq.qtype, q_, xb_, Ly.wq.w, Ly.wq.bytes, q_dim, c.dim, scratch_, L, s);
+      if (!rc) rc = gemv_launch(Ly.wk.qtype, k_, xb_, Ly.wk.w, Ly.wk.bytes, kv_dim, c.dim, scratch_, L, s);
+      if (!rc) rc = gemv_launch(Ly.wv.qtype, v_, xb_, Ly.wv.w, Ly.wv.bytes, kv_dim, c.dim, scratch_, L, s);
+    }
+    if (rc) return rc;
+    if (Ly.bq) e = launch(pdl, blocks(q_dim, 256), dim3(256), 0, s, add_kernel, q_, Ly.bq, q_dim);
+    if (Ly.bk && e == cudaSuccess) e = launch(pdl, blocks(kv_dim, 256), dim3(256), 0, s, add_kernel, k_, Ly.bk, kv_dim);
+    if (Ly.bv && e == cudaSuccess) e = launch(pdl, blocks(kv_dim, 256), dim3(256), 0, s, add_kernel, v_, Ly.bv, kv_dim);
+    if (e != cudaSuccess) return -5;
+    const int nrope = (c.n_heads + c.n_kv_heads) * (hd / 2) + kv_dim;
+    e = launch(pdl, blocks(nrope, 256), dim3(256), 0, s, rope_kv_kernel, (const StepState*)st_, q_,
+               (const float*)k_, (const float*)v_, (const float2*)rope_, kc, vc, c.n_heads, c.n_kv_heads, hd, kv_dim,
+               (uint32_t)c.max_pos, scratch_.error);
+    if (e != cudaSuccess) return -5;
+    e = launch(pdl, dim3(c.n_kv_heads, att_splits_), dim3(256), att_smem, s, attn_partial_kernel,
+               (const StepState*)st_, (const float*)q_, (const float*)kc, (const float*)vc, part_, kv_mul, hd, kv_dim,
+               att_splits_, c.attn_scale);
+    if (e != cudaSuccess) return -5;
+    e = launch(pdl, dim3(c.n_heads), dim3(hd), 0, s, attn_combine_kernel, (const float*)part_, att_, hd, att_splits_);
+    if (e != cudaSuccess) return -5;
+    // Output projection + residual (x += Wo att).
+    if (Ly.wo.qtype == kTypeQ4_K) {
+      float* ys[1] = {x_};
+      const void* ws[1] = {Ly.wo.w};
+      const size_t wb[1] = {Ly.wo.bytes};
+      const int64_t rows[1] = {c.dim};
+      GemvFuse f;
+      f.ymode = kYAdd;
+      rc = gemv_q4k_fused(1, ys, att_, ws, wb, rows, q_dim, f, L, s);
+    } else {
+      rc = gemv_launch(Ly.wo.qtype, proj_, att_, Ly.wo.w, Ly.wo.bytes, c.dim, q_dim, scratch_, L, s);
+      if (!rc && launch(pdl, blocks(c.dim, 256), dim3(256), 0, s, residual_kernel, x_, (const float*)proj_, c.dim) !=
+                     cudaSuccess)
+        rc = -5;
+    }
+    if (rc) return rc;
+    // RMSNorm + gate and up + SwiGLU: one launch for Q4_K.
+    if (Ly.gate.qtype == kTypeQ4_K && Ly.up.qtype == kTypeQ4_K) {
+      float* ys[2] = {gate_, up_};
+      const void* ws[2] = {Ly.gate.w, Ly.up.w};
+      const size_t wb[2] = {Ly.gate.bytes, Ly.up.bytes};
+      const int64_t rows[2] = {c.hidden, c.hidden};
+      GemvFuse f;
+      f.xmode = kXNorm;
+      f.x2 = Ly.ffn_norm;
+      f.eps = c.eps;
+      f.ymode = kYSwiGLU;
+      rc = gemv_q4k_fused(2, ys, x_, ws, wb, rows, c.dim, f, L, s);
+    } else {
+      e = launch(pdl, dim3(1), dim3(1024), 0, s, rmsnorm_kernel, (const float*)x_, Ly.ffn_norm, xb_, c.dim, c.eps);
+      if (e != cudaSuccess) return -5;
+      rc = gemv_launch(Ly.gate.qtype, gate_, xb_, Ly.gate.w, Ly.gate.bytes, c.hidden, c.dim, scratch_, L, s);
+      if (!rc) rc = gemv_launch(Ly.up.qtype, up_, xb_, Ly.up.w, Ly.up.bytes, c.hidden, c.dim, scratch_, L, s);
+      if (!rc && launch(pdl, blocks(c.hidden, 256), dim3(256), 0, s, swiglu_kernel, gate_, (const float*)up_,
+                        c.hidden) != cudaSuccess)
+        rc = -5;
+    }
+    if (rc) return rc;
+    // Down projection + residual (x += Wdown h).
+    if (Ly.down.qtype == kTypeQ4_K) {
+      float* ys[1] = {x_};
+      const void* ws[1] = {Ly.down.w};
+      const size_t wb[1] = {Ly.down.bytes};
+      const int64_t rows[1] = {c.dim};
+      GemvFuse f;
+      f.ymode = kYAdd;
+      rc = gemv_q4k_fused(1, ys, gate_, ws, wb, rows, c.hidden, f, L, s);
+    } else {
+      rc = gemv_launch(Ly.down.qtype, proj_, gate_, Ly.down.w, Ly.down.bytes, c.dim, c.hidden, scratch_, L, s);
+      if (!rc && launch(pdl, blocks(c.dim, 256), dim3(256), 0, s, residual_kernel, x_, (const float*)proj_, c.dim) !=
+                     cudaSuccess)
+        rc = -5;
+    }
+    if (rc) return rc;
+  }
+  e = launch(pdl, dim3(1), dim3(1024), 0, s, rmsnorm_kernel, (const float*)x_, out_norm_, xb_, c.dim, c.eps);
+  if (e != cudaSuccess) return -5;
+  rc = gemv_launch(out_.qtype, logits_, xb_, out_.w, out_.bytes, c.vocab, c.dim, scratch_, L, s);
+  if (rc) return rc;
+  e = launch(pdl, dim3(1), dim3(1024), 0, s, argmax_kernel, (const float*)logits_, c.vocab, st_, tokens_out_,
+             max_out_, c.max_seq);
+  return e == cudaSuccess ? 0 : -5;
+}
+
+}  // namespace gi

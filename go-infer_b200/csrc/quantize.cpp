@@ -240,4 +240,62 @@ int quantize_host(int qtype, const float* src, int64_t rows, int64_t cols, uint8
   return 0;
 }
 
+// Seeded N(0, std) weights, quantised row by row without holding the fp32
+// matrix: row r draws from a splitmix64 stream keyed by (seed, r) through the
+// Box-Muller transform (in double), so the bytes do not depend on the
+// thread count.  F32 writes the float32 values themselves.
+namespace {
+inline uint64_t splitmix64(uint64_t& s) {
+  uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+void normal_row(uint64_t seed, int64_t row, float stddev, float* out, int64_t n) {
+  uint64_t s = seed * 0xD1B54A32D192ED03ull ^ (uint64_t)row * 0x8CB92BA72F3D8DD7ull;
+  for (int64_t i = 0; i < n; i += 2) {
+    const double u1 = ((splitmix64(s) >> 11) + 1) * 0x1.0p-53;  // (0, 1]
+    const double u2 = (splitmix64(s) >> 11) * 0x1.0p-53;        // [0, 1)
+    const double r = std::sqrt(-2.0 * std::log(u1)), a = 6.283185307179586 * u2;
+    out[i] = (float)(r * std::cos(a) * stddev);
+    if (i + 1 < n) out[i + 1] = (float)(r * std::sin(a) * stddev);
+  }
+}
+}  // namespace
+
+int quantize_seeded(int qtype, uint64_t seed, float stddev, int64_t rows, int64_t cols, uint8_t* dst, int threads) {
+  const bool f32 = qtype == kTypeF32;
+  const int64_t block = qtype == kTypeQ8_0 ? 32 : (f32 ? 1 : 256);
+  if (!f32 && qtype != kTypeQ8_0 && qtype != kTypeQ4_K && qtype != kTypeQ6_K) return -2;
+  if (rows < 1 || cols < block || cols % block) return -4;
+  const int64_t rb = f32 ? cols * 4 : row_bytes(qtype, cols);
+  auto work = [&](int64_t r0, int64_t r1) {
+    std::vector<float> buf((size_t)cols);
+    for (int64_t r = r0; r < r1; ++r) {
+      normal_row(seed, r, stddev, buf.data(), cols);
+      uint8_t* o = dst + r * rb;
+      if (f32) {
+        std::memcpy(o, buf.data(), (size_t)cols * 4);
+      } else if (qtype == kTypeQ8_0) {
+        q8_0_row(buf.data(), cols, o);
+      } else {
+        for (int64_t b = 0; b < cols / 256; ++b) {
+          if (qtype == kTypeQ4_K) q4_k_block(buf.data() + 256 * b, o + 144 * b);
+          else q6_k_block(buf.data() + 256 * b, o + 210 * b);
+        }
+      }
+    }
+  };
+  if (threads < 1) threads = 1;
+  if (threads > rows) threads = (int)rows;
+  std::vector<std::thread> pool;
+  const int64_t chunk = (rows + threads - 1) / threads;
+  for (int i = 0; i < threads; ++i) {
+    const int64_t r0 = i * chunk, r1 = r0 + chunk < rows ? r0 + chunk : rows;
+    if (r0 < r1) pool.emplace_back(work, r0, r1);
+  }
+  for (auto& th : pool) th.join();
+  return 0;
+}
+
 }  // namespace gi

@@ -48,8 +48,35 @@ EXPORTS = (
     "gi_cuda_gemm_buf", "gi_cuda_gemv_q8_0", "gi_cuda_gemv_q4_k", "gi_cuda_gemv_q6_k",
     "gi_cuda_gemm_q8_0", "gi_cuda_gemm_q4_k", "gi_cuda_gemm_q6_k", "gi_cuda_gemv_dev",
     "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl",
-    "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize",
+    "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize", "gi_quantize_seeded",
+    "gi_cuda_alloc_buffers", "gi_cuda_forward_transformer", "gi_cuda_model_create", "gi_cuda_model_destroy",
+    "gi_cuda_model_reset", "gi_cuda_model_generate",
 )
+
+
+class LayerWeights(ctypes.Structure):
+    """gi_cuda_layer_weights_t (metal_layer_weights_t, metal_bridge.h:54-67)."""
+    _fields_ = [("wq", ctypes.c_void_p), ("wq_type", ctypes.c_int),
+                ("wk", ctypes.c_void_p), ("wk_type", ctypes.c_int),
+                ("wv", ctypes.c_void_p), ("wv_type", ctypes.c_int),
+                ("wo", ctypes.c_void_p), ("wo_type", ctypes.c_int),
+                ("ffn_gate", ctypes.c_void_p), ("ffn_gate_type", ctypes.c_int),
+                ("ffn_up", ctypes.c_void_p), ("ffn_up_type", ctypes.c_int),
+                ("ffn_down", ctypes.c_void_p), ("ffn_down_type", ctypes.c_int),
+                ("attn_norm", ctypes.c_void_p), ("ffn_norm", ctypes.c_void_p),
+                ("bq", ctypes.c_void_p), ("bk", ctypes.c_void_p), ("bv", ctypes.c_void_p)]
+
+
+class ModelDesc(ctypes.Structure):
+    """gi_cuda_model_desc_t."""
+    _fields_ = [("num_layers", ctypes.c_uint32), ("dim", ctypes.c_uint32), ("hidden_dim", ctypes.c_uint32),
+                ("num_heads", ctypes.c_uint32), ("num_kv_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
+                ("vocab_size", ctypes.c_uint32), ("max_seq", ctypes.c_uint32), ("max_pos", ctypes.c_uint32),
+                ("norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
+                ("layers", ctypes.POINTER(LayerWeights)),
+                ("token_embd", ctypes.c_void_p), ("token_embd_type", ctypes.c_int),
+                ("output_norm", ctypes.c_void_p),
+                ("output_weight", ctypes.c_void_p), ("output_weight_type", ctypes.c_int)]
 
 
 class GoInferCudaError(RuntimeError):
@@ -98,6 +125,16 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "gi_cuda_last_error": ([], ctypes.c_char_p),
         "gi_quant_row_bytes": ([i32, ctypes.c_int64], ctypes.c_int64),
         "gi_quantize": ([i32, f32p, ctypes.c_int64, ctypes.c_int64, vp, i32], i32),
+        "gi_quantize_seeded": ([i32, ctypes.c_uint64, ctypes.c_float, ctypes.c_int64, ctypes.c_int64, vp, i32], i32),
+        "gi_cuda_alloc_buffers": ([u32, u32, u32, u32, u32, u32], i32),
+        "gi_cuda_forward_transformer": ([f32p, f32p, ctypes.POINTER(u32), ctypes.POINTER(LayerWeights), vp, vp, i32,
+                                         u32, u32, u32, u32, u32, u32, u32, u32, u32, u32, u32, u32,
+                                         ctypes.c_float, ctypes.c_float, ctypes.c_float], i32),
+        "gi_cuda_model_create": ([ctypes.POINTER(ModelDesc)], vp),
+        "gi_cuda_model_destroy": ([vp], None),
+        "gi_cuda_model_reset": ([vp], i32),
+        "gi_cuda_model_generate": ([vp, ctypes.POINTER(ctypes.c_int32), u32, u32, u32, ctypes.POINTER(u32), f32p,
+                                    f32p], i32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -309,3 +346,94 @@ class Weights:
         for b in self.bufs.values():
             ReleaseBuffer(b)
         self.bufs.clear()
+
+
+# ---- whole-model decode ----------------------------------------------------
+
+def quantize_seeded(quant_type: int, seed: int, std: float, rows: int, cols: int, threads: int = 0) -> np.ndarray:
+    """Seeded N(0, std) rows x cols, quantised (F32: the float32 values)."""
+    rb = cols * 4 if quant_type == TYPE_F32 else row_bytes(quant_type, cols)
+    if rb < 0:
+        raise GoInferCudaError("gi_quantize_seeded", ERR_UNSUPPORTED_TYPE)
+    out = np.empty(max(rows * rb, 1), np.uint8)
+    _err("gi_quantize_seeded", load_library().gi_quantize_seeded(quant_type, seed, std, rows, cols,
+                                                                   out.ctypes.data, threads))
+    return out
+
+
+def _h(buf) -> Optional[int]:
+    return None if buf is None else buf.handle
+
+
+def layer_table(layers: list[dict]) -> ctypes.Array:
+    """LayerWeights[] from dicts of Buffers (keys wq, wk, wv, wo, ffn_gate, ffn_up, ffn_down, attn_norm,
+    ffn_norm, optional bq/bk/bv) and their types (wq_type ...)."""
+    arr = (LayerWeights * len(layers))()
+    for i, L in enumerate(layers):
+        e = arr[i]
+        for k in ("wq", "wk", "wv", "wo", "ffn_gate", "ffn_up", "ffn_down"):
+            setattr(e, k, _h(L[k]))
+            setattr(e, k + "_type", L[k + "_type"])
+        for k in ("attn_norm", "ffn_norm", "bq", "bk", "bv"):
+            setattr(e, k, _h(L.get(k)))
+    return arr
+
+
+def AllocBuffers(dim: int, hidden_dim: int, kv_dim: int, vocab_size: int, num_layers: int, max_seq: int) -> None:
+    """metal.AllocBuffers (metal_bridge.h:23)."""
+    _err("gi_cuda_alloc_buffers", load_library().gi_cuda_alloc_buffers(dim, hidden_dim, kv_dim, vocab_size,
+                                                                         num_layers, max_seq))
+
+
+def ForwardTransformer(x: np.ndarray, layers: ctypes.Array, out_norm, out_weight, out_type: int, *, num_layers: int,
+                       dim: int, hidden_dim: int, kv_dim: int, vocab_size: int, num_heads: int, num_kv_heads: int,
+                       head_dim: int, pos: int, slot: int, max_seq: int, active_context: int, norm_eps: float,
+                       rope_theta: float, attn_scale: float, want_logits: bool = True):
+    """metal.ForwardTransformer (metal_bridge.h:134-157): (logits or None, token)."""
+    logits = np.empty(vocab_size, np.float32) if want_logits else None
+    tok = ctypes.c_uint32(0)
+    _err("gi_cuda_forward_transformer", load_library().gi_cuda_forward_transformer(
+        _f32(np.ascontiguousarray(x, np.float32)), _f32(logits) if logits is not None else None,
+        ctypes.byref(tok), layers, _h(out_norm), _h(out_weight), out_type, num_layers, dim, hidden_dim, kv_dim,
+        vocab_size, num_heads, num_kv_heads, head_dim, pos, slot, max_seq, active_context, norm_eps, rope_theta,
+        attn_scale))
+    return logits, tok.value
+
+
+class Model:
+    """A device-resident model (gi_cuda_model_*): greedy generation on the GPU."""
+
+    def __init__(self, desc: ModelDesc, keep: object = None):
+        self._keep = keep  # buffers and tables that must outlive the handle
+        self.vocab = desc.vocab_size
+        h = load_library().gi_cuda_model_create(ctypes.byref(desc))
+        if not h:
+            raise GoInferCudaError("gi_cuda_model_create", ERR_UNAVAILABLE,
+                                   load_library().gi_cuda_last_error().decode(errors="replace"))
+        self.handle = h
+
+    def generate(self, tokens, n_gen: int, start_pos: int = 0, want_logits: bool = False):
+        """(generated ids, last logits or None, device ms of the n_gen - 1 decode steps)."""
+        toks = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty(n_gen, np.uint32)
+        logits = np.empty(self.vocab, np.float32) if want_logits else None
+        ms = ctypes.c_float(0.0)
+        _err("gi_cuda_model_generate", load_library().gi_cuda_model_generate(
+            self.handle, toks.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), toks.size, start_pos, n_gen,
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)), _f32(logits) if logits is not None else None,
+            ctypes.byref(ms)))
+        return out, logits, ms.value
+
+    def reset(self) -> None:
+        _err("gi_cuda_model_reset", load_library().gi_cuda_model_reset(self.handle))
+
+    def close(self) -> None:
+        if self.handle:
+            load_library().gi_cuda_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,143 @@
+"""Synthetic Llama-shaped GGUF models for the decode workloads.
+
+The benchmark configurations name random-init models (weights N(0, 0.02),
+quantised Q4_K, lm_head Q6_K, norms fp32).  This module draws them with the
+library's seeded generator (gi_quantize_seeded: one stream per (seed, row),
+so the bytes are the same on every machine and thread count), uploads them
+as weight buffers and describes them to the device-resident model
+(gi_cuda_model_create) or to gi_cuda_forward_transformer.  Tensor names and
+roles follow go-infer's GGUF loader (blk.N.attn_q.weight ...,
+pkg/engine/weights.go); norm weights are ones, the usual RMSNorm init.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+
+import goinfer_cuda as G
+
+
+@dataclass
+class LlamaConfig:
+    n_layers: int
+    dim: int
+    hidden: int
+    n_heads: int
+    n_kv_heads: int
+    vocab: int
+    max_seq: int
+    eps: float = 1e-5
+    rope_theta: float = 10000.0
+    wtype: int = G.TYPE_Q4_K
+    out_type: int = G.TYPE_Q6_K
+    embd_type: int = G.TYPE_Q4_K
+    std: float = 0.02
+
+    @property
+    def head_dim(self) -> int:  # config.go:29-37
+        return self.dim // self.n_heads
+
+    @property
+    def kv_dim(self) -> int:  # config.go:48-56
+        return self.head_dim * self.n_kv_heads
+
+    @property
+    def q_dim(self) -> int:
+        return self.head_dim * self.n_heads
+
+
+# Config 4: Llama-2-7B shape (32 layers, d=4096, 32 heads, FFN 11008, vocab
+# 32000, RoPE base 10000), 128-token prompt + 64 greedy steps.
+LLAMA2_7B = LlamaConfig(n_layers=32, dim=4096, hidden=11008, n_heads=32, n_kv_heads=32, vocab=32000, max_seq=192)
+
+LAYER_MATS = ("wq", "wk", "wv", "wo", "ffn_gate", "ffn_up", "ffn_down")
+
+
+def layer_shapes(cfg: LlamaConfig) -> dict:
+    """rows x cols of each layer matrix (rows = output features)."""
+    return {"wq": (cfg.q_dim, cfg.dim), "wk": (cfg.kv_dim, cfg.dim), "wv": (cfg.kv_dim, cfg.dim),
+            "wo": (cfg.dim, cfg.q_dim), "ffn_gate": (cfg.hidden, cfg.dim), "ffn_up": (cfg.hidden, cfg.dim),
+            "ffn_down": (cfg.dim, cfg.hidden)}
+
+
+@dataclass
+class HostModel:
+    """Raw tensors of a model: {name: (ggml type, uint8/float32 array)}."""
+    cfg: LlamaConfig
+    tensors: dict = field(default_factory=dict)
+
+    def layer(self, l: int, name: str):
+        return self.tensors[f"blk.{l}.{name}"]
+
+
+def synth_model(cfg: LlamaConfig, seed: int, threads: int = 0) -> HostModel:
+    """Every tensor drawn with seed * 1_000_003 + its index."""
+    m = HostModel(cfg)
+    shapes = layer_shapes(cfg)
+    k = 0
+
+    def draw(qt, rows, cols):
+        nonlocal k
+        k += 1
+        return (qt, G.quantize_seeded(qt, seed * 1_000_003 + k, cfg.std, rows, cols, threads))
+
+    m.tensors["token_embd.weight"] = draw(cfg.embd_type, cfg.vocab, cfg.dim)
+    for l in range(cfg.n_layers):
+        for name in LAYER_MATS:
+            r, c = shapes[name]
+            m.tensors[f"blk.{l}.{name}.weight"] = draw(cfg.wtype, r, c)
+        for name in ("attn_norm", "ffn_norm"):
+            m.tensors[f"blk.{l}.{name}.weight"] = (G.TYPE_F32, np.ones(cfg.dim, np.float32))
+    m.tensors["output_norm.weight"] = (G.TYPE_F32, np.ones(cfg.dim, np.float32))
+    m.tensors["output.weight"] = draw(cfg.out_type, cfg.vocab, cfg.dim)
+    return m
+
+
+class DeviceModel:
+    """The tensors of a HostModel as weight buffers, with the layer table."""
+
+    def __init__(self, host: HostModel):
+        self.cfg = host.cfg
+        self.bufs = {}
+        for name, (_qt, arr) in host.tensors.items():
+            b = G.CreateBuffer(arr)
+            if b is None:
+                raise G.GoInferCudaError("CreateBuffer " + name, G.ERR_BUFFER)
+            self.bufs[name] = b
+        self.types = {name: qt for name, (qt, _a) in host.tensors.items()}
+        layers = []
+        for l in range(self.cfg.n_layers):
+            d = {}
+            for name in LAYER_MATS:
+                key = f"blk.{l}.{name}.weight"
+                d[name] = self.bufs[key]
+                d[name + "_type"] = self.types[key]
+            d["attn_norm"] = self.bufs[f"blk.{l}.attn_norm.weight"]
+            d["ffn_norm"] = self.bufs[f"blk.{l}.ffn_norm.weight"]
+            layers.append(d)
+        self.table = G.layer_table(layers)
+
+    def desc(self, max_pos: int = 0) -> G.ModelDesc:
+        c = self.cfg
+        d = G.ModelDesc()
+        d.num_layers, d.dim, d.hidden_dim = c.n_layers, c.dim, c.hidden
+        d.num_heads, d.num_kv_heads, d.head_dim = c.n_heads, c.n_kv_heads, c.head_dim
+        d.vocab_size, d.max_seq, d.max_pos = c.vocab, c.max_seq, max_pos
+        d.norm_eps, d.rope_theta = c.eps, c.rope_theta
+        d.layers = ctypes.cast(self.table, ctypes.POINTER(G.LayerWeights))
+        d.token_embd = self.bufs["token_embd.weight"].handle
+        d.token_embd_type = self.types["token_embd.weight"]
+        d.output_norm = self.bufs["output_norm.weight"].handle
+        d.output_weight = self.bufs["output.weight"].handle
+        d.output_weight_type = self.types["output.weight"]
+        return d
+
+    def model(self, max_pos: int = 0) -> G.Model:
+        return G.Model(self.desc(max_pos), keep=self)
+
+    def close(self) -> None:
+        for b in self.bufs.values():
+            G.ReleaseBuffer(b)
+        self.bufs.clear()

@@ -131,6 +131,91 @@ int gi_cuda_gemv_multi_dev(int quant_type, int nmat, float* const* y, const floa
                            const void* const* w, const size_t* w_bytes, const uint32_t* rows,
                            uint32_t cols, void* stream);
 
+/* ---- whole-model decode (Llama layers) ---------------------------------- */
+
+/* Replaces int metal_alloc_buffers(uint32_t dim, uint32_t hidden_dim,
+ * uint32_t kv_dim, uint32_t vocab_size, uint32_t num_layers, uint32_t
+ * max_seq), metal_bridge.h:23: records the sizes of the persistent
+ * activation and KV-cache buffers of gi_cuda_forward_transformer (allocated
+ * at its first call, when the head layout is known).  Releases the previous
+ * ones; the KV cache starts at zero. */
+int gi_cuda_alloc_buffers(uint32_t dim, uint32_t hidden_dim, uint32_t kv_dim, uint32_t vocab_size,
+                          uint32_t num_layers, uint32_t max_seq);
+
+/* Replaces metal_layer_weights_t, metal_bridge.h:54-67.  Matrices are
+ * buffers of raw GGUF rows with their GGML type; attn_norm / ffn_norm are
+ * float32 buffers of dim values; bq / bk / bv are optional float32 biases
+ * (NULL for Llama). */
+typedef struct {
+  gi_cuda_buffer_t wq;
+  int wq_type;
+  gi_cuda_buffer_t wk;
+  int wk_type;
+  gi_cuda_buffer_t wv;
+  int wv_type;
+  gi_cuda_buffer_t wo;
+  int wo_type;
+  gi_cuda_buffer_t ffn_gate;
+  int ffn_gate_type;
+  gi_cuda_buffer_t ffn_up;
+  int ffn_up_type;
+  gi_cuda_buffer_t ffn_down;
+  int ffn_down_type;
+  gi_cuda_buffer_t attn_norm;
+  gi_cuda_buffer_t ffn_norm;
+  gi_cuda_buffer_t bq;
+  gi_cuda_buffer_t bk;
+  gi_cuda_buffer_t bv;
+} gi_cuda_layer_weights_t;
+
+/* Replaces int metal_forward_transformer(...), metal_bridge.h:134-157: one
+ * decode step over all layers with device-resident activations and KV cache
+ * (the work of Engine.Forward, pkg/engine/forward.go:102-130).  initial_x:
+ * host float32[dim], the embedding the caller extracted; out_logits (host
+ * float32[vocab_size]) and out_token (first maximum) may each be NULL.
+ * Blocks until the results are on the host. */
+int gi_cuda_forward_transformer(const float* initial_x, float* out_logits, uint32_t* out_token,
+                                const gi_cuda_layer_weights_t* layers, gi_cuda_buffer_t output_norm_buf,
+                                gi_cuda_buffer_t output_weight_buf, int output_weight_type, uint32_t num_layers,
+                                uint32_t dim, uint32_t hidden_dim, uint32_t kv_dim, uint32_t vocab_size,
+                                uint32_t num_heads, uint32_t num_kv_heads, uint32_t head_dim, uint32_t pos,
+                                uint32_t slot, uint32_t max_seq, uint32_t active_context, float norm_eps,
+                                float rope_theta, float attn_scale);
+
+/* Device-resident greedy generation (no reference counterpart: the
+ * engine's greedy loop, pkg/engine/engine.go:505-545, with the embedding
+ * lookup, the argmax and the position advance on the device and each token
+ * one CUDA-graph replay).  The model keeps its own KV cache. */
+typedef struct {
+  uint32_t num_layers, dim, hidden_dim, num_heads, num_kv_heads, head_dim, vocab_size;
+  uint32_t max_seq; /* KV-cache slots (rolling) */
+  uint32_t max_pos; /* positions the RoPE table covers; 0 = 32768 */
+  float norm_eps, rope_theta;
+  const gi_cuda_layer_weights_t* layers; /* num_layers entries */
+  gi_cuda_buffer_t token_embd;           /* vocab_size rows of dim */
+  int token_embd_type;
+  gi_cuda_buffer_t output_norm;
+  gi_cuda_buffer_t output_weight;
+  int output_weight_type;
+} gi_cuda_model_desc_t;
+
+typedef void* gi_cuda_model_t;
+
+/* NULL on failure (text in gi_cuda_last_error). */
+gi_cuda_model_t gi_cuda_model_create(const gi_cuda_model_desc_t* desc);
+void gi_cuda_model_destroy(gi_cuda_model_t model);
+
+/* Zeroes the KV cache. */
+int gi_cuda_model_reset(gi_cuda_model_t model);
+
+/* Runs tokens[0..n_tokens) at positions start_pos.. (one step each), then
+ * greedy steps: out_tokens[0..n_gen) are the argmax after the last prompt
+ * token and after each generated token (n_gen >= 1).  out_logits (host
+ * float32[vocab_size] or NULL) receives the logits of the last step;
+ * decode_ms (or NULL) the device time of the n_gen - 1 generation steps. */
+int gi_cuda_model_generate(gi_cuda_model_t model, const int32_t* tokens, uint32_t n_tokens, uint32_t start_pos,
+                           uint32_t n_gen, uint32_t* out_tokens, float* out_logits, float* decode_ms);
+
 /* Device address / size of a buffer created by gi_cuda_create_buffer. */
 const void* gi_cuda_buffer_device_ptr(gi_cuda_buffer_t buf);
 size_t gi_cuda_buffer_bytes(gi_cuda_buffer_t buf);
@@ -155,6 +240,13 @@ int64_t gi_quant_row_bytes(int quant_type, int64_t cols);
  * K-quant quantiser).  threads <= 0 uses every host core. */
 int gi_quantize(int quant_type, const float* src, int64_t rows, int64_t cols, void* dst,
                 int threads);
+
+/* Synthetic weights for the benchmark configurations (no reference
+ * counterpart): rows x cols drawn from N(0, stddev) with a generator keyed
+ * by (seed, row), quantised like gi_quantize (GI_TYPE_F32 stores the float32
+ * values).  The bytes do not depend on `threads` (<= 0: every core). */
+int gi_quantize_seeded(int quant_type, uint64_t seed, float stddev, int64_t rows, int64_t cols, void* dst,
+                       int threads);
 
 #ifdef __cplusplus
 }

@@ -365,3 +365,152 @@ int ref_matmul_batch(int type, float* y, const float* x, const uint8_t* raw, int
   }
   return 0;
 }
+
+/* ---------------------------------------------------------------------------
+ * Whole-model decode.  Float32 arithmetic is written one rounding per Go
+ * operation (the file is built with -ffp-contract=off, like Go on amd64 which
+ * never fuses); Go's float64 math.Sqrt/Pow/Cos/Sin/Exp become libm's double
+ * functions (sqrt is correctly rounded in both; the others agree to within an
+ * ulp of the double result, which the float32 conversion hides except in
+ * rare ties).
+ * ------------------------------------------------------------------------- */
+
+void ref_rmsnorm(float* out, const float* x, const float* w, int64_t n, float eps) {
+  float sum = 0.0f;
+  for (int64_t i = 0; i < n; i++) sum = sum + x[i] * x[i];
+  float mean = sum / (float)n;
+  float scale = (float)(1.0 / sqrt((double)(mean + eps)));
+  for (int64_t i = 0; i < n; i++) out[i] = x[i] * scale * w[i];
+}
+
+void ref_apply_rope(float* vec, int pos, int head_dim, float theta) {
+  int half = head_dim / 2;
+  for (int i = 0; i < half; i++) {
+    double freq = 1.0 / pow((double)theta, (double)(2 * i) / (double)head_dim);
+    double val = (double)pos * freq;
+    float c = (float)cos(val);
+    float sn = (float)sin(val);
+    float v0 = vec[i], v1 = vec[i + half];
+    vec[i] = v0 * c - v1 * sn;
+    vec[i + half] = v0 * sn + v1 * c;
+  }
+}
+
+void ref_swiglu(float* gate, const float* up, int64_t n) {
+  for (int64_t i = 0; i < n; i++) {
+    float g = gate[i];
+    float silu = g / (1.0f + (float)exp((double)(-g)));
+    gate[i] = silu * up[i];
+  }
+}
+
+void ref_softmax(float* x, int64_t n) {
+  if (n == 0) return;
+  float maxv = x[0];
+  for (int64_t i = 1; i < n; i++)
+    if (x[i] > maxv) maxv = x[i];
+  float sum = 0.0f;
+  for (int64_t i = 0; i < n; i++) {
+    float v = (float)exp((double)(x[i] - maxv));
+    x[i] = v;
+    sum = sum + v;
+  }
+  if (sum > 0) {
+    float inv = 1.0f / sum;
+    for (int64_t i = 0; i < n; i++) x[i] = x[i] * inv;
+  }
+}
+
+double ref_math_sqrt(double x) {
+  if (x <= 0) return 0;
+  double z = x / 2;
+  for (int i = 0; i < 10; i++) z = (z + x / z) / 2;
+  return z;
+}
+
+int ref_extract_embedding(const ref_mat* tbl, int token, float* out, int dim) {
+  int64_t bpr = ref_bytes_per_row(tbl->type, dim);
+  if (bpr < 0) return -2;
+  deq_row(tbl->type, tbl->raw + (int64_t)token * bpr, dim, bpr, out);
+  return 0;
+}
+
+int ref_argmax(const float* logits, int64_t n) {
+  int64_t best = 0;
+  float maxv = logits[0];
+  for (int64_t i = 0; i < n; i++)
+    if (logits[i] > maxv) {
+      maxv = logits[i];
+      best = i;
+    }
+  return (int)best;
+}
+
+static int mm(const ref_model* m, const ref_mat* w, float* y, const float* x, int64_t rows, int64_t cols) {
+  return ref_matmul(w->type, y, x, w->raw, rows, cols, m->nthreads);
+}
+
+int ref_forward(const ref_model* m, float* key, float* value, int token, int pos, float* logits) {
+  const int dim = m->dim, hd = dim / m->n_heads;           /* config.go:29-37 */
+  const int kv_dim = hd * m->n_kv_heads;                   /* config.go:48-56 */
+  const int kv_mul = m->n_heads / m->n_kv_heads;           /* config.go:59-64 */
+  const int64_t layer_stride = (int64_t)m->max_seq * kv_dim;
+  float* x = (float*)calloc((size_t)dim, 4);
+  float* xb = (float*)calloc((size_t)dim, 4);
+  float* q = (float*)calloc((size_t)dim, 4);
+  float* k = (float*)calloc((size_t)kv_dim, 4);
+  float* v = (float*)calloc((size_t)kv_dim, 4);
+  float* att = (float*)calloc((size_t)dim, 4);
+  float* proj = (float*)calloc((size_t)dim, 4);
+  float* gate = (float*)calloc((size_t)m->hidden, 4);
+  float* up = (float*)calloc((size_t)m->hidden, 4);
+  float* down = (float*)calloc((size_t)dim, 4);
+  float* scores = (float*)calloc((size_t)m->max_seq, 4);
+  int rc = ref_extract_embedding(&m->tok_embd, token, x, dim);
+  int active = pos + 1;
+  if (active > m->max_seq) active = m->max_seq;
+  const float attn_scale = (float)(1.0 / ref_math_sqrt((double)hd));
+  for (int l = 0; l < m->n_layers && rc == 0; l++) {
+    const ref_layer* L = &m->layers[l];
+    float* kc = key + l * layer_stride;
+    float* vc = value + l * layer_stride;
+    ref_rmsnorm(xb, x, L->attn_norm, dim, m->eps);
+    rc |= mm(m, &L->wq, q, xb, dim, dim);
+    rc |= mm(m, &L->wk, k, xb, kv_dim, dim);
+    rc |= mm(m, &L->wv, v, xb, kv_dim, dim);
+    for (int h = 0; h < m->n_heads; h++) ref_apply_rope(q + h * hd, pos, hd, m->rope_theta);
+    for (int h = 0; h < m->n_kv_heads; h++) ref_apply_rope(k + h * hd, pos, hd, m->rope_theta);
+    const int slot = pos % m->max_seq;
+    memcpy(kc + (int64_t)slot * kv_dim, k, (size_t)kv_dim * 4);
+    memcpy(vc + (int64_t)slot * kv_dim, v, (size_t)kv_dim * 4);
+    memset(att, 0, (size_t)dim * 4);
+    for (int h = 0; h < m->n_heads; h++) {
+      const float* qh = q + h * hd;
+      const int kvh = h / kv_mul;
+      for (int t = 0; t < active; t++)
+        scores[t] = ref_dot_vec_f32(qh, kc + (int64_t)t * kv_dim + kvh * hd, hd) * attn_scale;
+      ref_softmax(scores, active);
+      float* oh = att + h * hd;
+      for (int t = 0; t < active; t++) {
+        const float* vh = vc + (int64_t)t * kv_dim + kvh * hd;
+        const float wt = scores[t];
+        for (int d = 0; d < hd; d++) oh[d] = oh[d] + wt * vh[d];
+      }
+    }
+    rc |= mm(m, &L->wo, proj, att, dim, dim);
+    for (int i = 0; i < dim; i++) x[i] = x[i] + proj[i];
+    ref_rmsnorm(xb, x, L->ffn_norm, dim, m->eps);
+    rc |= mm(m, &L->gate, gate, xb, m->hidden, dim);
+    rc |= mm(m, &L->up, up, xb, m->hidden, dim);
+    ref_swiglu(gate, up, m->hidden);
+    rc |= mm(m, &L->down, down, gate, dim, m->hidden);
+    for (int i = 0; i < dim; i++) x[i] = x[i] + down[i];
+  }
+  if (rc == 0) {
+    ref_rmsnorm(xb, x, m->out_norm, dim, m->eps);
+    rc = mm(m, &m->out, logits, xb, m->vocab, dim);
+  }
+  free(x); free(xb); free(q); free(k); free(v); free(att); free(proj);
+  free(gate); free(up); free(down); free(scores);
+  return rc ? -2 : 0;
+}

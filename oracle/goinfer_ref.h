@@ -90,6 +90,52 @@ int ref_matmul_f64(int type, double* y, const float* x, const uint8_t* raw,
 int ref_matmul_batch(int type, float* y, const float* x, const uint8_t* raw,
                      int64_t batch, int64_t rows, int64_t cols, int nthreads);
 
+/* ---- whole-model decode: the CPU branch of Engine.Forward ------------------
+ * (pkg/engine/forward.go:14-297 with the Metal paths off), Llama layers only.
+ * Weight matrices are raw GGUF rows (rows = output features) of `type`
+ * (REF_GGML_F32 rows are float32).  The KV cache is the reference's float32
+ * rolling cache (pkg/engine/kvcache.go): key/value[layer][slot][kv_dim],
+ * slot = pos % max_seq. */
+typedef struct {
+  int type;
+  const uint8_t* raw;
+} ref_mat;
+
+typedef struct {
+  ref_mat wq, wk, wv, wo, gate, up, down;
+  const float* attn_norm; /* dim */
+  const float* ffn_norm;  /* dim */
+} ref_layer;
+
+typedef struct {
+  int n_layers, dim, hidden, n_heads, n_kv_heads, vocab, max_seq;
+  float eps, rope_theta;
+  ref_mat tok_embd;       /* vocab x dim */
+  const float* out_norm;  /* dim */
+  ref_mat out;            /* vocab x dim */
+  const ref_layer* layers;
+  int nthreads;           /* GEMV workers, gemv.go:17-24 */
+} ref_model;
+
+/* pkg/math/kernels.go:9-19 */
+void ref_rmsnorm(float* out, const float* x, const float* w, int64_t n, float eps);
+/* pkg/math/kernels.go:22-36 */
+void ref_apply_rope(float* vec, int pos, int head_dim, float theta);
+/* pkg/math/kernels.go:39-46 */
+void ref_swiglu(float* gate, const float* up, int64_t n);
+/* pkg/math/kernels.go:49-71 */
+void ref_softmax(float* x, int64_t n);
+/* forward.go:771-780 (10 Newton steps) */
+double ref_math_sqrt(double x);
+/* weights.go:132-234 for F32, Q8_0, Q4_K and Q6_K tables */
+int ref_extract_embedding(const ref_mat* tbl, int token, float* out, int dim);
+/* Engine.Forward: logits[vocab] for `token` at `pos`; key/value caches are
+ * n_layers * max_seq * kv_dim floats.  Returns 0, or -2 for an unsupported
+ * weight type. */
+int ref_forward(const ref_model* m, float* key, float* value, int token, int pos, float* logits);
+/* forward.go:397-404: first maximum wins. */
+int ref_argmax(const float* logits, int64_t n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -164,3 +164,135 @@ def matmul_batch(qtype: int, x: np.ndarray, raw: np.ndarray, batch: int, rows: i
     if rc:
         raise ValueError(f"ref_matmul_batch: unsupported type {qtype}")
     return y.reshape(batch, rows)
+
+
+# ---- whole-model decode (ref_forward, the CPU branch of Engine.Forward) ------
+
+class RefMat(ctypes.Structure):
+    _fields_ = [("type", ctypes.c_int), ("raw", ctypes.c_void_p)]
+
+
+class RefLayer(ctypes.Structure):
+    _fields_ = [("wq", RefMat), ("wk", RefMat), ("wv", RefMat), ("wo", RefMat), ("gate", RefMat),
+                ("up", RefMat), ("down", RefMat), ("attn_norm", ctypes.c_void_p), ("ffn_norm", ctypes.c_void_p)]
+
+
+class RefModelC(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int), ("dim", ctypes.c_int), ("hidden", ctypes.c_int),
+                ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("vocab", ctypes.c_int),
+                ("max_seq", ctypes.c_int), ("eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
+                ("tok_embd", RefMat), ("out_norm", ctypes.c_void_p), ("out", RefMat),
+                ("layers", ctypes.POINTER(RefLayer)), ("nthreads", ctypes.c_int)]
+
+
+def _forward_sigs(L):
+    L.ref_forward.argtypes = [ctypes.POINTER(RefModelC), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                              ctypes.c_int, ctypes.c_void_p]
+    L.ref_forward.restype = ctypes.c_int
+    L.ref_rmsnorm.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_float]
+    L.ref_apply_rope.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_float]
+    L.ref_swiglu.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64]
+    L.ref_softmax.argtypes = [ctypes.c_void_p, ctypes.c_int64]
+    L.ref_math_sqrt.argtypes = [ctypes.c_double]
+    L.ref_math_sqrt.restype = ctypes.c_double
+    L.ref_argmax.argtypes = [ctypes.c_void_p, ctypes.c_int64]
+    L.ref_argmax.restype = ctypes.c_int
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    L = lib(); _forward_sigs(L)
+    x = np.ascontiguousarray(x, np.float32); w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    L.ref_rmsnorm(out.ctypes.data, x.ctypes.data, w.ctypes.data, x.size, eps)
+    return out
+
+
+def apply_rope(vec: np.ndarray, pos: int, theta: float) -> np.ndarray:
+    L = lib(); _forward_sigs(L)
+    v = np.array(vec, np.float32)
+    L.ref_apply_rope(v.ctypes.data, pos, v.size, theta)
+    return v
+
+
+def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    L = lib(); _forward_sigs(L)
+    g = np.array(gate, np.float32); u = np.ascontiguousarray(up, np.float32)
+    L.ref_swiglu(g.ctypes.data, u.ctypes.data, g.size)
+    return g
+
+
+def softmax(x: np.ndarray) -> np.ndarray:
+    L = lib(); _forward_sigs(L)
+    v = np.array(x, np.float32)
+    L.ref_softmax(v.ctypes.data, v.size)
+    return v
+
+
+def math_sqrt(x: float) -> float:
+    L = lib(); _forward_sigs(L)
+    return L.ref_math_sqrt(x)
+
+
+class RefModel:
+    """The oracle's view of a model: raw tensors {name: (type, array)} with
+    go-infer's GGUF names, its own float32 KV cache, Engine.Forward per step."""
+
+    def __init__(self, cfg, tensors: dict, nthreads: int = 0):
+        self.cfg = cfg
+        self._keep = []
+
+        def mat(name):
+            qt, arr = tensors[name]
+            arr = np.ascontiguousarray(arr)
+            self._keep.append(arr)
+            return RefMat(qt, arr.ctypes.data)
+
+        def vec(name):
+            _qt, arr = tensors[name]
+            arr = np.ascontiguousarray(arr, np.float32)
+            self._keep.append(arr)
+            return arr.ctypes.data
+
+        layers = (RefLayer * cfg.n_layers)()
+        for l in range(cfg.n_layers):
+            p = f"blk.{l}."
+            layers[l] = RefLayer(mat(p + "wq.weight"), mat(p + "wk.weight"), mat(p + "wv.weight"),
+                                 mat(p + "wo.weight"), mat(p + "ffn_gate.weight"), mat(p + "ffn_up.weight"),
+                                 mat(p + "ffn_down.weight"), vec(p + "attn_norm.weight"),
+                                 vec(p + "ffn_norm.weight"))
+        self._layers = layers
+        self.c = RefModelC(cfg.n_layers, cfg.dim, cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.vocab, cfg.max_seq,
+                           cfg.eps, cfg.rope_theta, mat("token_embd.weight"), vec("output_norm.weight"),
+                           mat("output.weight"), layers, nthreads or os.cpu_count() or 1)
+        kv = cfg.n_layers * cfg.max_seq * cfg.kv_dim
+        self.key = np.zeros(kv, np.float32)
+        self.value = np.zeros(kv, np.float32)
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        L = lib(); _forward_sigs(L)
+        logits = np.empty(self.cfg.vocab, np.float32)
+        rc = L.ref_forward(ctypes.byref(self.c), self.key.ctypes.data, self.value.ctypes.data, token, pos,
+                           logits.ctypes.data)
+        if rc:
+            raise RuntimeError(f"ref_forward failed: {rc}")
+        return logits
+
+    def greedy(self, prompt, n_gen: int, start_pos: int = 0):
+        """Engine.Generate at temperature 0 with sequential prefill: the ids
+        and, per generated id, the top-2 logit margin."""
+        L = lib(); _forward_sigs(L)
+        pos = start_pos
+        logits = None
+        for t in prompt:
+            logits = self.forward(int(t), pos)
+            pos += 1
+        ids, margins = [], []
+        for i in range(n_gen):
+            nxt = int(L.ref_argmax(logits.ctypes.data, logits.size))
+            top = np.sort(logits)[-2:]
+            ids.append(nxt)
+            margins.append(float(top[1] - top[0]))
+            if i + 1 < n_gen:
+                logits = self.forward(nxt, pos)
+                pos += 1
+        return np.array(ids, np.uint32), np.array(margins), logits

@@ -1,0 +1,132 @@
+"""GPU whole-model decode against the oracle's Engine.Forward, through the C ABI.
+
+gi_cuda_forward_transformer (the metal_forward_transformer mirror) is
+compared step by step on logits (per-element parity bar); the
+device-resident greedy loop (gi_cuda_model_generate) on token ids, which
+must be identical to the oracle's greedy decode (forward.go:394-405,
+first maximum), with the smallest top-2 margin reported on failure.
+"""
+import numpy as np
+import pytest
+
+import goinfer_cuda as G
+import oracle as O
+import synth
+from _util import assert_parity
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda():
+    G.Init(0)
+    assert G.IsAvailable()
+    yield
+
+
+SMALL = synth.LlamaConfig(n_layers=2, dim=512, hidden=1024, n_heads=8, n_kv_heads=2, vocab=1000, max_seq=64)
+
+
+@pytest.fixture(scope="module")
+def small():
+    host = synth.synth_model(SMALL, seed=11)
+    dev = synth.DeviceModel(host)
+    yield host, dev
+    dev.close()
+
+
+def embedding(host, token):
+    qt, raw = host.tensors["token_embd.weight"]
+    rb = O.bytes_per_row(qt, host.cfg.dim)
+    return O.dequantize(qt, raw[token * rb:(token + 1) * rb], host.cfg.dim)
+
+
+def test_forward_transformer_matches_oracle(small):
+    host, dev = small
+    c = host.cfg
+    ref = O.RefModel(c, host.tensors)
+    G.AllocBuffers(c.dim, c.hidden, c.kv_dim, c.vocab, c.n_layers, c.max_seq)
+    scale = float(np.float32(1.0 / O.math_sqrt(float(c.head_dim))))
+    for pos, tok in enumerate([3, 141, 59, 26, 535, 897, 932, 384]):
+        logits, nxt = G.ForwardTransformer(
+            embedding(host, tok), dev.table, dev.bufs["output_norm.weight"], dev.bufs["output.weight"],
+            dev.types["output.weight"], num_layers=c.n_layers, dim=c.dim, hidden_dim=c.hidden, kv_dim=c.kv_dim,
+            vocab_size=c.vocab, num_heads=c.n_heads, num_kv_heads=c.n_kv_heads, head_dim=c.head_dim, pos=pos,
+            slot=pos % c.max_seq, max_seq=c.max_seq, active_context=min(pos + 1, c.max_seq), norm_eps=c.eps,
+            rope_theta=c.rope_theta, attn_scale=scale)
+        want = ref.forward(tok, pos)
+        assert_parity(logits, want, what=f"logits at pos {pos}")
+        assert nxt == int(np.argmax(logits))
+
+
+def check_greedy(dev_model, ref, prompt, n_gen):
+    ids, logits, _ms = dev_model.generate(prompt, n_gen, want_logits=True)
+    want, margins, want_logits = ref.greedy(prompt, n_gen)
+    if not np.array_equal(ids, want):
+        i = int(np.argmax(ids != want))
+        pytest.fail(f"greedy ids differ first at step {i}: gpu {ids[i]} vs oracle {want[i]} "
+                    f"(oracle top-2 margin there {margins[i]:.3e}, smallest {margins.min():.3e})")
+    assert_parity(logits, want_logits, what="last-step logits")
+    return ids
+
+
+def test_generate_matches_oracle_greedy(small):
+    host, dev = small
+    ref = O.RefModel(host.cfg, host.tensors)
+    model = dev.model()
+    try:
+        prompt = np.random.default_rng(12).integers(0, host.cfg.vocab, 16)
+        ids = check_greedy(model, ref, prompt, 24)
+        # reset + replay gives the same ids (the captured step is reused)
+        model.reset()
+        again, _l, _ms = model.generate(prompt, 24)
+        assert np.array_equal(again, ids)
+    finally:
+        model.close()
+
+
+def test_generate_wraps_the_kv_cache():
+    """Positions past max_seq reuse slots pos % max_seq (engine_test.go:194)."""
+    cfg = synth.LlamaConfig(n_layers=2, dim=256, hidden=512, n_heads=4, n_kv_heads=4, vocab=512, max_seq=8)
+    host = synth.synth_model(cfg, seed=13)
+    dev = synth.DeviceModel(host)
+    model = dev.model()
+    try:
+        check_greedy(model, O.RefModel(cfg, host.tensors), [5, 77, 300, 12, 9], 12)
+    finally:
+        model.close()
+        dev.close()
+
+
+def test_synthetic_engine_model():
+    """engine_test.go:159-192's model (all-0.1 F32 weights, dim 16, vocab 6)."""
+    cfg = synth.LlamaConfig(n_layers=1, dim=16, hidden=32, n_heads=2, n_kv_heads=2, vocab=6, max_seq=32,
+                            rope_theta=500000.0)
+    T = {}
+    for name, (r, c) in [("token_embd.weight", (cfg.vocab, cfg.dim)), ("output.weight", (cfg.vocab, cfg.dim))]:
+        T[name] = (G.TYPE_F32, np.full((r, c), 0.1, np.float32))
+    for name, (r, c) in synth.layer_shapes(cfg).items():
+        T[f"blk.0.{name}.weight"] = (G.TYPE_F32, np.full((r, c), 0.1, np.float32))
+    for name in ("blk.0.attn_norm.weight", "blk.0.ffn_norm.weight", "output_norm.weight"):
+        T[name] = (G.TYPE_F32, np.full(cfg.dim, 0.1, np.float32))
+    dev = synth.DeviceModel(synth.HostModel(cfg, T))
+    model = dev.model()
+    try:
+        ids = check_greedy(model, O.RefModel(cfg, T, nthreads=1), [1, 3, 4], 3)
+        assert list(ids) == [0, 0, 0]
+    finally:
+        model.close()
+        dev.close()
+
+
+def test_model_rejects_bad_arguments(small):
+    _host, dev = small
+    model = dev.model(max_pos=40)
+    try:
+        with pytest.raises(G.GoInferCudaError) as e:
+            model.generate([1, 2, 3], 40)  # positions 0..41 > max_pos 40
+        assert e.value.code == G.ERR_SHAPE
+        with pytest.raises(G.GoInferCudaError):
+            model.generate([SMALL.vocab], 1)  # token id out of range
+    finally:
+        model.close()
