@@ -130,3 +130,34 @@ def test_model_rejects_bad_arguments(small):
             model.generate([SMALL.vocab], 1)  # token id out of range
     finally:
         model.close()
+
+
+def test_config4_greedy_matches_oracle_golden():
+    """Config 4 (Llama-2-7B shape, Q4_K / Q6_K lm_head): 128-token prompt then
+    64 greedy steps, ids identical to the CPU oracle's (tests/golden/
+    make_decode_golden.py; smallest oracle top-2 margin stored with them)."""
+    import os
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), "golden"))
+    from make_decode_golden import model_digest
+    gold = np.load(os.path.join(os.path.dirname(__file__), "golden", "decode_llama7b.npz"))
+    host = synth.synth_model(synth.LLAMA2_7B, seed=int(gold["seed"]))
+    assert model_digest(host) == str(gold["digest"]), "the synthetic-weight generator changed"
+    dev = synth.DeviceModel(host)
+    del host
+    model = dev.model()
+    try:
+        ids, logits, _ms = model.generate(gold["prompt"], 64, want_logits=True)
+        if not np.array_equal(ids, gold["ids"]):
+            i = int(np.argmax(ids != gold["ids"]))
+            pytest.fail(f"config-4 greedy ids differ first at step {i}: gpu {ids[i]} vs oracle {gold['ids'][i]} "
+                        f"(oracle top-2 margin {gold['margins'][i]:.3e})")
+        # After 32 layers and 191 steps the float32 summation-order noise of
+        # the residual stream is larger than one GEMV's: the logits are held
+        # to a normwise bar, max |gpu - oracle| <= 2e-3 * rms(oracle logits).
+        ref = gold["last_logits"].astype(np.float64)
+        dev_err = np.abs(logits - ref).max() / np.sqrt(np.mean(ref * ref))
+        assert dev_err <= 2e-3, f"config-4 last logits: max |diff| / rms = {dev_err:.3e}"
+    finally:
+        model.close()
+        dev.close()
