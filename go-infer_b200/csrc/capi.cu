@@ -25,7 +25,8 @@
 namespace gi {
 int quantize_host(int qtype, const float* src, int64_t rows, int64_t cols, uint8_t* dst,
                   int threads);
-int quantize_seeded(int qtype, uint64_t seed, float stddev, int64_t rows, int64_t cols, uint8_t* dst, int threads);
+int quantize_seeded(int qtype, uint64_t seed, float stddev, int64_t row0, int64_t rows, int64_t col0, int64_t cols,
+                    uint8_t* dst, int threads);
 }
 
 namespace {
@@ -266,6 +267,23 @@ struct Mirror {
   float eps = 0.f, theta = 0.f, scale = 0.f;
 };
 Mirror g_mirror;
+
+// Tensor-parallel exchange region of this process and its peers' mappings.
+struct TpCtx {
+  int world = 0, rank = -1, max_dim = 0;
+  bool connected = false;
+  uint8_t* region = nullptr;
+  void* peer[gi::kTpMaxWorld] = {};
+  gi::TpDev dev;
+};
+TpCtx g_tp;
+
+void tp_release() {
+  for (int r = 0; r < gi::kTpMaxWorld; ++r)
+    if (g_tp.peer[r]) cudaIpcCloseMemHandle(g_tp.peer[r]);
+  if (g_tp.region) cudaFree(g_tp.region);
+  g_tp = TpCtx();
+}
 
 struct ModelHandle {
   gi::DecodeModel m;
@@ -659,8 +677,17 @@ gi_cuda_model_t gi_cuda_model_create(const gi_cuda_model_desc_t* d) {
   c.eps = d->norm_eps;
   c.rope_theta = d->rope_theta;
   c.attn_scale = gi::attn_scale_for((int)d->head_dim);
+  c.tp_world = d->tp_world > 1 ? (int)d->tp_world : 1;
+  c.tp_rank = c.tp_world > 1 ? (int)d->tp_rank : 0;
+  c.vocab_offset = c.tp_world > 1 ? (int)d->vocab_offset : 0;
+  if (c.tp_world > 1 && (!g_tp.connected || g_tp.world != c.tp_world || g_tp.rank != c.tp_rank ||
+                         g_tp.max_dim < (int)d->dim)) {
+    fail(-4, "gi_cuda_model_create: tensor parallelism not connected for this rank / world / dim");
+    return nullptr;
+  }
   ModelHandle* h = new ModelHandle();
-  const int rc = h->m.init(c, refs.data(), embd_ref, onorm, out_ref, g.sm_count, g.scratch.error);
+  const int rc = h->m.init(c, refs.data(), embd_ref, onorm, out_ref, g.sm_count, g.scratch.error,
+                           c.tp_world > 1 ? &g_tp.dev : nullptr);
   if (rc) {
     delete h;
     fail(rc, "gi_cuda_model_create: device buffers");
@@ -702,8 +729,9 @@ int gi_cuda_model_generate(gi_cuda_model_t model, const int32_t* tokens, uint32_
   const uint64_t steps = (uint64_t)n_tokens + n_gen - 1;
   if ((uint64_t)start_pos + steps > (uint64_t)c.max_pos) return fail(-4, "positions beyond the RoPE table");
   if (steps > (uint64_t)m.max_out()) return fail(-4, "too many steps for one call");
+  const int64_t full_vocab = (int64_t)c.vocab * c.tp_world;  // the token table is replicated
   for (uint32_t i = 0; i < n_tokens; ++i)
-    if (tokens[i] < 0 || tokens[i] >= c.vocab) return fail(-4, "token id out of range");
+    if (tokens[i] < 0 || tokens[i] >= full_vocab) return fail(-4, "token id out of range");
   if (!m.graph) {
     cudaGraph_t graph = nullptr;
     GI_CUDA_TRY(cudaStreamBeginCapture(g.stream, cudaStreamCaptureModeThreadLocal), "begin capture");
@@ -761,6 +789,68 @@ int gi_cuda_model_generate(gi_cuda_model_t model, const int32_t* tokens, uint32_
   return check_device_error();
 }
 
+int gi_cuda_tp_prepare(int world, uint32_t max_dim, void* handle_out) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (world < 1 || world > gi::kTpMaxWorld || max_dim < 1 || !handle_out) return fail(-4, "bad tensor-parallel size");
+  tp_release();
+  const gi::TpLayout L = gi::tp_layout(world, (int)max_dim);
+  GI_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&g_tp.region), L.total), "cudaMalloc exchange region");
+  GI_CUDA_TRY(cudaMemset(g_tp.region, 0, L.total), "clear exchange region");
+  // flags start at 0xffffffff: no sequence number matches them
+  GI_CUDA_TRY(cudaMemset(g_tp.region + L.flags, 0xFF, sizeof(uint32_t) * 2 * world), "init flags");
+  GI_CUDA_TRY(cudaMemset(g_tp.region + L.aflag, 0xFF, sizeof(uint32_t) * 2 * world), "init flags");
+  GI_CUDA_TRY(cudaDeviceSynchronize(), "exchange region");
+  cudaIpcMemHandle_t hnd;
+  GI_CUDA_TRY(cudaIpcGetMemHandle(&hnd, g_tp.region), "cudaIpcGetMemHandle");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  std::memcpy(handle_out, &hnd, sizeof hnd);
+  g_tp.world = world;
+  g_tp.max_dim = (int)max_dim;
+  return 0;
+}
+
+int gi_cuda_tp_connect(int rank, int world, const void* handles) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!g_tp.region || world != g_tp.world || rank < 0 || rank >= world || !handles)
+    return fail(-4, "gi_cuda_tp_connect: call gi_cuda_tp_prepare with the same world first");
+  const gi::TpLayout L = gi::tp_layout(world, g_tp.max_dim);
+  gi::TpDev d;
+  d.rank = rank;
+  d.world = world;
+  d.max_dim = g_tp.max_dim;
+  for (int r = 0; r < world; ++r) {
+    uint8_t* base = g_tp.region;
+    if (r != rank) {
+      cudaIpcMemHandle_t hnd;
+      std::memcpy(&hnd, static_cast<const uint8_t*>(handles) + 64 * r, 64);
+      void* p = nullptr;
+      GI_CUDA_TRY(cudaIpcOpenMemHandle(&p, hnd, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+      g_tp.peer[r] = p;
+      base = static_cast<uint8_t*>(p);
+    }
+    d.recv[r] = reinterpret_cast<float*>(base + L.recv);
+    d.flags[r] = reinterpret_cast<uint32_t*>(base + L.flags);
+    d.argv[r] = reinterpret_cast<float2*>(base + L.argv);
+    d.aflag[r] = reinterpret_cast<uint32_t*>(base + L.aflag);
+  }
+  d.seq = reinterpret_cast<uint32_t*>(g_tp.region + L.seq);
+  d.done = reinterpret_cast<unsigned*>(g_tp.region + L.done);
+  g_tp.dev = d;
+  g_tp.rank = rank;
+  g_tp.connected = true;
+  return 0;
+}
+
+int gi_cuda_tp_close(void) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  cudaDeviceSynchronize();
+  tp_release();
+  return 0;
+}
+
 int gi_cuda_gemv_multi_dev(int quant_type, int nmat, float* const* y, const float* x, const void* const* w,
                            const size_t* w_bytes, const uint32_t* rows, uint32_t cols, void* stream) {
   std::lock_guard<std::mutex> lk(g.mu);
@@ -788,11 +878,12 @@ const char* gi_cuda_last_error(void) { return t_err.c_str(); }
 
 int64_t gi_quant_row_bytes(int quant_type, int64_t cols) { return gi::row_bytes(quant_type, cols); }
 
-int gi_quantize_seeded(int quant_type, uint64_t seed, float stddev, int64_t rows, int64_t cols, void* dst,
-                       int threads) {
+int gi_quantize_seeded(int quant_type, uint64_t seed, float stddev, int64_t row0, int64_t rows, int64_t col0,
+                       int64_t cols, void* dst, int threads) {
   if (!dst) return fail(-4, "null pointer");
   if (threads <= 0) threads = (int)std::thread::hardware_concurrency();
-  const int rc = gi::quantize_seeded(quant_type, seed, stddev, rows, cols, static_cast<uint8_t*>(dst), threads);
+  const int rc = gi::quantize_seeded(quant_type, seed, stddev, row0, rows, col0, cols, static_cast<uint8_t*>(dst),
+                                     threads);
   if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : "unsupported shape");
   return 0;
 }

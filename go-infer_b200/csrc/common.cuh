@@ -153,7 +153,7 @@ GI_DEVINL uint64_t l2_evict_first_policy() {
   return pol;
 }
 
-// Global -> shared bulk copy (no multicast); completes `bytes` of tx on `bar`.
+// Global -> shared bulk copy into this CTA only; completes `bytes` of tx on `bar`.
 // dst, src 16-byte aligned, bytes a multiple of 16.
 GI_DEVINL void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t pol) {
   asm volatile(

@@ -115,7 +115,7 @@ GI_DEVINL void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// Contiguous global -> shared bulk copy (no multicast); completes `bytes`
+// Contiguous global -> shared bulk copy into this CTA only; completes `bytes`
 // of tx on `bar`.  Both addresses 16-byte aligned, bytes a multiple of 16.
 GI_DEVINL void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),

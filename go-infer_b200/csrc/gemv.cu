@@ -80,6 +80,7 @@ struct Params {
   const float* x2;  // RMSNorm weight (xmode kXNorm)
   float eps;
   int xmode, ymode;
+  TpDev tp;  // kYPush
   long long rowb;
   int nku, ntiles, ctas;
   int x_off, slot_off;  // dynamic smem byte offsets (rings at 0)
@@ -402,8 +403,31 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
           const float silu = __fdiv_rn(sum, __fadd_rn(1.0f, (float)exp(-(double)sum)));
           p.y[0][row] = __fmul_rn(silu, up);
         }
+      } else if (p.ymode == kYPush) {
+        if (row < p.rows[m]) {  // this rank's partial into slot `rank` of every rank's region
+          const uint32_t set = *p.tp.seq & 1u;
+          const size_t off = ((size_t)set * p.tp.world + p.tp.rank) * p.tp.max_dim + row;
+          for (int r = 0; r < p.tp.world; ++r) p.tp.recv[r][off] = sum;
+        }
       } else if (row < p.rows[m]) {
         p.y[m][row] = p.ymode == kYAdd ? __fadd_rn(p.y[m][row], sum) : sum;  // residual: y += W x
+      }
+    }
+  }
+  if (p.ymode == kYPush) {
+    // The last CTA to finish publishes the push: flag[rank] = seq on every
+    // rank, after every CTA's stores are visible system-wide.
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned d = atomicAdd(p.tp.done, 1u);
+      if (d == gridDim.x - 1) {
+        *p.tp.done = 0u;
+        __threadfence_system();
+        const uint32_t seq = *p.tp.seq;
+        const size_t f = (size_t)(seq & 1u) * p.tp.world + p.tp.rank;
+        for (int r = 0; r < p.tp.world; ++r)
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.tp.flags[r] + f), "r"(seq) : "memory");
       }
     }
   }
@@ -454,6 +478,10 @@ int launch(int nmat, float* const* y, const float* x, const void* const* w, cons
   p.eps = f.eps;
   p.xmode = f.xmode;
   p.ymode = f.ymode;
+  if (f.ymode == kYPush) {
+    if (!f.tp || f.tp->world < 1 || rows[0] > f.tp->max_dim || nmat != 1) return -4;
+    p.tp = *f.tp;
+  }
   p.rowb = row_bytes(kTypeQ4_K, cols);
   p.nku = (int)(cols / 256);
   p.ntiles = o.ntiles;

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "tp.cuh"
+
 namespace gi {
 
 // GGML type ids (pkg/gguf/types.go:25-52 of go-infer).
@@ -24,12 +26,15 @@ struct GemvScratch {
 
 // Fusions of the Q4_K GEMV used by the decode step (internal).
 enum : int { kXPlain = 0, kXNorm = 1 };              // staged x, or RMSNorm(x) * x2 (weight)
-enum : int { kYStore = 0, kYAdd = 1, kYSwiGLU = 2 };  // y = Wx, y += Wx, or silu(W0 x) * (W1 x)
+// y = Wx, y += Wx, silu(W0 x) * (W1 x), or (kYPush) Wx pushed as this
+// rank's partial into every rank's tensor-parallel exchange region.
+enum : int { kYStore = 0, kYAdd = 1, kYSwiGLU = 2, kYPush = 3 };
 struct GemvFuse {
   int xmode = kXPlain;
   const float* x2 = nullptr;
   float eps = 0.f;
   int ymode = kYStore;
+  const TpDev* tp = nullptr;  // kYPush
 };
 
 struct GemvLaunch {

@@ -278,10 +278,83 @@ __global__ void swiglu_kernel(float* __restrict__ gate, const float* __restrict_
   gate[i] = __fmul_rn(silu, up[i]);
 }
 
+// ---- tensor-parallel exchange (TPCoordinator.AllReduce,
+// pkg/distributed/tensor_parallel.go:33-108) --------------------------------
+GI_DEVINL uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+GI_DEVINL uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait (at most 2 s) for a flag to read `want`; false when it never did, or
+// at once when an earlier wait has already failed (*error set), so that a
+// missing peer costs one timeout, not one per exchange.
+GI_DEVINL bool wait_flag(const uint32_t* f, uint32_t want, const int* error) {
+  if (ld_acquire_sys(f) == want) return true;
+  const uint64_t t0 = now_ns();
+  while (ld_acquire_sys(f) != want) {
+    if (*(volatile const int*)error) return false;
+    if (now_ns() - t0 > 2000000000ull) return false;
+  }
+  return true;
+}
+
+// Push this rank's partial p[n] into slot `rank` of every rank's region and
+// publish it (used when the projection is not the Q4_K GEMV, which pushes
+// from its own epilogue).
+__global__ void __launch_bounds__(1024) tp_push_kernel(const float* __restrict__ p, int n, TpDev tp) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const uint32_t seq = *tp.seq;
+  const size_t base = ((size_t)(seq & 1u) * tp.world + tp.rank) * tp.max_dim;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = p[i];
+    for (int r = 0; r < tp.world; ++r) tp.recv[r][base + i] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const size_t f = (size_t)(seq & 1u) * tp.world + tp.rank;
+    for (int r = 0; r < tp.world; ++r)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(tp.flags[r] + f), "r"(seq) : "memory");
+  }
+}
+
+// x += sum of the ranks' partials, in rank order (the same x on every rank),
+// once every rank's push of this exchange has landed; then seq += 1.
+__global__ void __launch_bounds__(1024) tp_reduce_kernel(float* __restrict__ x, int n, TpDev tp, int* error) {
+  __shared__ int ok;
+  griddep_wait();
+  griddep_launch_dependents();
+  const uint32_t seq = *tp.seq;
+  const uint32_t set = seq & 1u;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (threadIdx.x < tp.world && !wait_flag(tp.flags[tp.rank] + (size_t)set * tp.world + threadIdx.x, seq, error)) {
+    ok = 0;
+    atomicExch(error, 1);
+  }
+  __syncthreads();
+  const float* rv = tp.recv[tp.rank] + (size_t)set * tp.world * tp.max_dim;
+  if (ok)
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      float s = __ldcg(rv + i);
+      for (int r = 1; r < tp.world; ++r) s = __fadd_rn(s, __ldcg(rv + (size_t)r * tp.max_dim + i));
+      x[i] = __fadd_rn(x[i], s);
+    }
+  __syncthreads();
+  if (threadIdx.x == 0) *tp.seq = seq + 1;
+}
+
 // ---- greedy pick (forward.go:397-404: the first maximum wins) and the
 // position advance of the generation loop ------------------------------------
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int n, StepState* st,
-                                                      uint32_t* __restrict__ out, int max_out, int max_seq) {
+                                                      uint32_t* __restrict__ out, int max_out, int max_seq,
+                                                      int vocab_offset, TpDev tp, int* error) {
   __shared__ float bv[32];
   __shared__ int bi[32];
   griddep_wait();
@@ -325,6 +398,31 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     }
     if (threadIdx.x == 0) {
       if (idx == 0x7fffffff) idx = 0;
+      idx += vocab_offset;
+      if (tp.world > 1) {  // compare the vocabulary slices' maxima across ranks
+        const uint32_t seq = *tp.seq;
+        const size_t f = (size_t)(seq & 1u) * tp.world;
+        for (int r = 0; r < tp.world; ++r) tp.argv[r][f + tp.rank] = make_float2(v, __int_as_float(idx));
+        __threadfence_system();
+        for (int r = 0; r < tp.world; ++r)
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(tp.aflag[r] + f + tp.rank), "r"(seq) : "memory");
+        float bv2 = -INFINITY;
+        int bi2 = 0x7fffffff;
+        for (int r = 0; r < tp.world; ++r) {
+          if (!wait_flag(tp.aflag[tp.rank] + f + r, seq, error)) {
+            atomicExch(error, 1);
+            continue;
+          }
+          const float2 e = __ldcg(tp.argv[tp.rank] + f + r);
+          const int ei = __float_as_int(e.y);
+          if (bi2 == 0x7fffffff || e.x > bv2 || (e.x == bv2 && ei < bi2)) {
+            bv2 = e.x;
+            bi2 = ei;
+          }
+        }
+        idx = bi2 == 0x7fffffff ? 0 : bi2;
+        *tp.seq = seq + 1;
+      }
       if ((int)st->n_out < max_out) out[st->n_out] = (uint32_t)idx;
       st->n_out += 1;
       st->token = (uint32_t)idx;
@@ -369,8 +467,14 @@ DecodeModel::~DecodeModel() {
 }
 
 int DecodeModel::init(const ModelCfg& cfg, const LayerRef* layers, const MatRef& tok_embd, const float* out_norm,
-                      const MatRef& out, int sm_count, int* error_word) {
+                      const MatRef& out, int sm_count, int* error_word, const TpDev* tp) {
   cfg_ = cfg;
+  if (cfg.tp_world > 1) {
+    if (!tp || tp->world != cfg.tp_world || tp->rank != cfg.tp_rank || tp->max_dim < cfg.dim) return -4;
+    tp_ = *tp;
+  } else {
+    tp_ = TpDev();
+  }
   if (cfg.n_layers < 1 || cfg.dim < 1 || cfg.n_heads < 1 || cfg.n_kv_heads < 1 || cfg.head_dim < 2 ||
       cfg.head_dim % 2 || cfg.head_dim > 1024 || cfg.n_heads % cfg.n_kv_heads || cfg.max_seq < 1 ||
       cfg.max_pos < 1 || cfg.vocab < 1 || cfg.hidden < 1)
@@ -445,6 +549,35 @@ void DecodeModel::reset_cache(cudaStream_t s) {
   cudaMemsetAsync(vcache_, 0, sizeof(float) * kv, s);
 }
 
+// x += (sum over ranks of) W_shard * in: this rank's partial goes to every
+// rank's exchange region (from the Q4_K GEMV's epilogue, or through
+// tp_push_kernel), then the rank-ordered sum is added to x.
+int DecodeModel::project_partial(const MatRef& W, const float* in, int cols, cudaStream_t s, bool pdl) {
+  GemvLaunch L;
+  L.sm_count = sm_count_;
+  L.pdl = pdl;
+  int rc = 0;
+  if (W.qtype == kTypeQ4_K) {
+    float* ys[1] = {proj_};
+    const void* ws[1] = {W.w};
+    const size_t wb[1] = {W.bytes};
+    const int64_t rows[1] = {cfg_.dim};
+    GemvFuse f;
+    f.ymode = kYPush;
+    f.tp = &tp_;
+    rc = gemv_q4k_fused(1, ys, in, ws, wb, rows, cols, f, L, s);
+  } else {
+    rc = gemv_launch(W.qtype, proj_, in, W.w, W.bytes, cfg_.dim, cols, scratch_, L, s);
+    if (!rc && launch(pdl, dim3(1), dim3(1024), 0, s, tp_push_kernel, (const float*)proj_, cfg_.dim, tp_) !=
+                   cudaSuccess)
+      rc = -5;
+  }
+  if (rc) return rc;
+  return launch(pdl, dim3(1), dim3(1024), 0, s, tp_reduce_kernel, x_, cfg_.dim, tp_, scratch_.error) == cudaSuccess
+             ? 0
+             : -5;
+}
+
 int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
   const ModelCfg& c = cfg_;
   const int hd = c.head_dim, q_dim = c.n_heads * hd, kv_dim = c.n_kv_heads * hd;
@@ -503,8 +636,12 @@ int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
     if (e != cudaSuccess) return -5;
     e = launch(pdl, dim3(c.n_heads), dim3(hd), 0, s, attn_combine_kernel, (const float*)part_, att_, hd, att_splits_);
     if (e != cudaSuccess) return -5;
-    // Output projection + residual (x += Wo att).
-    if (Ly.wo.qtype == kTypeQ4_K) {
+    // Output projection + residual (x += Wo att); across ranks the partial
+    // products are summed first.
+    if (c.tp_world > 1) {
+      rc = project_partial(Ly.wo, att_, q_dim, s, pdl);
+      if (rc) return rc;
+    } else if (Ly.wo.qtype == kTypeQ4_K) {
       float* ys[1] = {x_};
       const void* ws[1] = {Ly.wo.w};
       const size_t wb[1] = {Ly.wo.bytes};
@@ -542,7 +679,10 @@ int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
     }
     if (rc) return rc;
     // Down projection + residual (x += Wdown h).
-    if (Ly.down.qtype == kTypeQ4_K) {
+    if (c.tp_world > 1) {
+      rc = project_partial(Ly.down, gate_, c.hidden, s, pdl);
+      if (rc) return rc;
+    } else if (Ly.down.qtype == kTypeQ4_K) {
       float* ys[1] = {x_};
       const void* ws[1] = {Ly.down.w};
       const size_t wb[1] = {Ly.down.bytes};
@@ -563,7 +703,7 @@ int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
   rc = gemv_launch(out_.qtype, logits_, xb_, out_.w, out_.bytes, c.vocab, c.dim, scratch_, L, s);
   if (rc) return rc;
   e = launch(pdl, dim3(1), dim3(1024), 0, s, argmax_kernel, (const float*)logits_, c.vocab, st_, tokens_out_,
-             max_out_, c.max_seq);
+             max_out_, c.max_seq, c.vocab_offset, tp_, scratch_.error);
   return e == cudaSuccess ? 0 : -5;
 }
 

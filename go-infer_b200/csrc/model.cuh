@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include "gemv.cuh"
+#include "tp.cuh"
 
 namespace gi {
 
@@ -33,6 +34,11 @@ struct ModelCfg {
   int max_seq = 0;   // KV-cache slots (rolling, slot = pos % max_seq)
   int max_pos = 0;   // positions covered by the RoPE table
   float eps = 1e-5f, rope_theta = 10000.f, attn_scale = 0.f;
+  // Tensor parallelism (Megatron): n_heads, n_kv_heads, hidden and vocab are
+  // this rank's shares; wq/wk/wv/gate/up/output hold its rows, wo/down its
+  // columns; the output and down projections are summed across ranks, the
+  // argmax compared across the vocabulary slices (vocab_offset = first row).
+  int tp_world = 1, tp_rank = 0, vocab_offset = 0;
 };
 
 // Position state the captured step reads and advances on the device.
@@ -50,7 +56,7 @@ class DecodeModel {
   ~DecodeModel();
   // Validates shapes, allocates activations, KV cache and the RoPE table.
   int init(const ModelCfg& cfg, const LayerRef* layers, const MatRef& tok_embd, const float* out_norm,
-           const MatRef& out, int sm_count, int* error_word);
+           const MatRef& out, int sm_count, int* error_word, const TpDev* tp = nullptr);
   // Enqueue one decode step on `s`: embedding of st.token (if `embed`),
   // all layers, final norm, logits and the greedy argmax, which writes the
   // next token into st and tokens_out[st.n_out] and advances the position.
@@ -58,6 +64,7 @@ class DecodeModel {
   void reset_cache(cudaStream_t s);
   // Re-point the weights (same shapes) without touching the KV cache.
   void bind(const LayerRef* layers, const MatRef& tok_embd, const float* out_norm, const MatRef& out);
+  int project_partial(const MatRef& W, const float* in, int cols, cudaStream_t s, bool pdl);
 
   const ModelCfg& cfg() const { return cfg_; }
   float* x() const { return x_; }
@@ -78,6 +85,7 @@ class DecodeModel {
   MatRef tok_embd_, out_;
   const float* out_norm_ = nullptr;
   GemvScratch scratch_;
+  TpDev tp_;
   int sm_count_ = 148;
   float *x_ = nullptr, *xb_ = nullptr, *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *att_ = nullptr;
   float *proj_ = nullptr, *gate_ = nullptr, *up_ = nullptr, *logits_ = nullptr;

@@ -8,6 +8,7 @@
 // formats that DequantizeQ4_K / DequantizeQ6_K decode
 // (pkg/quant/quant.go:215-291).  Every step is a single IEEE float32
 // operation, so the result is deterministic across compilers.
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -241,8 +242,10 @@ int quantize_host(int qtype, const float* src, int64_t rows, int64_t cols, uint8
 }
 
 // Seeded N(0, std) weights, quantised row by row without holding the fp32
-// matrix: row r draws from a splitmix64 stream keyed by (seed, r) through the
-// Box-Muller transform (in double), so the bytes do not depend on the
+// matrix.  Every 256-column block of row r draws from its own splitmix64
+// stream keyed by (seed, r, block) through the Box-Muller transform (in
+// double), so any rows and any 256-aligned column range can be generated on
+// their own (tensor-parallel shards) and the bytes do not depend on the
 // thread count.  F32 writes the float32 values themselves.
 namespace {
 inline uint64_t splitmix64(uint64_t& s) {
@@ -251,8 +254,9 @@ inline uint64_t splitmix64(uint64_t& s) {
   z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
   return z ^ (z >> 31);
 }
-void normal_row(uint64_t seed, int64_t row, float stddev, float* out, int64_t n) {
-  uint64_t s = seed * 0xD1B54A32D192ED03ull ^ (uint64_t)row * 0x8CB92BA72F3D8DD7ull;
+void normal_block(uint64_t seed, int64_t row, int64_t blk, float stddev, float* out, int64_t n) {
+  uint64_t s = seed * 0xD1B54A32D192ED03ull ^ (uint64_t)row * 0x8CB92BA72F3D8DD7ull ^
+               (uint64_t)blk * 0xA0761D6478BD642Full;
   for (int64_t i = 0; i < n; i += 2) {
     const double u1 = ((splitmix64(s) >> 11) + 1) * 0x1.0p-53;  // (0, 1]
     const double u2 = (splitmix64(s) >> 11) * 0x1.0p-53;        // [0, 1)
@@ -263,16 +267,20 @@ void normal_row(uint64_t seed, int64_t row, float stddev, float* out, int64_t n)
 }
 }  // namespace
 
-int quantize_seeded(int qtype, uint64_t seed, float stddev, int64_t rows, int64_t cols, uint8_t* dst, int threads) {
+// Rows [row0, row0 + rows) and columns [col0, col0 + cols) of the seeded
+// matrix (col0 a multiple of 256).
+int quantize_seeded(int qtype, uint64_t seed, float stddev, int64_t row0, int64_t rows, int64_t col0, int64_t cols,
+                    uint8_t* dst, int threads) {
   const bool f32 = qtype == kTypeF32;
   const int64_t block = qtype == kTypeQ8_0 ? 32 : (f32 ? 1 : 256);
   if (!f32 && qtype != kTypeQ8_0 && qtype != kTypeQ4_K && qtype != kTypeQ6_K) return -2;
-  if (rows < 1 || cols < block || cols % block) return -4;
+  if (rows < 1 || row0 < 0 || col0 < 0 || col0 % 256 || cols < block || cols % block) return -4;
   const int64_t rb = f32 ? cols * 4 : row_bytes(qtype, cols);
   auto work = [&](int64_t r0, int64_t r1) {
     std::vector<float> buf((size_t)cols);
     for (int64_t r = r0; r < r1; ++r) {
-      normal_row(seed, r, stddev, buf.data(), cols);
+      for (int64_t c = 0; c < cols; c += 256)
+        normal_block(seed, row0 + r, (col0 + c) / 256, stddev, buf.data() + c, std::min<int64_t>(256, cols - c));
       uint8_t* o = dst + r * rb;
       if (f32) {
         std::memcpy(o, buf.data(), (size_t)cols * 4);

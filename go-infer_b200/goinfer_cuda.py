@@ -50,7 +50,7 @@ EXPORTS = (
     "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl",
     "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize", "gi_quantize_seeded",
     "gi_cuda_alloc_buffers", "gi_cuda_forward_transformer", "gi_cuda_model_create", "gi_cuda_model_destroy",
-    "gi_cuda_model_reset", "gi_cuda_model_generate",
+    "gi_cuda_model_reset", "gi_cuda_model_generate", "gi_cuda_tp_prepare", "gi_cuda_tp_connect", "gi_cuda_tp_close",
 )
 
 
@@ -76,7 +76,8 @@ class ModelDesc(ctypes.Structure):
                 ("layers", ctypes.POINTER(LayerWeights)),
                 ("token_embd", ctypes.c_void_p), ("token_embd_type", ctypes.c_int),
                 ("output_norm", ctypes.c_void_p),
-                ("output_weight", ctypes.c_void_p), ("output_weight_type", ctypes.c_int)]
+                ("output_weight", ctypes.c_void_p), ("output_weight_type", ctypes.c_int),
+                ("tp_world", ctypes.c_uint32), ("tp_rank", ctypes.c_uint32), ("vocab_offset", ctypes.c_uint32)]
 
 
 class GoInferCudaError(RuntimeError):
@@ -125,12 +126,16 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "gi_cuda_last_error": ([], ctypes.c_char_p),
         "gi_quant_row_bytes": ([i32, ctypes.c_int64], ctypes.c_int64),
         "gi_quantize": ([i32, f32p, ctypes.c_int64, ctypes.c_int64, vp, i32], i32),
-        "gi_quantize_seeded": ([i32, ctypes.c_uint64, ctypes.c_float, ctypes.c_int64, ctypes.c_int64, vp, i32], i32),
+        "gi_quantize_seeded": ([i32, ctypes.c_uint64, ctypes.c_float, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                ctypes.c_int64, vp, i32], i32),
         "gi_cuda_alloc_buffers": ([u32, u32, u32, u32, u32, u32], i32),
         "gi_cuda_forward_transformer": ([f32p, f32p, ctypes.POINTER(u32), ctypes.POINTER(LayerWeights), vp, vp, i32,
                                          u32, u32, u32, u32, u32, u32, u32, u32, u32, u32, u32, u32,
                                          ctypes.c_float, ctypes.c_float, ctypes.c_float], i32),
         "gi_cuda_model_create": ([ctypes.POINTER(ModelDesc)], vp),
+        "gi_cuda_tp_prepare": ([i32, u32, vp], i32),
+        "gi_cuda_tp_connect": ([i32, i32, vp], i32),
+        "gi_cuda_tp_close": ([], i32),
         "gi_cuda_model_destroy": ([vp], None),
         "gi_cuda_model_reset": ([vp], i32),
         "gi_cuda_model_generate": ([vp, ctypes.POINTER(ctypes.c_int32), u32, u32, u32, ctypes.POINTER(u32), f32p,
@@ -350,13 +355,15 @@ class Weights:
 
 # ---- whole-model decode ----------------------------------------------------
 
-def quantize_seeded(quant_type: int, seed: int, std: float, rows: int, cols: int, threads: int = 0) -> np.ndarray:
-    """Seeded N(0, std) rows x cols, quantised (F32: the float32 values)."""
+def quantize_seeded(quant_type: int, seed: int, std: float, rows: int, cols: int, threads: int = 0,
+                    row0: int = 0, col0: int = 0) -> np.ndarray:
+    """Rows [row0, row0+rows) x cols [col0, col0+cols) of a seeded N(0, std)
+    matrix, quantised (F32: the float32 values)."""
     rb = cols * 4 if quant_type == TYPE_F32 else row_bytes(quant_type, cols)
     if rb < 0:
         raise GoInferCudaError("gi_quantize_seeded", ERR_UNSUPPORTED_TYPE)
     out = np.empty(max(rows * rb, 1), np.uint8)
-    _err("gi_quantize_seeded", load_library().gi_quantize_seeded(quant_type, seed, std, rows, cols,
+    _err("gi_quantize_seeded", load_library().gi_quantize_seeded(quant_type, seed, std, row0, rows, col0, cols,
                                                                    out.ctypes.data, threads))
     return out
 
@@ -437,3 +444,24 @@ class Model:
             self.close()
         except Exception:
             pass
+
+
+# ---- tensor parallelism (TPCoordinator's device counterpart) -----------------
+
+def tp_prepare(world: int, max_dim: int) -> bytes:
+    """Allocate this rank's exchange region; returns its 64-byte IPC handle."""
+    out = ctypes.create_string_buffer(64)
+    _err("gi_cuda_tp_prepare", load_library().gi_cuda_tp_prepare(world, max_dim, out))
+    return out.raw
+
+
+def tp_connect(rank: int, world: int, handles: bytes) -> None:
+    """Map every rank's region (handles = the ranks' 64-byte handles, in rank order)."""
+    if len(handles) != 64 * world:
+        raise GoInferCudaError("gi_cuda_tp_connect", ERR_SHAPE, "need 64 bytes per rank")
+    buf = ctypes.create_string_buffer(handles, len(handles))
+    _err("gi_cuda_tp_connect", load_library().gi_cuda_tp_connect(rank, world, buf))
+
+
+def tp_close() -> None:
+    _err("gi_cuda_tp_close", load_library().gi_cuda_tp_close())

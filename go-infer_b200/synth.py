@@ -2,8 +2,9 @@
 
 The benchmark configurations name random-init models (weights N(0, 0.02),
 quantised Q4_K, lm_head Q6_K, norms fp32).  This module draws them with the
-library's seeded generator (gi_quantize_seeded: one stream per (seed, row),
-so the bytes are the same on every machine and thread count), uploads them
+library's seeded generator (gi_quantize_seeded: one stream per (seed, row,
+256-column block), so the bytes are the same on every machine and thread
+count, and a tensor-parallel shard is drawn on its own), uploads them
 as weight buffers and describes them to the device-resident model
 (gi_cuda_model_create) or to gi_cuda_forward_transformer.  Tensor names and
 roles follow go-infer's GGUF loader (blk.N.attn_q.weight ...,
@@ -34,10 +35,11 @@ class LlamaConfig:
     out_type: int = G.TYPE_Q6_K
     embd_type: int = G.TYPE_Q4_K
     std: float = 0.02
+    hd: int = 0  # head dim when it is not dim / n_heads (a tensor-parallel shard)
 
     @property
     def head_dim(self) -> int:  # config.go:29-37
-        return self.dim // self.n_heads
+        return self.hd or self.dim // self.n_heads
 
     @property
     def kv_dim(self) -> int:  # config.go:48-56
@@ -51,6 +53,11 @@ class LlamaConfig:
 # Config 4: Llama-2-7B shape (32 layers, d=4096, 32 heads, FFN 11008, vocab
 # 32000, RoPE base 10000), 128-token prompt + 64 greedy steps.
 LLAMA2_7B = LlamaConfig(n_layers=32, dim=4096, hidden=11008, n_heads=32, n_kv_heads=32, vocab=32000, max_seq=192)
+
+# Config 5: Llama-3-70B shape (80 layers, d=8192, 64 query / 8 KV heads, FFN
+# 28672, vocab 128256, RoPE base 500000), 512-token prompt + 64 greedy steps.
+LLAMA3_70B = LlamaConfig(n_layers=80, dim=8192, hidden=28672, n_heads=64, n_kv_heads=8, vocab=128256, max_seq=576,
+                         rope_theta=500000.0)
 
 LAYER_MATS = ("wq", "wk", "wv", "wo", "ffn_gate", "ffn_up", "ffn_down")
 
@@ -72,26 +79,51 @@ class HostModel:
         return self.tensors[f"blk.{l}.{name}"]
 
 
-def synth_model(cfg: LlamaConfig, seed: int, threads: int = 0) -> HostModel:
-    """Every tensor drawn with seed * 1_000_003 + its index."""
-    m = HostModel(cfg)
+def shard_config(cfg: LlamaConfig, world: int) -> LlamaConfig:
+    """This rank's shapes under Megatron tensor parallelism over `world` GPUs."""
+    if cfg.n_heads % world or cfg.n_kv_heads % world or cfg.hidden % (256 * world) or cfg.vocab % world \
+            or (cfg.q_dim // world) % 256:
+        raise ValueError(f"{cfg} does not split {world} ways on 256-column blocks")
+    return LlamaConfig(cfg.n_layers, cfg.dim, cfg.hidden // world, cfg.n_heads // world, cfg.n_kv_heads // world,
+                       cfg.vocab // world, cfg.max_seq, cfg.eps, cfg.rope_theta, cfg.wtype, cfg.out_type,
+                       cfg.embd_type, cfg.std, hd=cfg.head_dim)
+
+
+def shard_slices(cfg: LlamaConfig, rank: int, world: int) -> dict:
+    """(row0, rows, col0, cols) of rank's shard of each matrix: column split
+    (rows) for Q, K, V, gate, up and the output head, row split (columns)
+    for the output and down projections; the token table is replicated."""
+    q, kv, h, v = cfg.q_dim // world, cfg.kv_dim // world, cfg.hidden // world, cfg.vocab // world
+    return {"wq": (rank * q, q, 0, cfg.dim), "wk": (rank * kv, kv, 0, cfg.dim), "wv": (rank * kv, kv, 0, cfg.dim),
+            "wo": (0, cfg.dim, rank * q, q), "ffn_gate": (rank * h, h, 0, cfg.dim),
+            "ffn_up": (rank * h, h, 0, cfg.dim), "ffn_down": (0, cfg.dim, rank * h, h),
+            "output": (rank * v, v, 0, cfg.dim), "token_embd": (0, cfg.vocab, 0, cfg.dim)}
+
+
+def synth_model(cfg: LlamaConfig, seed: int, threads: int = 0, rank: int = 0, world: int = 1) -> HostModel:
+    """Every tensor drawn with seed * 1_000_003 + its index; with world > 1
+    only rank's shard of each (a slice of the same tensors), under the
+    shard's config."""
     shapes = layer_shapes(cfg)
+    sl = shard_slices(cfg, rank, world) if world > 1 else None
+    m = HostModel(shard_config(cfg, world) if world > 1 else cfg)
     k = 0
 
-    def draw(qt, rows, cols):
+    def draw(qt, name, rows, cols):
         nonlocal k
         k += 1
-        return (qt, G.quantize_seeded(qt, seed * 1_000_003 + k, cfg.std, rows, cols, threads))
+        r0, nr, c0, nc = sl[name] if sl else (0, rows, 0, cols)
+        return (qt, G.quantize_seeded(qt, seed * 1_000_003 + k, cfg.std, nr, nc, threads, row0=r0, col0=c0))
 
-    m.tensors["token_embd.weight"] = draw(cfg.embd_type, cfg.vocab, cfg.dim)
+    m.tensors["token_embd.weight"] = draw(cfg.embd_type, "token_embd", cfg.vocab, cfg.dim)
     for l in range(cfg.n_layers):
         for name in LAYER_MATS:
             r, c = shapes[name]
-            m.tensors[f"blk.{l}.{name}.weight"] = draw(cfg.wtype, r, c)
+            m.tensors[f"blk.{l}.{name}.weight"] = draw(cfg.wtype, name, r, c)
         for name in ("attn_norm", "ffn_norm"):
             m.tensors[f"blk.{l}.{name}.weight"] = (G.TYPE_F32, np.ones(cfg.dim, np.float32))
     m.tensors["output_norm.weight"] = (G.TYPE_F32, np.ones(cfg.dim, np.float32))
-    m.tensors["output.weight"] = draw(cfg.out_type, cfg.vocab, cfg.dim)
+    m.tensors["output.weight"] = draw(cfg.out_type, "output", cfg.vocab, cfg.dim)
     return m
 
 
@@ -119,7 +151,7 @@ class DeviceModel:
             layers.append(d)
         self.table = G.layer_table(layers)
 
-    def desc(self, max_pos: int = 0) -> G.ModelDesc:
+    def desc(self, max_pos: int = 0, tp_rank: int = 0, tp_world: int = 1) -> G.ModelDesc:
         c = self.cfg
         d = G.ModelDesc()
         d.num_layers, d.dim, d.hidden_dim = c.n_layers, c.dim, c.hidden
@@ -132,10 +164,11 @@ class DeviceModel:
         d.output_norm = self.bufs["output_norm.weight"].handle
         d.output_weight = self.bufs["output.weight"].handle
         d.output_weight_type = self.types["output.weight"]
+        d.tp_world, d.tp_rank, d.vocab_offset = tp_world, tp_rank, tp_rank * c.vocab if tp_world > 1 else 0
         return d
 
-    def model(self, max_pos: int = 0) -> G.Model:
-        return G.Model(self.desc(max_pos), keep=self)
+    def model(self, max_pos: int = 0, tp_rank: int = 0, tp_world: int = 1) -> G.Model:
+        return G.Model(self.desc(max_pos, tp_rank, tp_world), keep=self)
 
     def close(self) -> None:
         for b in self.bufs.values():

@@ -1,0 +1,39 @@
+"""Tensor-parallel decode on the GPUs of one node (one process per GPU).
+
+The counterpart of go-infer's TPCoordinator (pkg/distributed/
+tensor_parallel.go): NewTPCoordinator(rank, peers) becomes connect(), which
+exchanges the ranks' CUDA IPC handles of their exchange regions over an
+initialised torch.distributed process group; AllReduce itself runs on the
+GPUs inside every decode step (the row-split projections push their
+partials over NVLink, see gi_cuda_tp_prepare).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch.distributed as dist
+
+import goinfer_cuda as G
+import synth
+
+
+def connect(rank: int, world: int, max_dim: int) -> None:
+    """Allocate this rank's exchange region and map every peer's."""
+    handle = G.tp_prepare(world, max_dim)
+    handles = [None] * world
+    dist.all_gather_object(handles, handle)
+    G.tp_connect(rank, world, b"".join(handles))
+    dist.barrier()
+
+
+def build(cfg: synth.LlamaConfig, seed: int, rank: int, world: int, max_pos: int = 0):
+    """This rank's shard of the seeded synthetic model, on the device."""
+    host = synth.synth_model(cfg, seed, rank=rank, world=world)
+    dev = synth.DeviceModel(host)
+    del host
+    return dev, dev.model(max_pos, tp_rank=rank, tp_world=world)
+
+
+def greedy(model: G.Model, prompt, n_gen: int):
+    """Greedy decode on every rank (identical ids on all ranks)."""
+    ids, _logits, ms = model.generate(np.asarray(prompt, np.int32), n_gen)
+    return ids, ms

@@ -197,6 +197,12 @@ typedef struct {
   gi_cuda_buffer_t output_norm;
   gi_cuda_buffer_t output_weight;
   int output_weight_type;
+  /* Tensor parallelism (0 or 1 = off): this process is rank tp_rank of
+   * tp_world (gi_cuda_tp_connect first).  num_heads, num_kv_heads,
+   * hidden_dim and vocab_size are then this rank's shares and the weight
+   * buffers its shards: rows of wq/wk/wv/ffn_gate/ffn_up/output, columns of
+   * wo/ffn_down; vocab_offset is the first output row it holds. */
+  uint32_t tp_world, tp_rank, vocab_offset;
 } gi_cuda_model_desc_t;
 
 typedef void* gi_cuda_model_t;
@@ -215,6 +221,20 @@ int gi_cuda_model_reset(gi_cuda_model_t model);
  * decode_ms (or NULL) the device time of the n_gen - 1 generation steps. */
 int gi_cuda_model_generate(gi_cuda_model_t model, const int32_t* tokens, uint32_t n_tokens, uint32_t start_pos,
                            uint32_t n_gen, uint32_t* out_tokens, float* out_logits, float* decode_ms);
+
+/* ---- tensor parallelism across the GPUs of one node -------------------------
+ * The device-side counterpart of TPCoordinator (pkg/distributed/
+ * tensor_parallel.go:13-31, AllReduce :33-108): instead of HTTP peers, each
+ * rank allocates an exchange region in its own HBM that every peer writes over
+ * NVLink.  1) gi_cuda_tp_prepare allocates it and returns its CUDA IPC handle
+ * (64 bytes) for the caller to share (e.g. an all-gather over
+ * torch.distributed); 2) gi_cuda_tp_connect maps every peer's region
+ * (handles[r * 64 ...] is rank r's); then models created with tp_world > 1
+ * sum their row-split projections across the ranks. */
+int gi_cuda_tp_prepare(int world, uint32_t max_dim, void* handle_out);
+int gi_cuda_tp_connect(int rank, int world, const void* handles);
+/* Unmaps the peers and frees the region (no model may use it any more). */
+int gi_cuda_tp_close(void);
 
 /* Device address / size of a buffer created by gi_cuda_create_buffer. */
 const void* gi_cuda_buffer_device_ptr(gi_cuda_buffer_t buf);
@@ -242,11 +262,14 @@ int gi_quantize(int quant_type, const float* src, int64_t rows, int64_t cols, vo
                 int threads);
 
 /* Synthetic weights for the benchmark configurations (no reference
- * counterpart): rows x cols drawn from N(0, stddev) with a generator keyed
- * by (seed, row), quantised like gi_quantize (GI_TYPE_F32 stores the float32
- * values).  The bytes do not depend on `threads` (<= 0: every core). */
-int gi_quantize_seeded(int quant_type, uint64_t seed, float stddev, int64_t rows, int64_t cols, void* dst,
-                       int threads);
+ * counterpart): rows [row0, row0 + rows) x columns [col0, col0 + cols) of a
+ * matrix drawn from N(0, stddev) by a generator keyed by (seed, row,
+ * 256-column block), quantised like gi_quantize (GI_TYPE_F32 stores the
+ * float32 values).  col0 is a multiple of 256, so a tensor-parallel shard is
+ * generated on its own; the bytes do not depend on `threads` (<= 0: every
+ * core). */
+int gi_quantize_seeded(int quant_type, uint64_t seed, float stddev, int64_t row0, int64_t rows, int64_t col0,
+                       int64_t cols, void* dst, int threads);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,58 @@
+"""One rank of a tensor-parallel greedy decode (run under torchrun by
+tests/test_tp_gpu.py and bench.py): builds this rank's shard of a seeded
+synthetic model, connects the exchange regions, decodes, and (rank 0) writes
+the ids and device time to --out as .npz."""
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "go-infer_b200"))
+
+import goinfer_cuda as G  # noqa: E402
+import synth  # noqa: E402
+import tp  # noqa: E402
+
+CONFIGS = {
+    # small enough for a test, every split 256-column aligned for 2 / 4 / 8 ranks
+    "small": synth.LlamaConfig(n_layers=2, dim=1024, hidden=4096, n_heads=16, n_kv_heads=8, vocab=4096, max_seq=64),
+    "llama70b": synth.LLAMA3_70B,
+}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--config", default="small")
+    ap.add_argument("--seed", type=int, default=21)
+    ap.add_argument("--prompt", type=int, default=12)
+    ap.add_argument("--gen", type=int, default=16)
+    ap.add_argument("--out", required=True)
+    a = ap.parse_args()
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", init_method="env://")
+    G.Init(local)
+    cfg = CONFIGS[a.config]
+    tp.connect(rank, world, cfg.dim)
+    dev, model = tp.build(cfg, a.seed, rank, world)
+    prompt = np.random.default_rng(a.seed + 1).integers(0, cfg.vocab, a.prompt)
+    ids, ms = tp.greedy(model, prompt, a.gen)
+    all_ids = [None] * world
+    dist.all_gather_object(all_ids, ids.tolist())
+    if rank == 0:
+        np.savez(a.out, ids=ids, ms=np.array(ms), prompt=prompt,
+                 same_on_all_ranks=np.array(all(x == all_ids[0] for x in all_ids)))
+    model.close()
+    dev.close()
+    dist.barrier()
+    G.tp_close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
