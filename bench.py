@@ -26,6 +26,14 @@ line with "impl": "reference".
 Multi-GPU: one process per GPU (torchrun); each rank runs its own copy of
 the workload (the GEMV units are independent, no collective on this path):
 weak scaling, value = bytes of all ranks / max rank time.
+
+decode   (the metric's second half) greedy decode tokens/s of the Llama-
+         shaped synthetic models, device-timed (CUDA events around the
+         generation steps, max over ranks): config 5 (Llama-3-70B shape,
+         512-token prompt, 64 steps) tensor-parallel over the N ranks, and at
+         N=1 config 4 (Llama-2-7B shape, 128-token prompt, 64 steps) with a
+         bounded CPU-oracle sample of the same decode step; prefill (config
+         3, 512 tokens x 4096 columns) at N=1.
 """
 from __future__ import annotations
 
@@ -216,6 +224,104 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def decode_section(args, world, rank, local, pg):
+    """Config 5 on all ranks (tensor parallel), config 4 / prefill / CPU sample at N=1."""
+    import dataclasses
+    import torch
+    import goinfer_cuda as G
+    import synth
+    import tp
+
+    dev = torch.device("cuda", local)
+    out = {}
+
+    def max_over_ranks(v):
+        t = torch.tensor([float(v)], device=dev)
+        if pg:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    # config 5: Llama-3-70B shape, weights drawn on the device (seeded)
+    cfg5 = synth.LLAMA3_70B
+    if world > 1:
+        tp.connect(rank, world, cfg5.dim)
+    dm = synth.DeviceModel.synth_on_device(cfg5, seed=5, rank=rank, world=world)
+    model = dm.model(tp_rank=rank, tp_world=world)
+    prompt5 = np.random.default_rng(50).integers(0, cfg5.vocab, 512).astype(np.int32)
+    ids, _l, ms = model.generate(prompt5, 64)
+    model.reset()
+    ids, _l, ms = model.generate(prompt5, 64)
+    ms = max_over_ranks(ms)
+    w_bytes = sum(b.nbytes for b in dm.bufs.values()) - dm.bufs["token_embd.weight"].nbytes
+    model.close()
+    dm.close()
+    if world > 1:
+        pg.barrier()
+        G.tp_close()
+    out["config5"] = {"model": "Llama-3-70B shape (80 x d8192, 64/8 heads, FFN 28672, vocab 128256), Q4_K + Q6_K head",
+                      "parallelism": f"tensor parallel x{world}" if world > 1 else "single GPU",
+                      "prompt": 512, "steps": 64, "tok_s": round(63 / (ms / 1e3), 2),
+                      "ms_per_token": round(ms / 63, 4),
+                      "weight_bytes_per_token_per_gpu": int(w_bytes),
+                      "ids_head": [int(i) for i in ids[:8]]}
+    if world > 1:
+        return out
+    # config 4: Llama-2-7B shape
+    cfg4 = synth.LLAMA2_7B
+    dm = synth.DeviceModel.synth_on_device(cfg4, seed=4)
+    model = dm.model()
+    prompt4 = np.random.default_rng(40).integers(0, cfg4.vocab, 128).astype(np.int32)
+    model.generate(prompt4, 64)
+    model.reset()
+    ids4, _l, ms4 = model.generate(prompt4, 64)
+    w_bytes = sum(b.nbytes for b in dm.bufs.values()) - dm.bufs["token_embd.weight"].nbytes
+    out["config4"] = {"model": "Llama-2-7B shape (32 x d4096, 32 heads, FFN 11008, vocab 32000), Q4_K + Q6_K head",
+                      "prompt": 128, "steps": 64, "tok_s": round(63 / (ms4 / 1e3), 2),
+                      "ms_per_token": round(ms4 / 63, 4), "weight_bytes_per_token": int(w_bytes),
+                      "effective_gbs": round(w_bytes / (ms4 / 63 / 1e3) / 1e9, 1)}
+    if not args.no_cpu_baseline:
+        # the CPU restatement of Engine.Forward on the same bytes, a bounded sample
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        tensors = {name: (dm.types[name], dm.raw(name)) for name in dm.bufs}
+        ref = O.RefModel(cfg4, tensors)
+        t0 = time.perf_counter()
+        nsteps = 0
+        while nsteps < 2 or (time.perf_counter() - t0 < args.cpu_seconds and nsteps < 8):
+            ref.forward(int(prompt4[nsteps]), nsteps)
+            nsteps += 1
+        cpu_s = (time.perf_counter() - t0) / nsteps
+        out["config4"]["cpu_baseline"] = {"tok_s": round(1.0 / cpu_s, 4), "cores": os.cpu_count(), "kind": "port",
+                                          "sample": f"{nsteps} decode steps of the same model (oracle ref_forward)"}
+        del tensors, ref
+    model.close()
+    dm.close()
+    # config 3: prefill dequant-GEMM (512 tokens x 4096 columns)
+    x = torch.randn(512, 4096, device=dev)
+    st = torch.cuda.Stream()
+    pre = {}
+    for name, qt, rows, seed in (("q4k_4096", G.TYPE_Q4_K, 4096, 8), ("q4k_11008", G.TYPE_Q4_K, 11008, 9),
+                                 ("q6k_32000", G.TYPE_Q6_K, 32000, 10)):
+        wb = G.synth_buffer(qt, seed, 0.02, rows, 4096)
+        y = torch.empty(512, rows, device=dev)
+        run = lambda: G.gemm_dev(qt, y.data_ptr(), x.data_ptr(), wb.device_ptr, wb.nbytes, 512, rows, 4096,
+                                 st.cuda_stream)
+        for _ in range(3):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            e0.record()
+            for _ in range(10):
+                run()
+            e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 100.0
+        pre[name] = {"us": round(us, 1), "tflops": round(2 * 512 * rows * 4096 / us / 1e6, 1)}
+        G.ReleaseBuffer(wb)
+    out["prefill_config3"] = pre
+    return out
+
+
 def run_ours(args):
     import torch
     import goinfer_cuda as G
@@ -319,6 +425,8 @@ def run_ours(args):
     for b in bufs.values():
         G.ReleaseBuffer(b)
 
+    decode = None if args.no_decode else decode_section(args, world, rank, local, pg)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, cores, sample = cpu_port_gemv_gbs(args.cpu_seconds)
@@ -345,6 +453,7 @@ def run_ours(args):
             "gpu_launches": 2 * args.steps,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     if pg:
@@ -361,6 +470,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode / prefill section")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -27,6 +27,8 @@ int quantize_host(int qtype, const float* src, int64_t rows, int64_t cols, uint8
                   int threads);
 int quantize_seeded(int qtype, uint64_t seed, float stddev, int64_t row0, int64_t rows, int64_t col0, int64_t cols,
                     uint8_t* dst, int threads);
+int synth_device(int qtype, uint64_t seed, float stddev, int64_t row0, int64_t rows, int64_t col0, int64_t cols,
+                 void* dst, size_t dst_bytes, cudaStream_t stream);
 }
 
 namespace {
@@ -885,6 +887,42 @@ int gi_quantize_seeded(int quant_type, uint64_t seed, float stddev, int64_t row0
   const int rc = gi::quantize_seeded(quant_type, seed, stddev, row0, rows, col0, cols, static_cast<uint8_t*>(dst),
                                      threads);
   if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : "unsupported shape");
+  return 0;
+}
+
+int gi_cuda_buffer_read(gi_cuda_buffer_t buf, void* dst, size_t bytes) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  const Buffer* b = static_cast<const Buffer*>(buf);
+  if (!b || !b->dptr || !dst || bytes > b->bytes) return fail(-4, "bad buffer read");
+  GI_CUDA_TRY(cudaMemcpy(dst, b->dptr, bytes, cudaMemcpyDeviceToHost), "read buffer");
+  return 0;
+}
+
+gi_cuda_buffer_t gi_cuda_alloc_buffer(size_t bytes) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (ensure_ready() || bytes == 0) return nullptr;
+  Buffer* b = new Buffer();
+  if (cudaMalloc(&b->dptr, bytes + 64) != cudaSuccess) {
+    delete b;
+    fail(-3, "cudaMalloc buffer");
+    return nullptr;
+  }
+  b->bytes = bytes;
+  b->device = g.device;
+  return b;
+}
+
+int gi_synth_weights(gi_cuda_buffer_t buf, int quant_type, uint64_t seed, float stddev, int64_t row0, int64_t rows,
+                     int64_t col0, int64_t cols) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  Buffer* b = static_cast<Buffer*>(buf);
+  if (!b || !b->dptr) return fail(-3, "null buffer");
+  const int rc = gi::synth_device(quant_type, seed, stddev, row0, rows, col0, cols, b->dptr, b->bytes, g.stream);
+  if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : rc == -4 ? "unsupported shape" : "launch failed",
+                      rc == -5 ? cudaGetLastError() : cudaSuccess);
+  GI_CUDA_TRY(cudaStreamSynchronize(g.stream), "synthetic weights");
   return 0;
 }
 

@@ -83,15 +83,16 @@ struct Params {
   TpDev tp;  // kYPush
   long long rowb;
   int nku, ntiles, ctas;
-  int x_off, slot_off;  // dynamic smem byte offsets (rings at 0)
+  int x_off, slot_off, red_off;  // dynamic smem byte offsets (rings at 0)
 };
 
 // Matrix m and its local 16-row tile lt of global tile T: matrices one
 // after another (tiles of matrix m are [tstart[m], tstart[m+1])), or in
 // kYSwiGLU mode gate and up tiles interleaved (gate tile i = 2i, up = 2i+1)
 // so that one CTA holds both halves of every row it finishes.
+template <bool F>
 GI_DEVINL void tile_of(const Params& p, int T, int& m, int& lt) {
-  if (p.ymode == kYSwiGLU) {
+  if (F && p.ymode == kYSwiGLU) {
     m = T & 1;
     lt = T >> 1;
   } else {
@@ -174,15 +175,15 @@ GI_DEVINL float4 mul3(float4 a, float s, float4 w) {  // (a * s) * w, one roundi
 // (pkg/math/kernels.go:9-19: float32 sum of squares, scale
 // float32(1 / sqrt(float64(mean + eps))), out = x * scale * w), computed by
 // every CTA from the same data in the same order.
-__device__ void stage_x(uint8_t* xs, const Params& p) {
+template <bool F>
+__device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int j = lane >> 2, q = lane & 3;
   const int off = 64 * (j >> 1) + 32 * (j & 1) + 8 * q;
   const int nku = p.nku;
   const float* __restrict__ x = p.x;
   float scale = 1.f;
-  if (p.xmode == kXNorm) {
-    __shared__ float red[kWarps];
+  if (F && p.xmode == kXNorm) {
     const float4* x4 = reinterpret_cast<const float4*>(x);
     float s = 0.f;
     for (int i = threadIdx.x; i < nku * 64; i += kThreads) {
@@ -209,7 +210,7 @@ __device__ void stage_x(uint8_t* xs, const Params& p) {
       if (u < nku) {
         a[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off));
         b[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off + 4));
-        if (p.xmode == kXNorm) {
+        if (F && p.xmode == kXNorm) {
           a[k] = mul3(a[k], scale, __ldg(reinterpret_cast<const float4*>(p.x2 + u * 256 + off)));
           b[k] = mul3(b[k], scale, __ldg(reinterpret_cast<const float4*>(p.x2 + u * 256 + off + 4)));
         }
@@ -294,7 +295,9 @@ GI_DEVINL void compute_unit(uint32_t stage, uint32_t xu, int g, int t, uint32_t 
   yB = fmaf((cm[2] + cm[3]) * -dB.y, inv_min, yB);
 }
 
-template <int S>
+// F: the decode-step fusions (RMSNorm staging, residual / SwiGLU / push
+// epilogues) are compiled in; without them the kernel is the plain GEMV.
+template <int S, bool F>
 __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
   extern __shared__ __align__(16) uint8_t smem[];
   griddep_launch_dependents();
@@ -302,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
   const int g = lane >> 2, t = lane & 3;
   const int c = blockIdx.x;
   // CTA c owns tiles [T0, T1); in kYSwiGLU mode whole (gate, up) pairs.
-  const int gran = p.ymode == kYSwiGLU ? 2 : 1, nun = p.ntiles / gran;
+  const int gran = (F && p.ymode == kYSwiGLU) ? 2 : 1, nun = p.ntiles / gran;
   const int T0 = gran * (int)((long long)nun * c / p.ctas), T1 = gran * (int)((long long)nun * (c + 1) / p.ctas);
   const int ntl = T1 - T0, n = ntl * p.nku;  // the CTA's units, tile-major
   const uint32_t ring = smem_u32(smem) + warp * S * kStageBytes;
@@ -328,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
   auto request = [&](int stage) {  // always commits one group (possibly empty)
     if (next < n) {
       int m, lt;
-      tile_of(p, T0 + ltile, m, lt);
+      tile_of<F>(p, T0 + ltile, m, lt);
       const int r0 = lt * 16, rl = p.rows[m] - 1;
       const int rA = min(r0 + g, rl);
       const int rB = min(r0 + g + 8, rl);
@@ -349,7 +352,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
 #pragma unroll
   for (int s = 0; s < S; ++s) request(s);
   griddep_wait();
-  stage_x(xs, p);  // ends with a CTA barrier (also orders the slot zeroing)
+  // ends with a CTA barrier (also orders the slot zeroing)
+  stage_x<F>(xs, reinterpret_cast<float*>(smem + p.red_off), p);
 
   const uint32_t sh8 = 8u * (uint32_t)t;
   // Limb weights 256^(3-n) of this lane's two columns, divided by the 16
@@ -391,9 +395,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) sum += slots[(tl * kWarps + w) * 16 + lane];
       int m, lt;
-      tile_of(p, T0 + tl, m, lt);
+      tile_of<F>(p, T0 + tl, m, lt);
       const int row = lt * 16 + lane;
-      if (p.ymode == kYSwiGLU) {
+      if (F && p.ymode == kYSwiGLU) {
         // gate tile (even) pairs with the next (up) tile: SwiGLU
         // (kernels.go:39-46), silu = g / (1 + float32(exp(float64(-g)))).
         if ((tl & 1) == 0 && row < p.rows[0]) {
@@ -403,18 +407,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
           const float silu = __fdiv_rn(sum, __fadd_rn(1.0f, (float)exp(-(double)sum)));
           p.y[0][row] = __fmul_rn(silu, up);
         }
-      } else if (p.ymode == kYPush) {
+      } else if (F && p.ymode == kYPush) {
         if (row < p.rows[m]) {  // this rank's partial into slot `rank` of every rank's region
           const uint32_t set = *p.tp.seq & 1u;
           const size_t off = ((size_t)set * p.tp.world + p.tp.rank) * p.tp.max_dim + row;
           for (int r = 0; r < p.tp.world; ++r) p.tp.recv[r][off] = sum;
         }
       } else if (row < p.rows[m]) {
-        p.y[m][row] = p.ymode == kYAdd ? __fadd_rn(p.y[m][row], sum) : sum;  // residual: y += W x
+        p.y[m][row] = (F && p.ymode == kYAdd) ? __fadd_rn(p.y[m][row], sum) : sum;  // residual: y += W x
       }
     }
   }
-  if (p.ymode == kYPush) {
+  if (F && p.ymode == kYPush) {
     // The last CTA to finish publishes the push: flag[rank] = seq on every
     // rank, after every CTA's stores are visible system-wide.
     __threadfence_system();
@@ -434,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
 }
 
 struct Layout {
-  int ctas, ntiles, stages, x_off, slot_off, smem;
+  int ctas, ntiles, stages, x_off, slot_off, red_off, smem;
 };
 
 Layout layout(int64_t ntiles, int64_t cols, const GemvLaunch& L, int gran = 1) {
@@ -446,13 +450,14 @@ Layout layout(int64_t ntiles, int64_t cols, const GemvLaunch& L, int gran = 1) {
   const int max_tiles = gran * ((nun + o.ctas - 1) / o.ctas);
   const int xbytes = nku * kUnitX;
   const int slot_bytes = max_tiles * kWarps * 16 * 4;
-  const int fixed = xbytes + slot_bytes;
+  const int fixed = xbytes + slot_bytes + 4 * kWarps;
   // As many stages as fit next to a co-resident CTA, at least 2.
   o.stages = 4;
   while (o.stages > 2 && fixed + kWarps * o.stages * kStageBytes > kCoresidentSmem) --o.stages;
   o.x_off = kWarps * o.stages * kStageBytes;
   o.slot_off = o.x_off + xbytes;
-  o.smem = o.slot_off + slot_bytes;
+  o.red_off = o.slot_off + slot_bytes;  // RMSNorm reduction (kWarps floats)
+  o.smem = o.red_off + 4 * kWarps;
   return o;
 }
 
@@ -488,6 +493,7 @@ int launch(int nmat, float* const* y, const float* x, const void* const* w, cons
   p.ctas = o.ctas;
   p.x_off = o.x_off;
   p.slot_off = o.slot_off;
+  p.red_off = o.red_off;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(o.ctas);
   cfg.blockDim = dim3(kThreads);
@@ -499,21 +505,31 @@ int launch(int nmat, float* const* y, const float* x, const void* const* w, cons
   cfg.attrs = attr;
   cfg.numAttrs = L.pdl ? 1 : 0;
   cudaError_t e;
-  switch (o.stages) {  // tile counts past nmat equal the total: mat_of stays < nmat
-    case 4: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<4>, p); break;
-    case 3: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<3>, p); break;
-    default: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<2>, p); break;
+  const bool fused = f.xmode != kXPlain || f.ymode != kYStore;
+  switch (o.stages * 2 + (fused ? 1 : 0)) {  // tile counts past nmat equal the total: tile_of stays < nmat
+    case 8: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<4, false>, p); break;
+    case 9: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<4, true>, p); break;
+    case 6: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<3, false>, p); break;
+    case 7: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<3, true>, p); break;
+    case 5: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<2, true>, p); break;
+    default: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<2, false>, p); break;
   }
   return e == cudaSuccess ? 0 : -5;
 }
 
+template <int S, bool F>
+cudaError_t prepare_one() {
+  cudaError_t e = cudaFuncSetAttribute(gemv_q4k_kernel<S, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  return e == cudaSuccess ? set_max_shared_carveout(gemv_q4k_kernel<S, F>) : e;
+}
+
 int prepare() {
-  cudaError_t e = cudaFuncSetAttribute(gemv_q4k_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_q4k_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_q4k_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
-  if (e == cudaSuccess) e = set_max_shared_carveout(gemv_q4k_kernel<4>);
-  if (e == cudaSuccess) e = set_max_shared_carveout(gemv_q4k_kernel<3>);
-  if (e == cudaSuccess) e = set_max_shared_carveout(gemv_q4k_kernel<2>);
+  cudaError_t e = prepare_one<4, false>();
+  if (e == cudaSuccess) e = prepare_one<4, true>();
+  if (e == cudaSuccess) e = prepare_one<3, false>();
+  if (e == cudaSuccess) e = prepare_one<3, true>();
+  if (e == cudaSuccess) e = prepare_one<2, false>();
+  if (e == cudaSuccess) e = prepare_one<2, true>();
   return e == cudaSuccess ? 0 : -5;
 }
 }  // namespace q4k

@@ -1,4 +1,5 @@
-// quantize.cpp -- host quantisers that produce GGUF Q8_0 / Q4_K / Q6_K rows.
+// quantize.cu -- quantisers that produce GGUF Q8_0 / Q4_K / Q6_K rows, on the
+// host and (for the synthetic benchmark models) on the device.
 //
 // Model-preparation tooling (the counterpart of go-infer's cmd/quantize),
 // not part of the GEMV path.  Q8_0 follows go-infer's own QuantizeQ8_0
@@ -7,7 +8,8 @@
 // those two are this library's own min/max fits written from the block
 // formats that DequantizeQ4_K / DequantizeQ6_K decode
 // (pkg/quant/quant.go:215-291).  Every step is a single IEEE float32
-// operation, so the result is deterministic across compilers.
+// operation (host code built with -ffp-contract=off, device code with
+// -fmad=false), so host and device quantise a block identically.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -15,24 +17,28 @@
 #include <thread>
 #include <vector>
 
+#include <cuda_runtime.h>
+
 #include "gemv.cuh"
+
+#define GI_HD __host__ __device__ inline
 
 namespace gi {
 namespace {
 
-inline uint32_t f2u(float f) {
+GI_HD uint32_t f2u(float f) {
   uint32_t u;
   std::memcpy(&u, &f, 4);
   return u;
 }
-inline float u2f(uint32_t u) {
+GI_HD float u2f(uint32_t u) {
   float f;
   std::memcpy(&f, &u, 4);
   return f;
 }
 
 // fp32 -> fp16 by truncation of the mantissa, as go-infer's FP32ToFP16.
-uint16_t f32_to_f16_trunc(float val) {
+GI_HD uint16_t f32_to_f16_trunc(float val) {
   const uint32_t bits = f2u(val);
   const uint32_t sign = (bits >> 16) & 0x8000u;
   int exp = (int)((bits >> 23) & 0xFF);
@@ -49,7 +55,7 @@ uint16_t f32_to_f16_trunc(float val) {
 }
 
 // Exact fp16 -> fp32 for every finite value.
-float f16_to_f32(uint16_t h) {
+GI_HD float f16_to_f32(uint16_t h) {
   const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
   uint32_t exp = (h >> 10) & 0x1F, mant = h & 0x3FFu;
   if (exp == 0) {
@@ -66,18 +72,18 @@ float f16_to_f32(uint16_t h) {
   return u2f(sign | ((exp + 112) << 23) | (mant << 13));
 }
 
-inline void put16(uint8_t* p, uint16_t v) {
+GI_HD void put16(uint8_t* p, uint16_t v) {
   p[0] = (uint8_t)(v & 0xFF);
   p[1] = (uint8_t)(v >> 8);
 }
 
 // QuantizeQ8_0 for one row of `n` floats (n a multiple of 32).
-void q8_0_row(const float* src, int64_t n, uint8_t* out) {
+GI_HD void q8_0_row(const float* src, int64_t n, uint8_t* out) {
   for (int64_t b = 0; b < n / 32; ++b) {
     const float* s = src + 32 * b;
     float maxv = 0.f;
     for (int i = 0; i < 32; ++i) {
-      const float v = std::fabs(s[i]);
+      const float v = fabsf(s[i]);
       if (v > maxv) maxv = v;
     }
     float scale = maxv / 127.0f;
@@ -95,21 +101,21 @@ void q8_0_row(const float* src, int64_t n, uint8_t* out) {
         float v = s[i] * inv;
         if (v > 127) v = 127;
         else if (v < -128) v = -128;
-        q = (int8_t)std::round(v);
+        q = (int8_t)roundf(v);
       }
       o[2 + i] = (uint8_t)q;
     }
   }
 }
 
-inline float clampf(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
+GI_HD float clampf(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
 // Q4_K super-block fit: per 32-weight sub-block j, w ~ d*sc_j*q - dmin*m_j
 // with q in [0,15] and 6-bit sc_j, m_j.  The offset m_j*dmin covers the
 // sub-block minimum (clipped at 0), the step d*sc_j its range / 15; d and
 // dmin put the largest step / offset at 63 and go through the truncating
 // fp16 conversion the repository uses for every block scale.
-void q4_k_block(const float* w, uint8_t* out) {
+GI_HD void q4_k_block(const float* w, uint8_t* out) {
   float step[8], off[8];
   float max_step = 0.f, max_off = 0.f;
   for (int j = 0; j < 8; ++j) {
@@ -129,8 +135,8 @@ void q4_k_block(const float* w, uint8_t* out) {
   const float d = f16_to_f32(dh), dmin = f16_to_f32(mh);
   uint8_t sc[8], mn[8];
   for (int j = 0; j < 8; ++j) {
-    sc[j] = d > 0 ? (uint8_t)clampf(std::round(step[j] / d), 0.f, 63.f) : 0;
-    mn[j] = dmin > 0 ? (uint8_t)clampf(std::round(off[j] / dmin), 0.f, 63.f) : 0;
+    sc[j] = d > 0 ? (uint8_t)clampf(roundf(step[j] / d), 0.f, 63.f) : 0;
+    mn[j] = dmin > 0 ? (uint8_t)clampf(roundf(off[j] / dmin), 0.f, 63.f) : 0;
   }
   put16(out, dh);
   put16(out + 2, mh);
@@ -147,7 +153,7 @@ void q4_k_block(const float* w, uint8_t* out) {
     const float dm = dmin * (float)mn[j];
     for (int i = 0; i < 32; ++i) {
       float v = 0.f;
-      if (ds > 0) v = clampf(std::round((w[32 * j + i] + dm) / ds), 0.f, 15.f);
+      if (ds > 0) v = clampf(roundf((w[32 * j + i] + dm) / ds), 0.f, 15.f);
       q[32 * j + i] = (uint8_t)v;
     }
   }
@@ -161,12 +167,12 @@ void q4_k_block(const float* w, uint8_t* out) {
 // Q6_K super-block fit: per 16-weight sub-block s, w ~ d*sc_s*q with
 // q in [-32,31] and int8 sc_s; step = max|w| / 31, d puts the largest step
 // at 127.  Layout of DequantizeQ6_K (pkg/quant/quant.go:263-286).
-void q6_k_block(const float* w, uint8_t* out) {
+GI_HD void q6_k_block(const float* w, uint8_t* out) {
   float step[16], max_step = 0.f;
   for (int s = 0; s < 16; ++s) {
     float amax = 0.f;
     for (int i = 0; i < 16; ++i) {
-      const float v = std::fabs(w[16 * s + i]);
+      const float v = fabsf(w[16 * s + i]);
       if (v > amax) amax = v;
     }
     step[s] = amax / 31.0f;
@@ -176,19 +182,19 @@ void q6_k_block(const float* w, uint8_t* out) {
   const float d = f16_to_f32(dh);
   int8_t sc[16];
   for (int s = 0; s < 16; ++s)
-    sc[s] = d > 0 ? (int8_t)clampf(std::round(step[s] / d), -128.f, 127.f) : 0;
+    sc[s] = d > 0 ? (int8_t)clampf(roundf(step[s] / d), -128.f, 127.f) : 0;
   uint8_t q[256];  // stored as q + 32
   for (int s = 0; s < 16; ++s) {
     const float ds = d * (float)sc[s];
     for (int i = 0; i < 16; ++i) {
       float v = 0.f;
-      if (ds > 0) v = clampf(std::round(w[16 * s + i] / ds), -32.f, 31.f);
+      if (ds > 0) v = clampf(roundf(w[16 * s + i] / ds), -32.f, 31.f);
       q[16 * s + i] = (uint8_t)((int)v + 32);
     }
   }
   uint8_t* ql = out;
   uint8_t* qh = out + 128;
-  std::memset(out, 0, 210);
+  for (int i = 0; i < 210; ++i) out[i] = 0;
   for (int n = 0; n < 2; ++n)
     for (int l = 0; l < 32; ++l) {
       const int b = 128 * n + l;
@@ -304,6 +310,63 @@ int quantize_seeded(int qtype, uint64_t seed, float stddev, int64_t row0, int64_
   }
   for (auto& th : pool) th.join();
   return 0;
+}
+
+// ---- device generator of the synthetic benchmark models --------------------
+// The same splitmix64 streams as normal_block (one per (seed, row, 256-column
+// block)), but a float32 Box-Muller transform, and the block quantisers
+// above: one thread per 256-column block.  Deterministic on a given GPU; not
+// bit-identical to the host generator (float vs double transform).
+namespace {
+__device__ inline uint64_t splitmix64_d(uint64_t& s) {
+  uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void synth_kernel(int qtype, uint64_t seed, float stddev, int64_t row0, int64_t rows, int64_t col0,
+                             int64_t nblk, uint8_t* __restrict__ dst, int64_t rb) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * nblk) return;
+  const int64_t r = i / nblk, b = i - r * nblk;
+  float w[256];
+  uint64_t s = seed * 0xD1B54A32D192ED03ull ^ (uint64_t)(row0 + r) * 0x8CB92BA72F3D8DD7ull ^
+               (uint64_t)(col0 / 256 + b) * 0xA0761D6478BD642Full;
+  for (int k = 0; k < 256; k += 2) {
+    const float u1 = (float)((splitmix64_d(s) >> 40) + 1) * 0x1.0p-24f;  // (0, 1]
+    const float u2 = (float)(splitmix64_d(s) >> 40) * 0x1.0p-24f;        // [0, 1)
+    const float rad = sqrtf(-2.0f * logf(u1));
+    float sn, cs;
+    sincospif(2.0f * u2, &sn, &cs);
+    w[k] = rad * cs * stddev;
+    w[k + 1] = rad * sn * stddev;
+  }
+  uint8_t* o = dst + r * rb;
+  if (qtype == kTypeQ4_K) {
+    q4_k_block(w, o + 144 * b);
+  } else if (qtype == kTypeQ6_K) {
+    q6_k_block(w, o + 210 * b);
+  } else if (qtype == kTypeQ8_0) {
+    q8_0_row(w, 256, o + 8 * 34 * b);
+  } else {
+    float* f = reinterpret_cast<float*>(o) + 256 * b;
+    for (int k = 0; k < 256; ++k) f[k] = w[k];
+  }
+}
+}  // namespace
+
+int synth_device(int qtype, uint64_t seed, float stddev, int64_t row0, int64_t rows, int64_t col0, int64_t cols,
+                 void* dst, size_t dst_bytes, cudaStream_t stream) {
+  if (qtype != kTypeF32 && qtype != kTypeQ8_0 && qtype != kTypeQ4_K && qtype != kTypeQ6_K) return -2;
+  if (rows < 1 || row0 < 0 || col0 < 0 || col0 % 256 || cols < 256 || cols % 256) return -4;
+  const int64_t rb = qtype == kTypeF32 ? cols * 4 : row_bytes(qtype, cols);
+  if (dst_bytes < (size_t)(rb * rows)) return -4;
+  if (qtype == kTypeF32 && (reinterpret_cast<uintptr_t>(dst) & 3)) return -4;
+  const int64_t n = rows * (cols / 256);
+  synth_kernel<<<(unsigned)((n + 127) / 128), 128, 0, stream>>>(qtype, seed, stddev, row0, rows, col0, cols / 256,
+                                                                 static_cast<uint8_t*>(dst), rb);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -5;
 }
 
 }  // namespace gi

@@ -51,6 +51,7 @@ EXPORTS = (
     "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize", "gi_quantize_seeded",
     "gi_cuda_alloc_buffers", "gi_cuda_forward_transformer", "gi_cuda_model_create", "gi_cuda_model_destroy",
     "gi_cuda_model_reset", "gi_cuda_model_generate", "gi_cuda_tp_prepare", "gi_cuda_tp_connect", "gi_cuda_tp_close",
+    "gi_cuda_alloc_buffer", "gi_synth_weights", "gi_cuda_buffer_read",
 )
 
 
@@ -136,6 +137,10 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "gi_cuda_tp_prepare": ([i32, u32, vp], i32),
         "gi_cuda_tp_connect": ([i32, i32, vp], i32),
         "gi_cuda_tp_close": ([], i32),
+        "gi_cuda_alloc_buffer": ([sz], vp),
+        "gi_cuda_buffer_read": ([vp, vp, sz], i32),
+        "gi_synth_weights": ([vp, i32, ctypes.c_uint64, ctypes.c_float, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                              ctypes.c_int64], i32),
         "gi_cuda_model_destroy": ([vp], None),
         "gi_cuda_model_reset": ([vp], i32),
         "gi_cuda_model_generate": ([vp, ctypes.POINTER(ctypes.c_int32), u32, u32, u32, ctypes.POINTER(u32), f32p,
@@ -465,3 +470,28 @@ def tp_connect(rank: int, world: int, handles: bytes) -> None:
 
 def tp_close() -> None:
     _err("gi_cuda_tp_close", load_library().gi_cuda_tp_close())
+
+
+def synth_buffer(quant_type: int, seed: int, std: float, rows: int, cols: int, row0: int = 0,
+                 col0: int = 0) -> Buffer:
+    """A device buffer holding the synthetic matrix slice drawn on the GPU."""
+    rb = cols * 4 if quant_type == TYPE_F32 else row_bytes(quant_type, cols)
+    n = rows * rb
+    h = load_library().gi_cuda_alloc_buffer(n)
+    if not h:
+        raise GoInferCudaError("gi_cuda_alloc_buffer", ERR_BUFFER,
+                               load_library().gi_cuda_last_error().decode(errors="replace"))
+    buf = Buffer(h, n)
+    try:
+        _err("gi_synth_weights", load_library().gi_synth_weights(h, quant_type, seed, std, row0, rows, col0, cols))
+    except Exception:
+        ReleaseBuffer(buf)
+        raise
+    return buf
+
+
+def read_buffer(buf: Buffer) -> np.ndarray:
+    """A buffer's bytes, copied to the host."""
+    out = np.empty(buf.nbytes, np.uint8)
+    _err("gi_cuda_buffer_read", load_library().gi_cuda_buffer_read(buf.handle, out.ctypes.data, buf.nbytes))
+    return out

@@ -130,15 +130,60 @@ def synth_model(cfg: LlamaConfig, seed: int, threads: int = 0, rank: int = 0, wo
 class DeviceModel:
     """The tensors of a HostModel as weight buffers, with the layer table."""
 
-    def __init__(self, host: HostModel):
-        self.cfg = host.cfg
-        self.bufs = {}
-        for name, (_qt, arr) in host.tensors.items():
-            b = G.CreateBuffer(arr)
-            if b is None:
-                raise G.GoInferCudaError("CreateBuffer " + name, G.ERR_BUFFER)
-            self.bufs[name] = b
-        self.types = {name: qt for name, (qt, _a) in host.tensors.items()}
+    def __init__(self, host: HostModel = None, *, cfg: LlamaConfig = None, bufs: dict = None, types: dict = None):
+        if host is not None:
+            cfg, bufs, types = host.cfg, {}, {}
+            for name, (qt, arr) in host.tensors.items():
+                b = G.CreateBuffer(arr)
+                if b is None:
+                    raise G.GoInferCudaError("CreateBuffer " + name, G.ERR_BUFFER)
+                bufs[name] = b
+                types[name] = qt
+        self.cfg, self.bufs, self.types = cfg, bufs, types
+        self._layer_table()
+
+    @classmethod
+    def synth_on_device(cls, cfg: LlamaConfig, seed: int, rank: int = 0, world: int = 1) -> "DeviceModel":
+        """synth_model's tensors (or rank's shard of them) drawn on the GPU
+        (gi_synth_weights: same streams, float32 transform), so a 70B-shaped
+        model takes seconds rather than host minutes."""
+        shapes = layer_shapes(cfg)
+        sl = shard_slices(cfg, rank, world) if world > 1 else None
+        bufs, types = {}, {}
+        k = 0
+
+        def draw(key, qt, name, rows, cols):
+            nonlocal k
+            k += 1
+            r0, nr, c0, nc = sl[name] if sl else (0, rows, 0, cols)
+            bufs[key] = G.synth_buffer(qt, seed * 1_000_003 + k, cfg.std, nr, nc, row0=r0, col0=c0)
+            types[key] = qt
+
+        ones = np.ones(cfg.dim, np.float32)
+        try:
+            draw("token_embd.weight", cfg.embd_type, "token_embd", cfg.vocab, cfg.dim)
+            for l in range(cfg.n_layers):
+                for name in LAYER_MATS:
+                    r, c = shapes[name]
+                    draw(f"blk.{l}.{name}.weight", cfg.wtype, name, r, c)
+                for name in ("attn_norm", "ffn_norm"):
+                    bufs[f"blk.{l}.{name}.weight"] = G.CreateBuffer(ones)
+                    types[f"blk.{l}.{name}.weight"] = G.TYPE_F32
+            bufs["output_norm.weight"] = G.CreateBuffer(ones)
+            types["output_norm.weight"] = G.TYPE_F32
+            draw("output.weight", cfg.out_type, "output", cfg.vocab, cfg.dim)
+        except Exception:
+            for b in bufs.values():
+                G.ReleaseBuffer(b)
+            raise
+        return cls(cfg=shard_config(cfg, world) if world > 1 else cfg, bufs=bufs, types=types)
+
+    def raw(self, name: str) -> np.ndarray:
+        """A tensor's bytes copied back to the host (for the oracle)."""
+        out = G.read_buffer(self.bufs[name])
+        return out.view(np.float32) if self.types[name] == G.TYPE_F32 else out
+
+    def _layer_table(self) -> None:
         layers = []
         for l in range(self.cfg.n_layers):
             d = {}

@@ -25,11 +25,13 @@ def connect(rank: int, world: int, max_dim: int) -> None:
     dist.barrier()
 
 
-def build(cfg: synth.LlamaConfig, seed: int, rank: int, world: int, max_pos: int = 0):
-    """This rank's shard of the seeded synthetic model, on the device."""
-    host = synth.synth_model(cfg, seed, rank=rank, world=world)
-    dev = synth.DeviceModel(host)
-    del host
+def build(cfg: synth.LlamaConfig, seed: int, rank: int, world: int, max_pos: int = 0, device_synth: bool = False):
+    """This rank's shard of the seeded synthetic model, on the device (drawn
+    on the host, or with device_synth on the GPU)."""
+    if device_synth:
+        dev = synth.DeviceModel.synth_on_device(cfg, seed, rank=rank, world=world)
+    else:
+        dev = synth.DeviceModel(synth.synth_model(cfg, seed, rank=rank, world=world))
     return dev, dev.model(max_pos, tp_rank=rank, tp_world=world)
 
 

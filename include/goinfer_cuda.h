@@ -271,6 +271,22 @@ int gi_quantize(int quant_type, const float* src, int64_t rows, int64_t cols, vo
 int gi_quantize_seeded(int quant_type, uint64_t seed, float stddev, int64_t row0, int64_t rows, int64_t col0,
                        int64_t cols, void* dst, int threads);
 
+/* Copies the first `bytes` of a buffer to host memory (no reference
+ * counterpart). */
+int gi_cuda_buffer_read(gi_cuda_buffer_t buf, void* dst, size_t bytes);
+
+/* A device buffer of `bytes` without host contents (no reference
+ * counterpart); release with gi_cuda_release_buffer.  NULL on failure. */
+gi_cuda_buffer_t gi_cuda_alloc_buffer(size_t bytes);
+
+/* Fills `buf` with the synthetic matrix slice of gi_quantize_seeded drawn on
+ * the device (the same (seed, row, 256-column block) streams, a float32
+ * Box-Muller transform, the same block quantisers; cols a multiple of 256).
+ * Deterministic on a given GPU, not bit-identical to gi_quantize_seeded.
+ * Returns when the buffer is written. */
+int gi_synth_weights(gi_cuda_buffer_t buf, int quant_type, uint64_t seed, float stddev, int64_t row0, int64_t rows,
+                     int64_t col0, int64_t cols);
+
 #ifdef __cplusplus
 }
 #endif

@@ -66,7 +66,11 @@ def check_greedy(dev_model, ref, prompt, n_gen):
         i = int(np.argmax(ids != want))
         pytest.fail(f"greedy ids differ first at step {i}: gpu {ids[i]} vs oracle {want[i]} "
                     f"(oracle top-2 margin there {margins[i]:.3e}, smallest {margins.min():.3e})")
-    assert_parity(logits, want_logits, what="last-step logits")
+    # Whole-model logits carry the float32 summation-order noise of every
+    # layer: held to a normwise bar, max |gpu - oracle| <= 1e-3 * rms(oracle).
+    ref = want_logits.astype(np.float64)
+    err = np.abs(logits - ref).max() / np.sqrt(np.mean(ref * ref))
+    assert err <= 1e-3, f"last-step logits: max |diff| / rms = {err:.3e}"
     return ids
 
 
@@ -158,6 +162,24 @@ def test_config4_greedy_matches_oracle_golden():
         ref = gold["last_logits"].astype(np.float64)
         dev_err = np.abs(logits - ref).max() / np.sqrt(np.mean(ref * ref))
         assert dev_err <= 2e-3, f"config-4 last logits: max |diff| / rms = {dev_err:.3e}"
+    finally:
+        model.close()
+        dev.close()
+
+
+def test_70b_widths_two_layers_match_oracle():
+    """Config 5's widths (d=8192, 64 query / 8 KV heads, FFN 28672, vocab
+    128256, RoPE base 500000) on two layers, weights drawn on the device and
+    read back for the oracle: greedy ids identical to Engine.Forward's."""
+    import dataclasses
+    cfg = dataclasses.replace(synth.LLAMA3_70B, n_layers=2, max_seq=64)
+    dev = synth.DeviceModel.synth_on_device(cfg, seed=70)
+    model = dev.model()
+    try:
+        tensors = {name: (dev.types[name], dev.raw(name)) for name in dev.bufs}
+        ref = O.RefModel(cfg, tensors)
+        prompt = np.random.default_rng(71).integers(0, cfg.vocab, 12)
+        check_greedy(model, ref, prompt, 8)
     finally:
         model.close()
         dev.close()

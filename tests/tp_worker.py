@@ -31,6 +31,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=12)
     ap.add_argument("--gen", type=int, default=16)
     ap.add_argument("--out", required=True)
+    ap.add_argument("--device-synth", action="store_true", help="draw the weights on the GPU")
     a = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -39,7 +40,7 @@ def main():
     G.Init(local)
     cfg = CONFIGS[a.config]
     tp.connect(rank, world, cfg.dim)
-    dev, model = tp.build(cfg, a.seed, rank, world)
+    dev, model = tp.build(cfg, a.seed, rank, world, device_synth=a.device_synth)
     prompt = np.random.default_rng(a.seed + 1).integers(0, cfg.vocab, a.prompt)
     ids, ms = tp.greedy(model, prompt, a.gen)
     all_ids = [None] * world
