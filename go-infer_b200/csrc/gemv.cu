@@ -420,8 +420,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
   }
   if (F && p.ymode == kYPush) {
     // The last CTA to finish publishes the push: flag[rank] = seq on every
-    // rank, after every CTA's stores are visible system-wide.
-    __threadfence_system();
+    // rank.  Each CTA orders its stores before its count (GPU scope); the
+    // last one, having observed every count, fences at system scope and
+    // releases the flags, which carries all CTAs' stores to the peers.
+    __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
       const unsigned d = atomicAdd(p.tp.done, 1u);
@@ -430,8 +432,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
         __threadfence_system();
         const uint32_t seq = *p.tp.seq;
         const size_t f = (size_t)(seq & 1u) * p.tp.world + p.tp.rank;
-        for (int r = 0; r < p.tp.world; ++r)
-          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.tp.flags[r] + f), "r"(seq) : "memory");
+        for (int r = 0; r < p.tp.world; ++r)  // ordered by the fence above: one fence, `world` plain stores
+          asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p.tp.flags[r] + f), "r"(seq) : "memory");
       }
     }
   }

@@ -318,9 +318,10 @@ __global__ void __launch_bounds__(1024) tp_push_kernel(const float* __restrict__
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const size_t f = (size_t)(seq & 1u) * tp.world + tp.rank;
     for (int r = 0; r < tp.world; ++r)
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(tp.flags[r] + f), "r"(seq) : "memory");
+      asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(tp.flags[r] + f), "r"(seq) : "memory");
   }
 }
 
@@ -403,9 +404,9 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
         const uint32_t seq = *tp.seq;
         const size_t f = (size_t)(seq & 1u) * tp.world;
         for (int r = 0; r < tp.world; ++r) tp.argv[r][f + tp.rank] = make_float2(v, __int_as_float(idx));
-        __threadfence_system();
+        __threadfence_system();  // orders the argv stores before the flags: one fence, `world` plain stores
         for (int r = 0; r < tp.world; ++r)
-          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(tp.aflag[r] + f + tp.rank), "r"(seq) : "memory");
+          asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(tp.aflag[r] + f + tp.rank), "r"(seq) : "memory");
         float bv2 = -INFINITY;
         int bi2 = 0x7fffffff;
         for (int r = 0; r < tp.world; ++r) {

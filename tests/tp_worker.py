@@ -18,8 +18,8 @@ import synth  # noqa: E402
 import tp  # noqa: E402
 
 CONFIGS = {
-    # small enough for a test, every split 256-column aligned for 2 / 4 / 8 ranks
-    "small": synth.LlamaConfig(n_layers=2, dim=1024, hidden=4096, n_heads=16, n_kv_heads=8, vocab=4096, max_seq=64),
+    # small enough for a test; every split is whole 256-column blocks for 2 / 4 / 8 ranks
+    "small": synth.LlamaConfig(n_layers=2, dim=2048, hidden=4096, n_heads=16, n_kv_heads=8, vocab=4096, max_seq=64),
     "llama70b": synth.LLAMA3_70B,
 }
 
