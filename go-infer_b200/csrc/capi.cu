@@ -839,6 +839,7 @@ int gi_cuda_tp_connect(int rank, int world, const void* handles) {
   }
   d.seq = reinterpret_cast<uint32_t*>(g_tp.region + L.seq);
   d.done = reinterpret_cast<unsigned*>(g_tp.region + L.done);
+  d.rdone = reinterpret_cast<unsigned*>(g_tp.region + L.rdone);
   g_tp.dev = d;
   g_tp.rank = rank;
   g_tp.connected = true;

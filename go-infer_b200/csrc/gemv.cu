@@ -60,8 +60,9 @@ namespace q4k {
 // and a unit's total leaves the integer domain once, through 4 int->float
 // conversions per lane.  The 6-bit mins ride on one fp16 MMA against the
 // per-sub-block activation sums (hi+lo fp16 split).
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+// Warps per CTA, W: 16 when each CTA has enough units to keep them busy
+// (more warps hide more of the per-warp dependency chains), else 8.
+constexpr int kWarpsSmall = 8, kWarpsLarge = 16;
 constexpr int kUnitX = 1104;       // staged activation bytes per unit (see stage_unit)
 constexpr int kStageBytes = 2304;  // qs: [16 rows][4 chunks, swizzled][32 B], headers: [16 rows][16 B]
 constexpr int kMaxCols = 45056;
@@ -175,7 +176,7 @@ GI_DEVINL float4 mul3(float4 a, float s, float4 w) {  // (a * s) * w, one roundi
 // (pkg/math/kernels.go:9-19: float32 sum of squares, scale
 // float32(1 / sqrt(float64(mean + eps))), out = x * scale * w), computed by
 // every CTA from the same data in the same order.
-template <bool F>
+template <int W, bool F>
 __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int j = lane >> 2, q = lane & 3;
@@ -186,7 +187,7 @@ __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
   if (F && p.xmode == kXNorm) {
     const float4* x4 = reinterpret_cast<const float4*>(x);
     float s = 0.f;
-    for (int i = threadIdx.x; i < nku * 64; i += kThreads) {
+    for (int i = threadIdx.x; i < nku * 64; i += W * 32) {
       const float4 v = __ldg(x4 + i);
       s = __fadd_rn(s, __fmul_rn(v.x, v.x));
       s = __fadd_rn(s, __fmul_rn(v.y, v.y));
@@ -198,15 +199,15 @@ __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
     __syncthreads();
     float tot = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) tot = __fadd_rn(tot, red[w]);
+    for (int w = 0; w < W; ++w) tot = __fadd_rn(tot, red[w]);
     const float mean = __fdiv_rn(tot, (float)(nku * 256));
     scale = (float)(1.0 / sqrt((double)__fadd_rn(mean, p.eps)));
   }
-  for (int u0 = warp; u0 < nku; u0 += 4 * kWarps) {
+  for (int u0 = warp; u0 < nku; u0 += 4 * W) {
     float4 a[4], b[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int u = u0 + k * kWarps;
+      const int u = u0 + k * W;
       if (u < nku) {
         a[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off));
         b[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off + 4));
@@ -218,7 +219,7 @@ __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int u = u0 + k * kWarps;
+      const int u = u0 + k * W;
       if (u < nku) stage_unit(xs + u * kUnitX, a[k], b[k], lane);
     }
   }
@@ -297,8 +298,9 @@ GI_DEVINL void compute_unit(uint32_t stage, uint32_t xu, int g, int t, uint32_t 
 
 // F: the decode-step fusions (RMSNorm staging, residual / SwiGLU / push
 // epilogues) are compiled in; without them the kernel is the plain GEMV.
-template <int S, bool F>
-__global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
+template <int W, int S, bool F>
+__global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_kernel(const Params p) {
+  constexpr int kWarps = W, kThreads = W * 32;
   extern __shared__ __align__(16) uint8_t smem[];
   griddep_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -353,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
   for (int s = 0; s < S; ++s) request(s);
   griddep_wait();
   // ends with a CTA barrier (also orders the slot zeroing)
-  stage_x<F>(xs, reinterpret_cast<float*>(smem + p.red_off), p);
+  stage_x<W, F>(xs, reinterpret_cast<float*>(smem + p.red_off), p);
 
   const uint32_t sh8 = 8u * (uint32_t)t;
   // Limb weights 256^(3-n) of this lane's two columns, divided by the 16
@@ -440,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_q4k_kernel(const Params p) {
 }
 
 struct Layout {
-  int ctas, ntiles, stages, x_off, slot_off, red_off, smem;
+  int warps, ctas, ntiles, stages, x_off, slot_off, red_off, smem;
 };
 
 Layout layout(int64_t ntiles, int64_t cols, const GemvLaunch& L, int gran = 1) {
@@ -450,16 +452,27 @@ Layout layout(int64_t ntiles, int64_t cols, const GemvLaunch& L, int gran = 1) {
   const int nun = o.ntiles / gran;
   o.ctas = nun < L.sm_count ? nun : L.sm_count;
   const int max_tiles = gran * ((nun + o.ctas - 1) / o.ctas);
+  // 16 warps when the CTAs are fewer than the SMs or hold 64+ units on
+  // average; below that the extra warps would idle (measured on B200:
+  // 16 warps gain 7-19 % on 4096-28672-column layers and lose 5-17 % on the
+  // 1024-3584-column row splits of a tensor-parallel shard).
+  bool large = o.ctas < L.sm_count || (long long)o.ntiles * nku >= 64LL * o.ctas;
   const int xbytes = nku * kUnitX;
-  const int slot_bytes = max_tiles * kWarps * 16 * 4;
-  const int fixed = xbytes + slot_bytes + 4 * kWarps;
-  // As many stages as fit next to a co-resident CTA, at least 2.
-  o.stages = 4;
-  while (o.stages > 2 && fixed + kWarps * o.stages * kStageBytes > kCoresidentSmem) --o.stages;
-  o.x_off = kWarps * o.stages * kStageBytes;
+  // 16 warps need 2 x 16 ring stages next to the staged activations: for
+  // the longest rows that does not fit, and 8 warps are used.
+  if (large && xbytes + max_tiles * kWarpsLarge * 64 + 4 * kWarpsLarge + kWarpsLarge * 2 * kStageBytes > kSmemMax)
+    large = false;
+  o.warps = large ? kWarpsLarge : kWarpsSmall;
+  const int slot_bytes = max_tiles * o.warps * 16 * 4;
+  const int fixed = xbytes + slot_bytes + 4 * o.warps;
+  // As many stages as fit next to a co-resident CTA (8 warps: up to 4; 16
+  // warps: up to 3), at least 2.
+  o.stages = large ? 3 : 4;
+  while (o.stages > 2 && fixed + o.warps * o.stages * kStageBytes > kCoresidentSmem) --o.stages;
+  o.x_off = o.warps * o.stages * kStageBytes;
   o.slot_off = o.x_off + xbytes;
-  o.red_off = o.slot_off + slot_bytes;  // RMSNorm reduction (kWarps floats)
-  o.smem = o.red_off + 4 * kWarps;
+  o.red_off = o.slot_off + slot_bytes;  // RMSNorm reduction (one float per warp)
+  o.smem = o.red_off + 4 * o.warps;
   return o;
 }
 
@@ -498,7 +511,7 @@ int launch(int nmat, float* const* y, const float* x, const void* const* w, cons
   p.red_off = o.red_off;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(o.ctas);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(o.warps * 32);
   cfg.dynamicSmemBytes = o.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -508,30 +521,43 @@ int launch(int nmat, float* const* y, const float* x, const void* const* w, cons
   cfg.numAttrs = L.pdl ? 1 : 0;
   cudaError_t e;
   const bool fused = f.xmode != kXPlain || f.ymode != kYStore;
-  switch (o.stages * 2 + (fused ? 1 : 0)) {  // tile counts past nmat equal the total: tile_of stays < nmat
-    case 8: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<4, false>, p); break;
-    case 9: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<4, true>, p); break;
-    case 6: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<3, false>, p); break;
-    case 7: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<3, true>, p); break;
-    case 5: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<2, true>, p); break;
-    default: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<2, false>, p); break;
+  // tile counts past nmat equal the total: tile_of stays < nmat
+  const int key = (o.warps == kWarpsLarge ? 100 : 0) + o.stages * 2 + (fused ? 1 : 0);
+  switch (key) {
+    case 8: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<kWarpsSmall, 4, false>, p); break;
+    case 9: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<kWarpsSmall, 4, true>, p); break;
+    case 6: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<kWarpsSmall, 3, false>, p); break;
+    case 7: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<kWarpsSmall, 3, true>, p); break;
+    case 4: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<kWarpsSmall, 2, false>, p); break;
+    case 5: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<kWarpsSmall, 2, true>, p); break;
+    case 106: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<kWarpsLarge, 3, false>, p); break;
+    case 107: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<kWarpsLarge, 3, true>, p); break;
+    case 104: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<kWarpsLarge, 2, false>, p); break;
+    case 105: e = cudaLaunchKernelEx(&cfg, gemv_q4k_kernel<kWarpsLarge, 2, true>, p); break;
+    default: return -4;
   }
   return e == cudaSuccess ? 0 : -5;
 }
 
-template <int S, bool F>
+template <int W, int S, bool F>
 cudaError_t prepare_one() {
-  cudaError_t e = cudaFuncSetAttribute(gemv_q4k_kernel<S, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
-  return e == cudaSuccess ? set_max_shared_carveout(gemv_q4k_kernel<S, F>) : e;
+  cudaError_t e =
+      cudaFuncSetAttribute(gemv_q4k_kernel<W, S, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  return e == cudaSuccess ? set_max_shared_carveout(gemv_q4k_kernel<W, S, F>) : e;
+}
+
+template <int W, int S>
+cudaError_t prepare_both() {
+  cudaError_t e = prepare_one<W, S, false>();
+  return e == cudaSuccess ? prepare_one<W, S, true>() : e;
 }
 
 int prepare() {
-  cudaError_t e = prepare_one<4, false>();
-  if (e == cudaSuccess) e = prepare_one<4, true>();
-  if (e == cudaSuccess) e = prepare_one<3, false>();
-  if (e == cudaSuccess) e = prepare_one<3, true>();
-  if (e == cudaSuccess) e = prepare_one<2, false>();
-  if (e == cudaSuccess) e = prepare_one<2, true>();
+  cudaError_t e = prepare_both<kWarpsSmall, 4>();
+  if (e == cudaSuccess) e = prepare_both<kWarpsSmall, 3>();
+  if (e == cudaSuccess) e = prepare_both<kWarpsSmall, 2>();
+  if (e == cudaSuccess) e = prepare_both<kWarpsLarge, 3>();
+  if (e == cudaSuccess) e = prepare_both<kWarpsLarge, 2>();
   return e == cudaSuccess ? 0 : -5;
 }
 }  // namespace q4k

@@ -326,8 +326,12 @@ __global__ void __launch_bounds__(1024) tp_push_kernel(const float* __restrict__
 }
 
 // x += sum of the ranks' partials, in rank order (the same x on every rank),
-// once every rank's push of this exchange has landed; then seq += 1.
-__global__ void __launch_bounds__(1024) tp_reduce_kernel(float* __restrict__ x, int n, TpDev tp, int* error) {
+// once every rank's push of this exchange has landed; then seq += 1.  Each
+// CTA waits for the flags and sums its slice of x; the last CTA to finish
+// advances seq (no CTA reads seq after that: each read it at its start).
+constexpr int kReduceCtas = 32, kReduceThreads = 256;
+__global__ void __launch_bounds__(kReduceThreads) tp_reduce_kernel(float* __restrict__ x, int n, TpDev tp,
+                                                                   int* error) {
   __shared__ int ok;
   griddep_wait();
   griddep_launch_dependents();
@@ -341,14 +345,23 @@ __global__ void __launch_bounds__(1024) tp_reduce_kernel(float* __restrict__ x, 
   }
   __syncthreads();
   const float* rv = tp.recv[tp.rank] + (size_t)set * tp.world * tp.max_dim;
+  const int i0 = (int)((long long)n * blockIdx.x / gridDim.x), i1 = (int)((long long)n * (blockIdx.x + 1) / gridDim.x);
   if (ok)
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      float s = __ldcg(rv + i);
-      for (int r = 1; r < tp.world; ++r) s = __fadd_rn(s, __ldcg(rv + (size_t)r * tp.max_dim + i));
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+      float v[kTpMaxWorld];
+#pragma unroll
+      for (int r = 0; r < kTpMaxWorld; ++r) v[r] = r < tp.world ? __ldcg(rv + (size_t)r * tp.max_dim + i) : 0.f;
+      float s = v[0];
+#pragma unroll
+      for (int r = 1; r < kTpMaxWorld; ++r)
+        if (r < tp.world) s = __fadd_rn(s, v[r]);
       x[i] = __fadd_rn(x[i], s);
     }
   __syncthreads();
-  if (threadIdx.x == 0) *tp.seq = seq + 1;
+  if (threadIdx.x == 0 && atomicAdd(tp.rdone, 1u) == gridDim.x - 1) {
+    *tp.rdone = 0u;
+    *tp.seq = seq + 1;
+  }
 }
 
 // ---- greedy pick (forward.go:397-404: the first maximum wins) and the
@@ -574,7 +587,8 @@ int DecodeModel::project_partial(const MatRef& W, const float* in, int cols, cud
       rc = -5;
   }
   if (rc) return rc;
-  return launch(pdl, dim3(1), dim3(1024), 0, s, tp_reduce_kernel, x_, cfg_.dim, tp_, scratch_.error) == cudaSuccess
+  return launch(pdl, dim3(kReduceCtas), dim3(kReduceThreads), 0, s, tp_reduce_kernel, x_, cfg_.dim, tp_,
+                scratch_.error) == cudaSuccess
              ? 0
              : -5;
 }

@@ -11,6 +11,7 @@
 //   aflag [2 sets][world] uint32           sequence number of rank r's argv
 //   seq   uint32                           exchanges completed (same on every rank)
 //   done  uint32                           CTAs of a pushing GEMV finished
+//   rdone uint32                           CTAs of a reducing kernel finished
 // Exchange k uses set k & 1.  A rank can only be one exchange ahead of a
 // peer (exchange k needs every rank's push k), so by the time it writes set
 // k & 1 again every peer has finished reading it.  Flags start at
@@ -32,11 +33,12 @@ struct TpDev {
   uint32_t* aflag[kTpMaxWorld] = {};
   uint32_t* seq = nullptr;  // this rank's copy
   unsigned* done = nullptr;
+  unsigned* rdone = nullptr;
 };
 
 // Byte layout of one region.
 struct TpLayout {
-  size_t recv, flags, argv, aflag, seq, done, total;
+  size_t recv, flags, argv, aflag, seq, done, rdone, total;
 };
 
 inline TpLayout tp_layout(int world, int max_dim) {
@@ -48,7 +50,8 @@ inline TpLayout tp_layout(int world, int max_dim) {
   L.aflag = up(L.argv + 8 * 2 * (size_t)world);
   L.seq = up(L.aflag + sizeof(uint32_t) * 2 * world);
   L.done = L.seq + 128;
-  L.total = up(L.done + 128);
+  L.rdone = L.done + 128;
+  L.total = up(L.rdone + 128);
   return L;
 }
 
