@@ -291,16 +291,20 @@ GI_DEVINL uint64_t now_ns() {
   return t;
 }
 // Wait (at most 2 s) for a flag to read `want`; false when it never did, or
-// at once when an earlier wait has already failed (*error set), so that a
-// missing peer costs one timeout, not one per exchange.
+// soon when an earlier wait has already failed (*error set), so that a
+// missing peer costs one timeout, not one per exchange.  The error word is
+// mapped host memory, a PCIe round trip per read: it and the clock are
+// checked once every 256 polls of the flag.
 GI_DEVINL bool wait_flag(const uint32_t* f, uint32_t want, const int* error) {
   if (ld_acquire_sys(f) == want) return true;
   const uint64_t t0 = now_ns();
-  while (ld_acquire_sys(f) != want) {
-    if (*(volatile const int*)error) return false;
-    if (now_ns() - t0 > 2000000000ull) return false;
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_sys(f) == want) return true;
+    if ((i & 255u) == 0) {
+      if (*(volatile const int*)error) return false;
+      if (now_ns() - t0 > 2000000000ull) return false;
+    }
   }
-  return true;
 }
 
 // Push this rank's partial p[n] into slot `rank` of every rank's region and
