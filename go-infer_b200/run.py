@@ -55,12 +55,17 @@ def prefill(args) -> None:
     y = torch.empty(args.batch, args.rows, device="cuda")
     st = torch.cuda.Stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    def run():
+        G.gemm_dev(qt, y.data_ptr(), x.data_ptr(), wb.device_ptr, wb.nbytes, args.batch, args.rows, args.cols,
+                   st.cuda_stream)
+
     try:
+        run()  # the first call sizes the library's workspace
+        st.synchronize()
         with torch.cuda.stream(st):
             e0.record()
             for _ in range(args.reps):
-                G.gemm_dev(qt, y.data_ptr(), x.data_ptr(), wb.device_ptr, wb.nbytes, args.batch, args.rows,
-                           args.cols, st.cuda_stream)
+                run()
             e1.record()
         e1.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / args.reps
