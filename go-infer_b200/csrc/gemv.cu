@@ -227,62 +227,68 @@ __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
 }
 
 // One unit: rows g and g+8 of a 16-row tile, 256 columns.  stage: the raw
-// super-blocks in shared memory; xu: the unit's staged activations.
-GI_DEVINL void compute_unit(uint32_t stage, uint32_t xu, int g, int t, uint32_t sh8, float W0, float W1,
-                            float& yA, float& yB) {
+// super-blocks in shared memory; xu: the unit's staged activations; xl: this
+// lane's B fragment in them (limb g of sub-block 0, or for g >= 4 limb g-4
+// of sub-block 1).
+//
+// Each 64-column chunk c takes two MMAs with the same B: its columns 0-3
+// hold the limbs of sub-block 2c (the low nibbles' activations), columns 4-7
+// those of sub-block 2c+1 (the high nibbles').  MMA L multiplies the low
+// nibbles alone, MMA F the whole bytes (q_lo + 16 q_hi): columns 0-3 of L
+// are the low-nibble products, columns 4-7 of F - L are 16 x the
+// high-nibble products.  Lanes t = 0, 1 hold columns 0-3 and lanes 2, 3
+// columns 4-7; each scales its accumulators by its sub-block's scale, so the
+// integer sums stay exact and every column of both MMAs is used.
+GI_DEVINL void compute_unit(uint32_t stage, uint32_t xu, uint32_t xl, int g, int t, uint32_t sh8, uint32_t selE,
+                            uint32_t selO, float W0, float W1, float& yA, float& yB) {
   const uint4 hA = lds128(stage + 2048 + g * 16);
   const uint4 hB = lds128(stage + 2048 + (g + 8) * 16);
   // 6-bit scales sc0..sc7 as bytes (getScaleMin, pkg/quant/quant.go:228-235)
   const uint32_t sA03 = hA.y & 0x3F3F3F3Fu, sB03 = hB.y & 0x3F3F3F3Fu;
   const uint32_t sA47 = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
   const uint32_t sB47 = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
-  int loA0 = 0, loA1 = 0, loB0 = 0, loB1 = 0, hiA0 = 0, hiA1 = 0, hiB0 = 0, hiB1 = 0;
+  int lA0 = 0, lA1 = 0, lB0 = 0, lB1 = 0, fA0 = 0, fA1 = 0, fB0 = 0, fB1 = 0;
   const uint32_t rowA = stage + g * 128 + 8 * t, rowB = rowA + 8 * 128;
-  const uint32_t xb = xu + g * 32 + 8 * t;  // this lane's limb (g < 4) at sub-block 0
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const uint32_t off = 32u * ((uint32_t)c ^ (uint32_t)(g & 3));
     const uint64_t qa = lds64(rowA + off), qb = lds64(rowB + off);
+    const uint64_t xv = lds64(xl + (2 * c) * 128);
     const uint32_t a0 = (uint32_t)qa, a1 = (uint32_t)(qa >> 32);
     const uint32_t b0 = (uint32_t)qb, b1 = (uint32_t)(qb >> 32);
-    uint64_t xl = 0, xh = 0;
-    if (g < 4) {
-      xl = lds64(xb + (2 * c) * 128);
-      xh = lds64(xb + (2 * c + 1) * 128);
-    }
-    int dl[4] = {0, 0, 0, 0}, dh[4] = {0, 0, 0, 0};
-    imma_16832(dl, a0 & 0x0F0F0F0Fu, b0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, b1 & 0x0F0F0F0Fu, (uint32_t)xl,
-               (uint32_t)(xl >> 32));
-    imma_16832(dh, a0 & 0xF0F0F0F0u, b0 & 0xF0F0F0F0u, a1 & 0xF0F0F0F0u, b1 & 0xF0F0F0F0u, (uint32_t)xh,
-               (uint32_t)(xh >> 32));
-    const uint32_t scA = c < 2 ? sA03 : sA47, scB = c < 2 ? sB03 : sB47;
-    const int kl = (2 * c) & 3, kh = (2 * c + 1) & 3;
-    const int slA = (int)((scA >> (8 * kl)) & 0xFFu), shA = (int)((scA >> (8 * kh)) & 0xFFu);
-    const int slB = (int)((scB >> (8 * kl)) & 0xFFu), shB = (int)((scB >> (8 * kh)) & 0xFFu);
-    loA0 += dl[0] * slA;
-    loA1 += dl[1] * slA;
-    loB0 += dl[2] * slB;
-    loB1 += dl[3] * slB;
-    hiA0 += dh[0] * shA;
-    hiA1 += dh[1] * shA;
-    hiB0 += dh[2] * shB;
-    hiB1 += dh[3] * shB;
+    int dl[4] = {0, 0, 0, 0}, df[4] = {0, 0, 0, 0};
+    imma_16832(dl, a0 & 0x0F0F0F0Fu, b0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, b1 & 0x0F0F0F0Fu, (uint32_t)xv,
+               (uint32_t)(xv >> 32));
+    imma_16832(df, a0, b0, a1, b1, (uint32_t)xv, (uint32_t)(xv >> 32));
+    // this lane's sub-block scale: byte (2c & 3) + (t >= 2) of the word
+    const uint32_t sel = (c & 1) ? selO : selE;
+    const int sA = (int)prmt(c < 2 ? sA03 : sA47, 0u, sel), sB = (int)prmt(c < 2 ? sB03 : sB47, 0u, sel);
+    lA0 += dl[0] * sA;
+    lA1 += dl[1] * sA;
+    lB0 += dl[2] * sB;
+    lB1 += dl[3] * sB;
+    fA0 += df[0] * sA;
+    fA1 += df[1] * sA;
+    fB0 += df[2] * sB;
+    fB1 += df[3] * sB;
   }
   // Mins: A = m_t, m_{t+4} (duplicated for the hi/lo halves of X), B col 4.
   const uint32_t zA = hA.z >> sh8, wA = hA.w >> sh8, zB = hB.z >> sh8, wB = hB.w >> sh8;
   const uint32_t mA0 = zA & 63u, mA4 = ((wA >> 4) & 0xFu) | ((zA >> 2) & 0x30u);
   const uint32_t mB0 = zB & 63u, mB4 = ((wB >> 4) & 0xFu) | ((zB >> 2) & 0x30u);
-  const uint32_t fA0 = hsub2_u32((mA0 * 0x10001u) | kMagic, kMagic);
-  const uint32_t fA4 = hsub2_u32((mA4 * 0x10001u) | kMagic, kMagic);
-  const uint32_t fB0 = hsub2_u32((mB0 * 0x10001u) | kMagic, kMagic);
-  const uint32_t fB4 = hsub2_u32((mB4 * 0x10001u) | kMagic, kMagic);
+  const uint32_t gA0 = hsub2_u32((mA0 * 0x10001u) | kMagic, kMagic);
+  const uint32_t gA4 = hsub2_u32((mA4 * 0x10001u) | kMagic, kMagic);
+  const uint32_t gB0 = hsub2_u32((mB0 * 0x10001u) | kMagic, kMagic);
+  const uint32_t gB4 = hsub2_u32((mB4 * 0x10001u) | kMagic, kMagic);
   uint64_t bm = 0;
   if (g == 4) bm = lds64(xu + 1024 + 8 * t);
   float cm[4] = {0.f, 0.f, 0.f, 0.f};
-  mma_16816(cm, fA0, fB0, fA4, fB4, (uint32_t)bm, (uint32_t)(bm >> 32));
-  // The high nibbles entered the MMA as 16*q.
-  const int iA0 = loA0 * 16 + hiA0, iA1 = loA1 * 16 + hiA1;
-  const int iB0 = loB0 * 16 + hiB0, iB1 = loB1 * 16 + hiB1;
+  mma_16816(cm, gA0, gB0, gA4, gB4, (uint32_t)bm, (uint32_t)(bm >> 32));
+  // lanes 0, 1: the low-nibble sums; lanes 2, 3: F - L, the high-nibble
+  // sums times 16 (W0, W1 divide it out)
+  const bool hi = t >= 2;
+  const int iA0 = hi ? fA0 - lA0 : lA0, iA1 = hi ? fA1 - lA1 : lA1;
+  const int iB0 = hi ? fB0 - lB0 : lB0, iB1 = hi ? fB1 - lB1 : lB1;
   // Scale factors multiply in an order that keeps every intermediate a
   // normal float (2^-e alone can be as small as 2^-126).
   const uint64_t inv = lds64(xu + 1088);
@@ -319,34 +325,45 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
 
   // Warp w takes the CTA's units w, w + kWarps, ...: at any moment the warps
   // stream neighbouring super-blocks of the same 16 rows (one long run of
-  // bytes per row), which keeps DRAM pages open.
-  int ltile = warp / p.nku, lku = warp - (warp / p.nku) * p.nku;  // next unit to request
+  // bytes per row), which keeps DRAM pages open.  Request cursor: unit
+  // `next` = (tile ltile, column block lku); pa, pb: its super-blocks in
+  // rows g and g + 8, advanced in place while the tile stays the same.
+  int ltile = warp / p.nku, lku = warp - ltile * p.nku;
   int next = warp;
-  const uint32_t swz = 32u * ((uint32_t)t ^ (uint32_t)(g & 3));  // where this lane's chunk t lands
-  auto advance = [&](int& tile, int& ku) {
-    ku += kWarps;
-    while (ku >= p.nku) {
-      ku -= p.nku;
-      ++tile;
-    }
+  const uint8_t* pa = nullptr;
+  const uint8_t* pb = nullptr;
+  auto seek = [&]() {
+    int m, lt;
+    tile_of<F>(p, T0 + ltile, m, lt);
+    const int r0 = lt * 16, rl = p.rows[m] - 1;
+    pa = p.w[m] + (long long)min(r0 + g, rl) * p.rowb + lku * 144;
+    pb = p.w[m] + (long long)min(r0 + g + 8, rl) * p.rowb + lku * 144;
   };
+  if (next < n) seek();
+  // this lane's destinations in a stage: chunk t of rows g, g + 8 (swizzled)
+  // and, for t < 2, the header of row g + 8t
+  const uint32_t dst = ring + g * 128 + 32u * ((uint32_t)t ^ (uint32_t)(g & 3));
+  const uint32_t dsth = ring + 2048 + (g + 8 * (t & 1)) * 16;
   auto request = [&](int stage) {  // always commits one group (possibly empty)
     if (next < n) {
-      int m, lt;
-      tile_of<F>(p, T0 + ltile, m, lt);
-      const int r0 = lt * 16, rl = p.rows[m] - 1;
-      const int rA = min(r0 + g, rl);
-      const int rB = min(r0 + g + 8, rl);
-      const uint8_t* a = p.w[m] + (long long)rA * p.rowb + lku * 144;
-      const uint8_t* b = p.w[m] + (long long)rB * p.rowb + lku * 144;
-      const uint32_t base = ring + stage * kStageBytes;
-      cp_async16_hint(base + g * 128 + swz, a + 16 + 32 * t, pol);
-      cp_async16_hint(base + g * 128 + swz + 16, a + 32 + 32 * t, pol);
-      cp_async16_hint(base + (g + 8) * 128 + swz, b + 16 + 32 * t, pol);
-      cp_async16_hint(base + (g + 8) * 128 + swz + 16, b + 32 + 32 * t, pol);
-      if (t < 2) cp_async16_hint(base + 2048 + (g + 8 * t) * 16, t ? b : a, pol);
-      advance(ltile, lku);
+      const uint32_t o = (uint32_t)stage * kStageBytes;
+      cp_async16_hint(dst + o, pa + 16 + 32 * t, pol);
+      cp_async16_hint(dst + o + 16, pa + 32 + 32 * t, pol);
+      cp_async16_hint(dst + o + 1024, pb + 16 + 32 * t, pol);
+      cp_async16_hint(dst + o + 1040, pb + 32 + 32 * t, pol);
+      if (t < 2) cp_async16_hint(dsth + o, t ? pb : pa, pol);
       next += kWarps;
+      lku += kWarps;
+      if (lku < p.nku) {
+        pa += kWarps * 144;
+        pb += kWarps * 144;
+      } else {
+        do {
+          lku -= p.nku;
+          ++ltile;
+        } while (lku >= p.nku);
+        if (next < n) seek();
+      }
     }
     cp_async_commit();
   };
@@ -358,22 +375,35 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
   stage_x<W, F>(xs, reinterpret_cast<float*>(smem + p.red_off), p);
 
   const uint32_t sh8 = 8u * (uint32_t)t;
-  // Limb weights 256^(3-n) of this lane's two columns, divided by the 16
-  // the high nibbles (and so the combined sums) carry.
-  const float W0 = t == 0 ? 1048576.f : (t == 1 ? 16.f : 0.f);
-  const float W1 = t == 0 ? 4096.f : (t == 1 ? 0.0625f : 0.f);
-  int ctile = warp / p.nku, cku = warp - (warp / p.nku) * p.nku;
+  // byte selectors of this lane's sub-block scale (even / odd chunk c)
+  const uint32_t selE = 0x4440u | (t >= 2 ? 1u : 0u), selO = 0x4440u | (t >= 2 ? 3u : 2u);
+  // Limb weights 256^(3-n) of this lane's two columns (lanes 2, 3: divided
+  // by the 16 their high-nibble sums carry).
+  const float W0 = t == 0 ? 16777216.f : (t == 1 ? 256.f : (t == 2 ? 1048576.f : 16.f));
+  const float W1 = t == 0 ? 65536.f : (t == 1 ? 1.f : (t == 2 ? 4096.f : 0.0625f));
+  const uint32_t xlo = (uint32_t)((g & 3) * 32 + 8 * t + (g >= 4 ? 128 : 0));
+  int ctile = warp / p.nku, cku = warp - ctile * p.nku;
+  uint32_t cx = xs_s + cku * kUnitX;  // the computed unit's staged activations
   float yA = 0.f, yB = 0.f;
   int stage = 0;
   for (int i = warp; i < n; i += kWarps) {
     cp_async_wait<S - 1>();
     __syncwarp();
-    compute_unit(ring + stage * kStageBytes, xs_s + cku * kUnitX, g, t, sh8, W0, W1, yA, yB);
+    compute_unit(ring + stage * kStageBytes, cx, cx + xlo, g, t, sh8, selE, selO, W0, W1, yA, yB);
     __syncwarp();
     request(stage);
     stage = stage + 1 == S ? 0 : stage + 1;
     const int tile = ctile;
-    advance(ctile, cku);
+    cku += kWarps;
+    if (cku < p.nku) {
+      cx += kWarps * kUnitX;
+    } else {
+      do {
+        cku -= p.nku;
+        ++ctile;
+      } while (cku >= p.nku);
+      cx = xs_s + cku * kUnitX;
+    }
     if (ctile != tile || i + kWarps >= n) {  // this warp is done with `tile`
       float vA = yA + __shfl_xor_sync(0xffffffffu, yA, 1);
       float vB = yB + __shfl_xor_sync(0xffffffffu, yB, 1);
