@@ -802,6 +802,8 @@ int gi_cuda_tp_prepare(int world, uint32_t max_dim, void* handle_out) {
   // flags start at 0xffffffff: no sequence number matches them
   GI_CUDA_TRY(cudaMemset(g_tp.region + L.flags, 0xFF, sizeof(uint32_t) * 2 * world), "init flags");
   GI_CUDA_TRY(cudaMemset(g_tp.region + L.aflag, 0xFF, sizeof(uint32_t) * 2 * world), "init flags");
+  // tags start at 0xffffffff too
+  GI_CUDA_TRY(cudaMemset(g_tp.region + L.ll, 0xFF, sizeof(unsigned long long) * 2 * world * max_dim), "init tags");
   GI_CUDA_TRY(cudaDeviceSynchronize(), "exchange region");
   cudaIpcMemHandle_t hnd;
   GI_CUDA_TRY(cudaIpcGetMemHandle(&hnd, g_tp.region), "cudaIpcGetMemHandle");
@@ -836,6 +838,7 @@ int gi_cuda_tp_connect(int rank, int world, const void* handles) {
     d.flags[r] = reinterpret_cast<uint32_t*>(base + L.flags);
     d.argv[r] = reinterpret_cast<float2*>(base + L.argv);
     d.aflag[r] = reinterpret_cast<uint32_t*>(base + L.aflag);
+    d.ll[r] = reinterpret_cast<unsigned long long*>(base + L.ll);
   }
   d.seq = reinterpret_cast<uint32_t*>(g_tp.region + L.seq);
   d.done = reinterpret_cast<unsigned*>(g_tp.region + L.done);

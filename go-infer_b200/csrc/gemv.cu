@@ -440,10 +440,10 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
           p.y[0][row] = __fmul_rn(silu, up);
         }
       } else if (F && p.ymode == kYPush) {
-        if (row < p.rows[m]) {  // this rank's partial into slot `rank` of every rank's region
-          const uint32_t set = *p.tp.seq & 1u;
-          const size_t off = ((size_t)set * p.tp.world + p.tp.rank) * p.tp.max_dim + row;
-          for (int r = 0; r < p.tp.world; ++r) p.tp.recv[r][off] = sum;
+        if (row < p.rows[m]) {  // this rank's tagged partial into slot `rank` of every rank's region
+          const uint32_t seq = *p.tp.seq;
+          const size_t off = ((size_t)(seq & 1u) * p.tp.world + p.tp.rank) * p.tp.max_dim + row;
+          for (int r = 0; r < p.tp.world; ++r) st_ll(p.tp.ll[r] + off, sum, seq);
         }
       } else if (row < p.rows[m]) {
         p.y[m][row] = (F && p.ymode == kYAdd) ? __fadd_rn(p.y[m][row], sum) : sum;  // residual: y += W x
@@ -451,21 +451,36 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
     }
   }
   if (F && p.ymode == kYPush) {
-    // The last CTA to finish publishes the push: flag[rank] = seq on every
-    // rank.  Each CTA orders its stores before its count (GPU scope); the
-    // last one, having observed every count, fences at system scope and
-    // releases the flags, which carries all CTAs' stores to the peers.
-    __threadfence();
+    // Every rank's CTA c computes and pushes the same tiles; this CTA waits
+    // for the tagged partials of its own rows from every rank and adds their
+    // rank-ordered sum into the residual p.y[0]: the same x on every rank.
+    // The last CTA to finish advances the exchange count (every CTA read it
+    // before counting itself).
+    const uint32_t seq = *p.tp.seq;
+    const int world = p.tp.world;
+    const unsigned long long* rv = p.tp.ll[p.tp.rank] + (size_t)(seq & 1u) * world * p.tp.max_dim;
+    for (int tl = warp; tl < ntl; tl += kWarps) {
+      const int row = (T0 + tl) * 16 + lane;
+      if (lane < 16 && row < p.rows[0]) {
+        float sum = 0.f;
+        bool ok = true;
+        for (int r = 0; r < world && ok; ++r) {
+          float v = 0.f;
+          ok = tp_wait_ll(rv + (size_t)r * p.tp.max_dim + row, seq, p.tp.error, &v);
+          sum = r == 0 ? v : __fadd_rn(sum, v);
+        }
+        if (ok)
+          p.y[0][row] = __fadd_rn(p.y[0][row], sum);
+        else
+          atomicExch(p.tp.error, 1);
+      }
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
-      const unsigned d = atomicAdd(p.tp.done, 1u);
-      if (d == gridDim.x - 1) {
+      __threadfence();
+      if (atomicAdd(p.tp.done, 1u) == gridDim.x - 1) {
         *p.tp.done = 0u;
-        __threadfence_system();
-        const uint32_t seq = *p.tp.seq;
-        const size_t f = (size_t)(seq & 1u) * p.tp.world + p.tp.rank;
-        for (int r = 0; r < p.tp.world; ++r)  // ordered by the fence above: one fence, `world` plain stores
-          asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p.tp.flags[r] + f), "r"(seq) : "memory");
+        *p.tp.seq = seq + 1;
       }
     }
   }
@@ -529,7 +544,8 @@ int launch(int nmat, float* const* y, const float* x, const void* const* w, cons
   p.xmode = f.xmode;
   p.ymode = f.ymode;
   if (f.ymode == kYPush) {
-    if (!f.tp || f.tp->world < 1 || rows[0] > f.tp->max_dim || nmat != 1) return -4;
+    if (!f.tp || f.tp->world < 1 || rows[0] > f.tp->max_dim || nmat != 1 || !f.tp->error)
+      return -4;
     p.tp = *f.tp;
   }
   p.rowb = row_bytes(kTypeQ4_K, cols);

@@ -27,7 +27,9 @@ struct GemvScratch {
 // Fusions of the Q4_K GEMV used by the decode step (internal).
 enum : int { kXPlain = 0, kXNorm = 1 };              // staged x, or RMSNorm(x) * x2 (weight)
 // y = Wx, y += Wx, silu(W0 x) * (W1 x), or (kYPush) Wx pushed as this
-// rank's partial into every rank's tensor-parallel exchange region.
+// rank's partial into every rank's tensor-parallel exchange region, then
+// y += the rank-ordered sum of all ranks' partials (tensor-parallel
+// all-reduce fused into the epilogue).
 enum : int { kYStore = 0, kYAdd = 1, kYSwiGLU = 2, kYPush = 3 };
 struct GemvFuse {
   int xmode = kXPlain;

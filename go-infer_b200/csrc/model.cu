@@ -280,31 +280,8 @@ __global__ void swiglu_kernel(float* __restrict__ gate, const float* __restrict_
 
 // ---- tensor-parallel exchange (TPCoordinator.AllReduce,
 // pkg/distributed/tensor_parallel.go:33-108) --------------------------------
-GI_DEVINL uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-GI_DEVINL uint64_t now_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// Wait (at most 2 s) for a flag to read `want`; false when it never did, or
-// soon when an earlier wait has already failed (*error set), so that a
-// missing peer costs one timeout, not one per exchange.  The error word is
-// mapped host memory, a PCIe round trip per read: it and the clock are
-// checked once every 256 polls of the flag.
 GI_DEVINL bool wait_flag(const uint32_t* f, uint32_t want, const int* error) {
-  if (ld_acquire_sys(f) == want) return true;
-  const uint64_t t0 = now_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (ld_acquire_sys(f) == want) return true;
-    if ((i & 255u) == 0) {
-      if (*(volatile const int*)error) return false;
-      if (now_ns() - t0 > 2000000000ull) return false;
-    }
-  }
+  return tp_wait_flag(f, want, error);
 }
 
 // Push this rank's partial p[n] into slot `rank` of every rank's region and
@@ -490,6 +467,7 @@ int DecodeModel::init(const ModelCfg& cfg, const LayerRef* layers, const MatRef&
   if (cfg.tp_world > 1) {
     if (!tp || tp->world != cfg.tp_world || tp->rank != cfg.tp_rank || tp->max_dim < cfg.dim) return -4;
     tp_ = *tp;
+    tp_.error = error_word;
   } else {
     tp_ = TpDev();
   }
@@ -574,22 +552,20 @@ int DecodeModel::project_partial(const MatRef& W, const float* in, int cols, cud
   GemvLaunch L;
   L.sm_count = sm_count_;
   L.pdl = pdl;
-  int rc = 0;
-  if (W.qtype == kTypeQ4_K) {
-    float* ys[1] = {proj_};
+  if (W.qtype == kTypeQ4_K) {  // push, wait and sum in the GEMV's epilogue: x += sum of the ranks' W x
+    float* ys[1] = {x_};
     const void* ws[1] = {W.w};
     const size_t wb[1] = {W.bytes};
     const int64_t rows[1] = {cfg_.dim};
     GemvFuse f;
     f.ymode = kYPush;
     f.tp = &tp_;
-    rc = gemv_q4k_fused(1, ys, in, ws, wb, rows, cols, f, L, s);
-  } else {
-    rc = gemv_launch(W.qtype, proj_, in, W.w, W.bytes, cfg_.dim, cols, scratch_, L, s);
-    if (!rc && launch(pdl, dim3(1), dim3(1024), 0, s, tp_push_kernel, (const float*)proj_, cfg_.dim, tp_) !=
-                   cudaSuccess)
-      rc = -5;
+    return gemv_q4k_fused(1, ys, in, ws, wb, rows, cols, f, L, s);
   }
+  int rc = gemv_launch(W.qtype, proj_, in, W.w, W.bytes, cfg_.dim, cols, scratch_, L, s);
+  if (!rc && launch(pdl, dim3(1), dim3(1024), 0, s, tp_push_kernel, (const float*)proj_, cfg_.dim, tp_) !=
+                 cudaSuccess)
+    rc = -5;
   if (rc) return rc;
   return launch(pdl, dim3(kReduceCtas), dim3(kReduceThreads), 0, s, tp_reduce_kernel, x_, cfg_.dim, tp_,
                 scratch_.error) == cudaSuccess

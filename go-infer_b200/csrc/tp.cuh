@@ -12,6 +12,11 @@
 //   seq   uint32                           exchanges completed (same on every rank)
 //   done  uint32                           CTAs of a pushing GEMV finished
 //   rdone uint32                           CTAs of a reducing kernel finished
+//   ll    [2 sets][world][max_dim] uint64  rank r's partial in slot r as
+//                                          (float bits | exchange number << 32):
+//                                          one 8-byte store carries value and
+//                                          tag, so a reader that sees the tag
+//                                          has the value (no fence, no flag)
 // Exchange k uses set k & 1.  A rank can only be one exchange ahead of a
 // peer (exchange k needs every rank's push k), so by the time it writes set
 // k & 1 again every peer has finished reading it.  Flags start at
@@ -34,11 +39,13 @@ struct TpDev {
   uint32_t* seq = nullptr;  // this rank's copy
   unsigned* done = nullptr;
   unsigned* rdone = nullptr;
+  unsigned long long* ll[kTpMaxWorld] = {};
+  int* error = nullptr;  // bounded waits that give up set it (mapped host word)
 };
 
 // Byte layout of one region.
 struct TpLayout {
-  size_t recv, flags, argv, aflag, seq, done, rdone, total;
+  size_t recv, flags, argv, aflag, seq, done, rdone, ll, total;
 };
 
 inline TpLayout tp_layout(int world, int max_dim) {
@@ -51,8 +58,68 @@ inline TpLayout tp_layout(int world, int max_dim) {
   L.seq = up(L.aflag + sizeof(uint32_t) * 2 * world);
   L.done = L.seq + 128;
   L.rdone = L.done + 128;
-  L.total = up(L.rdone + 128);
+  L.ll = up(L.rdone + 128);
+  L.total = up(L.ll + sizeof(unsigned long long) * 2 * (size_t)world * max_dim);
   return L;
 }
+
+#ifdef __CUDACC__
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait (at most 2 s) for a flag to read `want`; false when it never did, or
+// soon when an earlier wait has already failed (*error set), so that a
+// missing peer costs one timeout, not one per exchange.  The error word is
+// mapped host memory, a PCIe round trip per read: it and the clock are
+// checked once every 256 polls of the flag.
+__device__ __forceinline__ bool tp_wait_flag(const uint32_t* f, uint32_t want, const int* error) {
+  if (ld_acquire_sys(f) == want) return true;
+  const uint64_t t0 = now_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_sys(f) == want) return true;
+    if ((i & 255u) == 0) {
+      if (*(volatile const int*)error) return false;
+      if (now_ns() - t0 > 2000000000ull) return false;
+    }
+  }
+}
+// One tagged partial: 8-byte stores and loads are single-copy atomic.
+__device__ __forceinline__ void st_ll(unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_ll(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+// Wait (at most about 2 s; the error word and the clock are read every 256
+// polls) for a tagged partial; false when it never came.
+__device__ __forceinline__ bool tp_wait_ll(const unsigned long long* p, uint32_t tag, const int* error, float* v) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    const unsigned long long w = ld_ll(p);
+    if ((uint32_t)(w >> 32) == tag) {
+      *v = __uint_as_float((uint32_t)w);
+      return true;
+    }
+    if ((i & 255u) == 255u) {
+      if (*(volatile const int*)error) return false;
+      const uint64_t t = now_ns();
+      if (t0 == 0)
+        t0 = t;
+      else if (t - t0 > 2000000000ull)
+        return false;
+    }
+  }
+}
+#endif
 
 }  // namespace gi
