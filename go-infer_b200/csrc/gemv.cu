@@ -717,6 +717,120 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_q80_kernel(
     if (lane == 0 && r0 + i < rows) y[r0 + i] = v;
   }
 }
+
+// Ring variant for rows of whole 256-column groups (nb % 8 == 0, so every
+// row and every 32-block chunk starts on a 16-byte boundary): each warp owns
+// R rows and streams them chunk by chunk through a two-stage cp.async ring,
+// the first two chunks requested before the kernel waits on its
+// predecessor; the arithmetic is the staged kernel's.
+constexpr int kRingChunkBytes = kChunkBlocks * 34;  // 1088
+// Slot stride: lds_u32 reads the word after a misaligned offset, up to 4
+// bytes past the chunk, so every slot carries 16 bytes of padding.
+constexpr int kRingSlot = kRingChunkBytes + 16;
+template <int R>
+__global__ void __launch_bounds__(kWarps * 32) gemv_q80_ring_kernel(float* __restrict__ y, const float* __restrict__ x,
+                                                                    const uint8_t* __restrict__ w, long long rowb,
+                                                                    int rows, int nb) {
+  extern __shared__ __align__(16) uint8_t smem[];  // [warp][stage][R][kRingSlot]
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r0 = (blockIdx.x * kWarps + warp) * R;
+  const int nchunks = (nb + kChunkBlocks - 1) / kChunkBlocks;
+  uint8_t* ring = smem + (size_t)warp * 2 * R * kRingSlot;
+  const uint64_t pol = l2_evict_first_policy();
+  auto request = [&](int ch) {  // always commits one group (possibly empty)
+    if (ch < nchunks && r0 < rows) {
+      const int nvec = min(kChunkBlocks, nb - ch * kChunkBlocks) * 34 / 16;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const uint8_t* src = w + (long long)min(r0 + i, rows - 1) * rowb + (long long)ch * kRingChunkBytes;
+        const uint32_t dst = smem_u32(ring + ((ch & 1) * R + i) * kRingSlot);
+        for (int v = lane; v < nvec; v += 32) cp_async16_hint(dst + 16 * v, src + 16 * v, pol);
+      }
+    }
+    cp_async_commit();
+  };
+  request(0);
+  request(1);
+  griddep_wait();
+  if (r0 >= rows) return;  // nothing was requested
+  const int bq = lane >> 2, j = lane & 3;  // block within an 8-block group, quarter of it
+  float acc[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) acc[i] = 0.f;
+  for (int ch = 0; ch < nchunks; ++ch) {
+    cp_async_wait<1>();
+    __syncwarp();
+    const int c0 = ch * kChunkBlocks, nblk = min(kChunkBlocks, nb - c0);
+#pragma unroll
+    for (int sub = 0; sub < kChunkBlocks / 8; ++sub) {
+      const int bl = sub * 8 + bq;
+      if (bl < nblk) {
+        const float4* xp = reinterpret_cast<const float4*>(x + 32LL * (c0 + bl) + 8 * j);
+        const float4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+          const uint8_t* sb = ring + ((ch & 1) * R + i) * kRingSlot;
+          const uint32_t* sw = reinterpret_cast<const uint32_t*>(sb);
+          const int base = 34 * bl;
+          const float d = f16bits_to_f32(lds_u16(sb, base));
+          const uint32_t q0 = lds_u32(sw, base + 2 + 8 * j) ^ 0x80808080u;
+          const uint32_t q1 = lds_u32(sw, base + 6 + 8 * j) ^ 0x80808080u;
+          const float bias = 8388736.f;  // 2^23 + 128
+          float s = byte_as_float(q0, 0x7440u, bias) * x0.x;
+          s = fmaf(byte_as_float(q0, 0x7441u, bias), x0.y, s);
+          s = fmaf(byte_as_float(q0, 0x7442u, bias), x0.z, s);
+          s = fmaf(byte_as_float(q0, 0x7443u, bias), x0.w, s);
+          s = fmaf(byte_as_float(q1, 0x7440u, bias), x1.x, s);
+          s = fmaf(byte_as_float(q1, 0x7441u, bias), x1.y, s);
+          s = fmaf(byte_as_float(q1, 0x7442u, bias), x1.z, s);
+          s = fmaf(byte_as_float(q1, 0x7443u, bias), x1.w, s);
+          acc[i] = fmaf(s, d, acc[i]);
+        }
+      }
+    }
+    __syncwarp();
+    request(ch + 2);
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    const float v = warp_sum(acc[i]);
+    if (lane == 0 && r0 + i < rows) y[r0 + i] = v;
+  }
+}
+
+// R = 4 rows per warp, or 2 when 4 would leave SMs without a CTA.
+int launch_ring(float* y, const float* x, const uint8_t* w, int64_t rows, int64_t cols, const GemvLaunch& L,
+                cudaStream_t stream) {
+  const int per_cta4 = kWarps * 4;
+  const int R = (rows + per_cta4 - 1) / per_cta4 >= L.sm_count ? 4 : 2;
+  const int64_t ctas = (rows + (int64_t)kWarps * R - 1) / ((int64_t)kWarps * R);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = (size_t)kWarps * 2 * R * kRingSlot;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = L.pdl ? 1 : 0;
+  const long long rowb = (cols / 32) * 34;
+  const cudaError_t e = R == 4 ? cudaLaunchKernelEx(&cfg, gemv_q80_ring_kernel<4>, y, x, w, rowb, (int)rows,
+                                                    (int)(cols / 32))
+                               : cudaLaunchKernelEx(&cfg, gemv_q80_ring_kernel<2>, y, x, w, rowb, (int)rows,
+                                                    (int)(cols / 32));
+  return e == cudaSuccess ? 0 : -5;
+}
+
+int prepare_ring() {
+  const int smem4 = kWarps * 2 * 4 * kRingSlot;
+  if (cudaFuncSetAttribute(gemv_q80_ring_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem4) != cudaSuccess)
+    return -5;
+  if (set_max_shared_carveout(gemv_q80_ring_kernel<4>) != cudaSuccess) return -5;
+  return set_max_shared_carveout(gemv_q80_ring_kernel<2>) == cudaSuccess ? 0 : -5;
+}
 }  // namespace q80
 
 // ------------------------------- Q6_K ------------------------------------
@@ -798,11 +912,147 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_q6k_kernel(
     if (lane == 0 && r0 + i < rows) y[r0 + i] = v;
   }
 }
+
+// Ring variant for rows of whole 2048-column groups (nsb % 8 == 0, so rows
+// and 8-super-block chunks start on 16-byte boundaries): each warp owns R
+// rows and streams them through a two-stage cp.async ring, the first two
+// chunks requested before the kernel waits on its predecessor; the
+// arithmetic is the staged kernel's.
+constexpr int kRingSB = 8;
+constexpr int kRingChunkBytes = kRingSB * 210;  // 1680
+constexpr int kRingSlot = kRingChunkBytes + 16;  // padded like Q8_0's slots
+template <int R>
+__global__ void __launch_bounds__(kWarps * 32) gemv_q6k_ring_kernel(float* __restrict__ y, const float* __restrict__ x,
+                                                                    const uint8_t* __restrict__ w, long long rowb,
+                                                                    int rows, int nsb) {
+  extern __shared__ __align__(16) uint8_t smem[];  // [warp][stage][R][kRingSlot]
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r0 = (blockIdx.x * kWarps + warp) * R;
+  const int nchunks = (nsb + kRingSB - 1) / kRingSB;
+  uint8_t* ring = smem + (size_t)warp * 2 * R * kRingSlot;
+  const uint64_t pol = l2_evict_first_policy();
+  auto request = [&](int ch) {  // always commits one group (possibly empty)
+    if (ch < nchunks && r0 < rows) {
+      const int nvec = min(kRingSB, nsb - ch * kRingSB) * 210 / 16;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const uint8_t* src = w + (long long)min(r0 + i, rows - 1) * rowb + (long long)ch * kRingChunkBytes;
+        const uint32_t dst = smem_u32(ring + ((ch & 1) * R + i) * kRingSlot);
+        for (int v = lane; v < nvec; v += 32) cp_async16_hint(dst + 16 * v, src + 16 * v, pol);
+      }
+    }
+    cp_async_commit();
+  };
+  request(0);
+  request(1);
+  griddep_wait();
+  if (r0 >= rows) return;  // nothing was requested
+  const int q = lane >> 3, j = lane & 7;  // super-block within a 4-block group, l-quad 4j..4j+3
+  const uint32_t jsel = (uint32_t)(j >> 2);
+  float acc[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) acc[i] = 0.f;
+  for (int ch = 0; ch < nchunks; ++ch) {
+    cp_async_wait<1>();
+    __syncwarp();
+    const int s0 = ch * kRingSB, n8 = min(kRingSB, nsb - s0);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int sbk = q + 4 * half;
+      if (sbk < n8) {
+        const float* xb = x + 256LL * (s0 + sbk) + 4 * j;
+        float4 xv[2][4];
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) xv[n][k] = __ldg(reinterpret_cast<const float4*>(xb + 128 * n + 32 * k));
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+          const uint8_t* sb = ring + ((ch & 1) * R + i) * kRingSlot;
+          const uint32_t* sw = reinterpret_cast<const uint32_t*>(sb);
+          const int base = 210 * sbk;
+          const float d = f16bits_to_f32(lds_u16(sb, base + 208));
+          uint32_t S[4];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) S[m] = lds_u32(sw, base + 192 + 4 * m) ^ 0x80808080u;
+#pragma unroll
+          for (int n = 0; n < 2; ++n) {
+            const uint32_t L0 = lds_u32(sw, base + 64 * n + 4 * j);
+            const uint32_t L1 = lds_u32(sw, base + 64 * n + 32 + 4 * j);
+            const uint32_t Q = lds_u32(sw, base + 128 + 32 * n + 4 * j);
+            uint32_t V[4];
+            V[0] = (L0 & 0x0F0F0F0Fu) | ((Q << 4) & 0x30303030u);
+            V[1] = (L1 & 0x0F0F0F0Fu) | ((Q << 2) & 0x30303030u);
+            V[2] = ((L0 >> 4) & 0x0F0F0F0Fu) | (Q & 0x30303030u);
+            V[3] = ((L1 >> 4) & 0x0F0F0F0Fu) | ((Q >> 2) & 0x30303030u);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              // scale of sub-block 8n + 2k + (l/16), l = 4j..4j+3
+              const uint32_t scw = S[2 * n + (k >> 1)];
+              const float sc = byte_as_float(scw, 0x7440u + 2u * (k & 1) + jsel, 8388736.f);
+              const float ds = d * sc;  // (d * sc) as DequantizeQ6_K forms it
+              const float bias = 8388640.f;  // 2^23 + 32
+              float sum = byte_as_float(V[k], 0x7440u, bias) * xv[n][k].x;
+              sum = fmaf(byte_as_float(V[k], 0x7441u, bias), xv[n][k].y, sum);
+              sum = fmaf(byte_as_float(V[k], 0x7442u, bias), xv[n][k].z, sum);
+              sum = fmaf(byte_as_float(V[k], 0x7443u, bias), xv[n][k].w, sum);
+              acc[i] = fmaf(ds, sum, acc[i]);
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+    request(ch + 2);
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    const float v = warp_sum(acc[i]);
+    if (lane == 0 && r0 + i < rows) y[r0 + i] = v;
+  }
+}
+
+// R = 4 rows per warp, or 2 when 4 would leave SMs without a CTA.
+int launch_ring(float* y, const float* x, const uint8_t* w, int64_t rows, int64_t cols, const GemvLaunch& L,
+                cudaStream_t stream) {
+  const int R = (rows + kWarps * 4 - 1) / (kWarps * 4) >= L.sm_count ? 4 : 2;
+  const int64_t ctas = (rows + (int64_t)kWarps * R - 1) / ((int64_t)kWarps * R);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = (size_t)kWarps * 2 * R * kRingSlot;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = L.pdl ? 1 : 0;
+  const long long rowb = (cols / 256) * 210;
+  const cudaError_t e = R == 4 ? cudaLaunchKernelEx(&cfg, gemv_q6k_ring_kernel<4>, y, x, w, rowb, (int)rows,
+                                                    (int)(cols / 256))
+                               : cudaLaunchKernelEx(&cfg, gemv_q6k_ring_kernel<2>, y, x, w, rowb, (int)rows,
+                                                    (int)(cols / 256));
+  return e == cudaSuccess ? 0 : -5;
+}
+
+int prepare_ring() {
+  for (int R : {2, 4}) {
+    const int smem = kWarps * 2 * R * kRingSlot;
+    auto k = R == 4 ? gemv_q6k_ring_kernel<4> : gemv_q6k_ring_kernel<2>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -5;
+    if (set_max_shared_carveout(k) != cudaSuccess) return -5;
+  }
+  return 0;
+}
 }  // namespace q6k
 
 int gemv_prepare_device() {
   if (q4k::prepare() != 0) return -5;
   if (set_max_shared_carveout(q80::gemv_q80_kernel) != cudaSuccess) return -5;
+  if (q80::prepare_ring() != 0) return -5;
+  if (q6k::prepare_ring() != 0) return -5;
   if (set_max_shared_carveout(q6k::gemv_q6k_kernel) != cudaSuccess) return -5;
   return 0;
 }
@@ -888,9 +1138,11 @@ int gemv_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
       if ((reinterpret_cast<uintptr_t>(w) & 15) != 0) return -4;
       return q4k::launch(1, &y, x, &w, &rows, cols, L, stream);
     case kTypeQ8_0:
+      if (cols % 256 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) return q80::launch_ring(y, x, wb, rows, cols, L, stream);
       return launch_rowwarp(q80::gemv_q80_kernel, rows, L, stream, y, x, wb, wb + w_bytes,
                             (long long)rb, (int)rows, (int)(cols / 32));
     case kTypeQ6_K:
+      if (cols % 2048 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) return q6k::launch_ring(y, x, wb, rows, cols, L, stream);
       return launch_rowwarp(q6k::gemv_q6k_kernel, rows, L, stream, y, x, wb, wb + w_bytes,
                             (long long)rb, (int)rows, (int)(cols / 256));
     case kTypeF32: {
