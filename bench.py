@@ -449,7 +449,7 @@ def run_ours(args):
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": 4 * (GATE[1] + DOWN[1]),
                     "d2h_bytes_per_step": 4 * (2 * GATE[0] + DOWN[0]),
-                    "api": "gi_cuda_gemv_buf (host y/x, pinned)", "steps": e2e_steps},
+                    "api": "gi_cuda_gemv_buf (host y/x, pinned: x copied in, y stored by the kernel)", "steps": e2e_steps},
             "gpu_launches": 2 * args.steps,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),

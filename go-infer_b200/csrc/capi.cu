@@ -222,12 +222,26 @@ int run_host_io(int qtype, float* y, const float* x, const void* wdev, size_t w_
   const size_t xbytes = ((sizeof(float) * batch * cols) + 255) & ~(size_t)255;
   if ((rc = arena_alloc(xbytes + sizeof(float) * batch * rows, &xd))) return rc;
   yd = static_cast<uint8_t*>(xd) + xbytes;
+  // A y in page-locked host memory that the device can address (CUDA's
+  // unified addressing maps cudaHostAlloc'd buffers) is written by the
+  // kernel itself: no device-to-host copy.  Pageable y goes through the
+  // copy, as do calls inside a batch (their y is read at EndBatch).
+  float* ydirect = nullptr;
+  if (!g.batch) {
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, y) == cudaSuccess) {
+      if (pa.type == cudaMemoryTypeHost && pa.devicePointer) ydirect = static_cast<float*>(pa.devicePointer);
+    } else {
+      cudaGetLastError();
+    }
+  }
   GI_CUDA_TRY(cudaMemcpyAsync(xd, x, sizeof(float) * batch * cols, cudaMemcpyHostToDevice, g.stream),
               "copy x to device");
-  rc = run_dev(qtype, static_cast<float*>(yd), static_cast<const float*>(xd), wdev, w_bytes, batch,
-               rows, cols, g.stream, false);
+  rc = run_dev(qtype, ydirect ? ydirect : static_cast<float*>(yd), static_cast<const float*>(xd), wdev, w_bytes,
+               batch, rows, cols, g.stream, false);
   if (rc) return fail(rc, rc == -4 ? "unsupported shape or buffer too small" : "kernel launch failed",
                       rc == -5 ? cudaGetLastError() : cudaSuccess);
+  if (ydirect) return complete_locked();
   const size_t yb = sizeof(float) * batch * rows;
   if (g.batch) {
     size_t off;

@@ -109,8 +109,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "gi_cuda_end_batch": ([], None),
         "gi_cuda_create_buffer": ([vp, sz], vp),
         "gi_cuda_release_buffer": ([vp], None),
-        "gi_cuda_gemv_buf": ([i32, f32p, f32p, vp, u32, u32], i32),
-        "gi_cuda_gemm_buf": ([i32, f32p, f32p, vp, u32, u32, u32], i32),
+        "gi_cuda_gemv_buf": ([i32, vp, vp, vp, u32, u32], i32),
+        "gi_cuda_gemm_buf": ([i32, vp, vp, vp, u32, u32, u32], i32),
         "gi_cuda_gemv_q8_0": ([f32p, f32p, vp, u32, u32], i32),
         "gi_cuda_gemv_q4_k": ([f32p, f32p, vp, u32, u32], i32),
         "gi_cuda_gemv_q6_k": ([f32p, f32p, vp, u32, u32], i32),
@@ -164,6 +164,14 @@ def _f32(a: np.ndarray):
     if a.dtype != np.float32 or not a.flags.c_contiguous:
         raise TypeError("expected a C-contiguous float32 array")
     return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+def _f32_addr(a: np.ndarray) -> int:
+    """Address of a C-contiguous float32 array (the per-call hot path: no
+    ctypes pointer object is built)."""
+    if a.dtype != np.float32 or not a.flags.c_contiguous:
+        raise TypeError("expected a C-contiguous float32 array")
+    return a.__array_interface__["data"][0]
 
 
 def _bytes_ptr(raw) -> tuple[ctypes.c_void_p, int, object]:
@@ -232,7 +240,9 @@ def MatMulBuf(quant_type: int, y: np.ndarray, x: np.ndarray, buf: Buffer, rows: 
     """metal.MatMulBuf (metal_darwin.go:525): y[:rows] = W x."""
     if buf is None or y.size < rows or x.size < cols:
         raise GoInferCudaError("gi_cuda_gemv_buf", ERR_UNAVAILABLE, "bad arguments")
-    _err("gi_cuda_gemv_buf", load_library().gi_cuda_gemv_buf(quant_type, _f32(y), _f32(x), buf.handle, rows, cols))
+    rc = (_lib or load_library()).gi_cuda_gemv_buf(quant_type, _f32_addr(y), _f32_addr(x), buf.handle, rows, cols)
+    if rc:
+        _err("gi_cuda_gemv_buf", rc)
 
 
 def MatMulBatchBuf(quant_type: int, y: np.ndarray, x: np.ndarray, buf: Buffer, batch: int, rows: int,
@@ -240,7 +250,7 @@ def MatMulBatchBuf(quant_type: int, y: np.ndarray, x: np.ndarray, buf: Buffer, b
     """metal.MatMulBatchBuf (metal_darwin.go:544): y[b*rows + r], x[b*cols + k]."""
     if buf is None or y.size < batch * rows or x.size < batch * cols:
         raise GoInferCudaError("gi_cuda_gemm_buf", ERR_UNAVAILABLE, "bad arguments")
-    _err("gi_cuda_gemm_buf", load_library().gi_cuda_gemm_buf(quant_type, _f32(y), _f32(x), buf.handle,
+    _err("gi_cuda_gemm_buf", load_library().gi_cuda_gemm_buf(quant_type, _f32_addr(y), _f32_addr(x), buf.handle,
                                                               batch, rows, cols))
 
 

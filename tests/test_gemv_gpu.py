@@ -266,3 +266,31 @@ def test_prefill_batch_matches_per_token_oracle():
         G.ReleaseBuffer(buf)
         ref = O.matmul_batch(qt, x, raw, batch, rows, cols)
         assert_parity(y, ref.reshape(-1), what=f"batch {qt}")
+
+
+@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
+def test_pinned_host_output_written_directly(qt):
+    """A page-locked, device-mapped y is written by the kernel itself (no
+    device-to-host copy); the result is bit-identical to the copied one."""
+    import torch
+    rows, cols = 1000, 2048
+    raw = G.quantize(qt, seeded_weights(90, rows, cols))
+    x = seeded_x(91, cols)
+    buf = G.CreateBuffer(raw)
+    try:
+        y_page = np.full(rows, np.nan, np.float32)
+        G.MatMulBuf(qt, y_page, x, buf, rows, cols)
+        y_pin = torch.full((rows,), float("nan")).pin_memory().numpy()
+        x_pin = torch.from_numpy(x).pin_memory().numpy()
+        G.MatMulBuf(qt, y_pin, x_pin, buf, rows, cols)
+        assert np.array_equal(y_pin.view(np.uint32), y_page.view(np.uint32))
+        assert_parity(y_pin, O.matmul(qt, x, raw, rows, cols), what=f"pinned {qt}")
+        if qt != G.TYPE_Q8_0:  # batched prefill (tensor-core path for batch >= 16)
+            xb = np.stack([seeded_x(92 + b, cols) for b in range(16)])
+            yb_page = np.zeros(16 * rows, np.float32)
+            G.MatMulBatchBuf(qt, yb_page, xb.reshape(-1), buf, 16, rows, cols)
+            yb_pin = torch.zeros(16 * rows).pin_memory().numpy()
+            G.MatMulBatchBuf(qt, yb_pin, torch.from_numpy(xb.reshape(-1)).pin_memory().numpy(), buf, 16, rows, cols)
+            assert np.array_equal(yb_pin.view(np.uint32), yb_page.view(np.uint32))
+    finally:
+        G.ReleaseBuffer(buf)
