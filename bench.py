@@ -296,6 +296,39 @@ def decode_section(args, world, rank, local, pg):
         del tensors, ref
     model.close()
     dm.close()
+    # config 1 (Q8_0 4096x4096) and the Q6_K lm_head shapes: HBM GB/s of the
+    # plain decode GEMV, rotating weight copies past the L2, graph + PDL
+    peak, _kind = measured_peak()
+    other = {}
+    for name, qt, rows, cols in (("q8_0_config1_4096x4096", G.TYPE_Q8_0, 4096, 4096),
+                                 ("q6_k_lm_head_32000x4096", G.TYPE_Q6_K, 32000, 4096),
+                                 ("q6_k_lm_head_128256x8192", G.TYPE_Q6_K, 128256, 8192)):
+        wbytes = rows * G.row_bytes(qt, cols)
+        ncopy = max(2, int(2 * 126e6 / wbytes) + 1)
+        bufs = [G.synth_buffer(qt, 20 + c, 0.02, rows, cols) for c in range(ncopy)]
+        xv = torch.randn(cols, device=dev)
+        yv = torch.empty(rows, device=dev)
+        nl = 200
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            cs = torch.cuda.current_stream().cuda_stream
+            for i in range(nl):
+                b = bufs[i % ncopy]
+                G.gemv_dev(qt, yv.data_ptr(), xv.data_ptr(), b.device_ptr, b.nbytes, rows, cols, cs)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / nl
+        gbs = (wbytes + 4 * (rows + cols)) / us / 1e3
+        other[name] = {"us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+        del graph
+        for b in bufs:
+            G.ReleaseBuffer(b)
+    out["gemv_other"] = other
     # config 3: prefill dequant-GEMM (512 tokens x 4096 columns)
     x = torch.randn(512, 4096, device=dev)
     st = torch.cuda.Stream()
