@@ -83,7 +83,6 @@ int fail(int code, const char* what, cudaError_t e = cudaSuccess) {
     if (e_ != cudaSuccess) return fail(-5, what, e_); \
   } while (0)
 
-constexpr int kMaxTiles = 1 << 17;  // rows up to 2,097,152 per GEMV
 
 int init_locked(int device) {
   if (g.ready) {
@@ -106,11 +105,6 @@ int init_locked(int device) {
   GI_CUDA_TRY(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "cudaStreamCreate");
   if (gi::gemv_prepare_device() != 0 || gi::gemm_prepare_device() != 0)
     return fail(-5, "kernel attribute set-up", cudaGetLastError());
-  g.scratch.max_warps = g.sm_count * 32;
-  g.scratch.max_tiles = kMaxTiles;
-  GI_CUDA_TRY(cudaMalloc(&g.scratch.partials, sizeof(float) * 32 * g.scratch.max_warps), "cudaMalloc scratch");
-  GI_CUDA_TRY(cudaMalloc(&g.scratch.counters, sizeof(unsigned) * kMaxTiles), "cudaMalloc counters");
-  GI_CUDA_TRY(cudaMemset(g.scratch.counters, 0, sizeof(unsigned) * kMaxTiles), "cudaMemset counters");
   GI_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&g.err_host), sizeof(int), cudaHostAllocMapped),
               "cudaHostAlloc error word");
   *g.err_host = 0;

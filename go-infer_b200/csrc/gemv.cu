@@ -1097,16 +1097,6 @@ __global__ void __launch_bounds__(256) gemv_f32_kernel(float* __restrict__ y, co
 }
 }  // namespace f32
 
-void gemv_scratch_need(int qtype, int64_t rows, int64_t cols, const GemvLaunch& L, int* warps,
-                       int* tiles) {
-  *warps = 0;
-  *tiles = 0;
-  (void)qtype;
-  (void)rows;
-  (void)cols;
-  (void)L;
-}
-
 template <typename K, typename... Args>
 static int launch_rowwarp(K kernel, int64_t rows, const GemvLaunch& L, cudaStream_t stream,
                           Args... args) {

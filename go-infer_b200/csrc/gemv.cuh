@@ -11,17 +11,11 @@ namespace gi {
 // GGML type ids (pkg/gguf/types.go:25-52 of go-infer).
 enum : int { kTypeF32 = 0, kTypeQ8_0 = 8, kTypeQ4_K = 12, kTypeQ6_K = 14 };
 
-// Device scratch used by the stream-K Q4_K GEMV to combine row tiles that
-// straddle two CTAs: two 16-float partial slots per CTA and one arrival
-// counter per 16-row tile.  Counters must start at zero; every launch leaves
-// them at zero again.  `error` is set to 1 when a bounded device wait gives
-// up (never expected; the host reports GI_ERR_TIMEOUT).
+// Per-device state the kernels share: `error` (host-mapped) is set to 1 when
+// a bounded device wait gives up (never expected; the host reports
+// GI_ERR_TIMEOUT).
 struct GemvScratch {
-  float* partials = nullptr;     // [max_warps][2][16] (max_warps bounds the CTA count)
-  unsigned* counters = nullptr;  // [max_tiles]
   int* error = nullptr;
-  int max_warps = 0;
-  int max_tiles = 0;
 };
 
 // Fusions of the Q4_K GEMV used by the decode step (internal).
@@ -56,10 +50,6 @@ int64_t row_bytes(int qtype, int64_t cols);
 // memory).
 // Returns 0, -2 unsupported type, -4 bad shape, -5 CUDA launch error.
 int gemv_check(int qtype, int64_t rows, int64_t cols);
-
-// Scratch sizes the Q4_K launch needs for this shape (zero for other types).
-void gemv_scratch_need(int qtype, int64_t rows, int64_t cols, const GemvLaunch& L,
-                       int* warps, int* tiles);
 
 // y[rows] = W[rows x cols] * x[cols]; every pointer is device memory.
 // `w_bytes` bounds the weight reads (no access beyond w + w_bytes).
