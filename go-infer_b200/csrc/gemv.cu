@@ -5,16 +5,17 @@
 // 536-545).  Weights are the raw GGUF blocks, row-major, rows = output
 // features; x and y are fp32 (go-infer never quantises activations).
 //
-// Q4_K kernel: one small CTA per SM, each owning a contiguous run of 16-row
-// tiles.  Its 8 warps stream their units' raw super-blocks into per-warp
-// shared-memory rings with cp.async (up to 4 units ahead, the first ones
-// requested before the kernel waits on its predecessor) and take exact
+// Q4_K kernel: at most one CTA per SM, each owning a contiguous run of
+// 16-row tiles.  Its 8 or 16 warps stream their units' raw super-blocks into
+// per-warp shared-memory rings with cp.async (up to 4 units ahead, the first
+// ones requested before the kernel waits on its predecessor) and take exact
 // integer dot products on the int8 tensor cores (see namespace q4k).
 //
-// Q8_0 / Q6_K kernels: 4 rows per warp, fp32 CUDA-core dot products.  Their
-// 34- and 210-byte blocks are only 2-byte aligned, so each warp stages its
-// rows' bytes through shared memory with aligned 128-bit loads and realigns
-// words with funnel shifts.
+// Q8_0 / Q6_K kernels: 2 or 4 rows per warp, fp32 CUDA-core dot products.
+// Their 34- and 210-byte blocks are only 2-byte aligned; rows whose length
+// keeps 32-block (Q8_0) or 8-super-block (Q6_K) chunks 16-byte aligned are
+// streamed through per-warp two-stage cp.async rings, other rows are staged
+// with aligned 128-bit loads; words are realigned with funnel shifts.
 #include "common.cuh"
 #include "gemv.cuh"
 
