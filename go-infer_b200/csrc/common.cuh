@@ -204,6 +204,28 @@ GI_DEVINL void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, ui
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D += A(16x32 s8, row) * B(32x8 s8, col), exact int32 accumulate.
+GI_DEVINL void imma_16832s(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                           uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+GI_DEVINL uint32_t lds32(uint32_t addr) {
+  uint32_t r;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(addr));
+  return r;
+}
+
+GI_DEVINL uint32_t lds16(uint32_t addr) {
+  unsigned short r;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(r) : "r"(addr));
+  return r;
+}
+
 GI_DEVINL uint64_t lds64(uint32_t addr) {
   uint64_t r;
   asm volatile("ld.shared.u64 %0, [%1];" : "=l"(r) : "r"(addr));

@@ -609,6 +609,302 @@ int prepare() {
 }
 }  // namespace q4k
 
+// ------------------------ Q8_0 on the int8 tensor cores ---------------------
+// Rows of whole 256-column groups (every row and every 8-block unit is then
+// 16-byte aligned: 8 x 34 = 272 = 17 x 16).  The structure is the Q4_K
+// kernel's: a unit is 16 rows x 256 columns (8 blocks per row, 4352 bytes),
+// each CTA owns whole 16-row tiles, units are dealt to the warps round-robin
+// and streamed through per-warp cp.async rings, and every tile's per-warp
+// partials are summed in fixed warp order.
+//
+// Arithmetic: one m16n8k32 s8 MMA per block computes the exact int32 dot
+// products of its 32 int8 quants (A) with the four balanced base-256 limbs
+// of the 30-bit fixed-point activation (B, columns 0-3; one exponent per 256
+// columns, as for Q4_K).  The contraction order inside a block is free, so a
+// block's 32 quants are read as eight aligned words: odd blocks start on a
+// word boundary (34b + 2 = 0 mod 4); even blocks use seven aligned words
+// (quants 2..29) and one word assembled from quants 0, 1, 30, 31; the staged
+// activation uses the same order.  Per block and row the limb sums are
+// combined exactly in int32 (|sum| < 2^27), converted once to float and
+// scaled by the block's d, as DotVecQ8_0 scales its block sums
+// (pkg/quant/quant.go:320-339).
+namespace q80m {
+constexpr int kUnitBytes = 16 * 272;  // one 16-row x 256-column unit of raw blocks
+constexpr int kUnitX = 1040;          // staged activation bytes per unit: 8 blocks x 128 + scale
+constexpr int kSmemMax = 227 * 1024 - 256;
+constexpr int kCoresidentSmem = 110 * 1024;
+
+struct Params {
+  const uint8_t* w;
+  float* y;
+  const float* x;
+  long long rowb;
+  int rows, nku, ntiles, ctas;
+  int x_off, slot_off;
+};
+
+// Element of block b carried by byte j of slot word i (see above).
+GI_DEVINL int kslot(int b, int i, int j) {
+  if (b & 1) return 4 * i + j;
+  if (i < 7) return 2 + 4 * i + j;
+  return j < 2 ? j : 28 + j;
+}
+
+// Stage one unit (256 columns) of x at xu: per block b, [limb n][t][slot t,
+// slot 4+t][4 bytes] (128 bytes), then float 2^-e at 1024.  Lane L owns
+// block L/4 and the slot words t = L%4 and 4+t.
+GI_DEVINL void stage_unit(uint8_t* xu, const float* xunit, int lane) {
+  const int b = lane >> 2, t = lane & 3;
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[j] = xunit[32 * b + kslot(b, t, j)];
+    v[4 + j] = xunit[32 * b + kslot(b, 4 + t, j)];
+  }
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
+  m = warp_max(m);
+  int e = 0;
+  if (m > 0.f && m <= 3.0e38f) e = min(126, max(-126, 29 - ilogbf(m)));  // max |x| * 2^e < 2^30
+  const float s = exp2i(e);
+  uint32_t u[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) u[j] = ((uint32_t)__float2int_rn(v[j] * s) + 0x80808080u) ^ 0x80808080u;
+  const uint32_t base = smem_u32(xu) + b * 128 + t * 8;
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    const uint32_t k = 3u - (uint32_t)n;  // limb n is byte 3-n
+    const uint32_t lo = q4k::gather_byte(u[0], u[1], u[2], u[3], k);
+    const uint32_t hi = q4k::gather_byte(u[4], u[5], u[6], u[7], k);
+    sts64(base + n * 32, (uint64_t)lo | ((uint64_t)hi << 32));
+  }
+  if (lane == 0) reinterpret_cast<float*>(xu + 1024)[0] = exp2i(-e);
+}
+
+template <int W>
+__device__ void stage_x(uint8_t* xs, const Params& p) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int u = warp; u < p.nku; u += W) stage_unit(xs + u * kUnitX, p.x + 256 * u, lane);
+  __syncthreads();
+}
+
+GI_DEVINL float h2f(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
+
+// One unit: rows g and g+8 of a 16-row tile.  stage: [16 rows][272 bytes];
+// xu: the unit's staged activations.  Wt: this lane's limb weight (lanes 0,
+// 1 hold limbs 0-1 and 2-3; lanes 2, 3 hold the zero columns 4-7).
+GI_DEVINL void compute_unit(uint32_t stage, uint32_t xu, int g, int t, float Wt, float& yA, float& yB) {
+  const uint32_t rowA = stage + g * 272, rowB = rowA + 8 * 272;
+  float aA = 0.f, aB = 0.f;
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    uint32_t a0, a1, a2, a3;  // rows g, g+8: slot t; rows g, g+8: slot 4+t
+    if (b & 1) {
+      const uint32_t o = 34 * b + 2;
+      a0 = lds32(rowA + o + 4 * t);
+      a1 = lds32(rowB + o + 4 * t);
+      a2 = lds32(rowA + o + 16 + 4 * t);
+      a3 = lds32(rowB + o + 16 + 4 * t);
+    } else {
+      const uint32_t o = 34 * b;  // word u_i at o + 4i; quants 0..31 at o + 2 ..
+      a0 = lds32(rowA + o + 4 + 4 * t);
+      a1 = lds32(rowB + o + 4 + 4 * t);
+      const uint32_t i2 = t < 3 ? 20 + 4 * t : 0;  // u_{5+t}, or u_0 for the assembled word
+      const uint32_t wA = lds32(rowA + o + i2), wB = lds32(rowB + o + i2);
+      const uint32_t eA = lds32(rowA + o + 32), eB = lds32(rowB + o + 32);
+      a2 = t < 3 ? wA : prmt(wA, eA, 0x5432u);
+      a3 = t < 3 ? wB : prmt(wB, eB, 0x5432u);
+    }
+    uint64_t xb = 0;
+    if (g < 4) xb = lds64(xu + b * 128 + g * 32 + t * 8);
+    int d[4] = {0, 0, 0, 0};
+    imma_16832s(d, a0, a1, a2, a3, (uint32_t)xb, (uint32_t)(xb >> 32));
+    const float dA = h2f(lds16(rowA + 34 * b)), dB = h2f(lds16(rowB + 34 * b));
+    aA = fmaf((float)(d[0] * 256 + d[1]), dA, aA);
+    aB = fmaf((float)(d[2] * 256 + d[3]), dB, aB);
+  }
+  const float inv = __uint_as_float(lds32(xu + 1024));
+  yA = fmaf(aA * Wt, inv, yA);
+  yB = fmaf(aB * Wt, inv, yB);
+}
+
+template <int W, int S>
+__global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gemv_q80m_kernel(const Params p) {
+  constexpr int kWarps = W, kThreads = W * 32;
+  extern __shared__ __align__(16) uint8_t smem[];
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int c = blockIdx.x;
+  const int T0 = (int)((long long)p.ntiles * c / p.ctas), T1 = (int)((long long)p.ntiles * (c + 1) / p.ctas);
+  const int ntl = T1 - T0, n = ntl * p.nku;
+  const uint32_t ring = smem_u32(smem) + warp * S * kUnitBytes;
+  uint8_t* xs = smem + p.x_off;
+  const uint32_t xs_s = smem_u32(xs);
+  float* slots = reinterpret_cast<float*>(smem + p.slot_off);  // [ntl][kWarps][16]
+  const uint64_t pol = l2_evict_first_policy();
+  for (int i = threadIdx.x; i < ntl * kWarps * 16; i += kThreads) slots[i] = 0.f;
+
+  // Request cursor: lane L copies row L/2 of the unit, chunks L%2, L%2 + 2,
+  // ... (adjacent lanes fetch adjacent 16-byte chunks of a row).
+  const int crow = lane >> 1, cpar = lane & 1;
+  int ltile = warp / p.nku, lku = warp - ltile * p.nku;
+  int next = warp;
+  const uint8_t* src = nullptr;
+  auto seek = [&]() {
+    src = p.w + (long long)min((T0 + ltile) * 16 + crow, p.rows - 1) * p.rowb + lku * 272;
+  };
+  if (next < n) seek();
+  const uint32_t dst = ring + crow * 272 + 16 * cpar;
+  auto request = [&](int stage) {  // always commits one group (possibly empty)
+    if (next < n) {
+      const uint32_t o = (uint32_t)stage * kUnitBytes;
+#pragma unroll
+      for (int i = 0; i < 9; ++i)
+        if (cpar + 2 * i < 17) cp_async16_hint(dst + o + 32 * i, src + 16 * cpar + 32 * i, pol);
+      next += kWarps;
+      lku += kWarps;
+      if (lku < p.nku) {
+        src += kWarps * 272;
+      } else {
+        do {
+          lku -= p.nku;
+          ++ltile;
+        } while (lku >= p.nku);
+        if (next < n) seek();
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int s = 0; s < S; ++s) request(s);
+  griddep_wait();
+  stage_x<W>(xs, p);  // ends with a CTA barrier (also orders the slot zeroing)
+
+  const float Wt = t == 0 ? 65536.f : (t == 1 ? 1.f : 0.f);
+  int ctile = warp / p.nku, cku = warp - ctile * p.nku;
+  uint32_t cx = xs_s + cku * kUnitX;
+  float yA = 0.f, yB = 0.f;
+  int stage = 0;
+  for (int i = warp; i < n; i += kWarps) {
+    cp_async_wait<S - 1>();
+    __syncwarp();
+    compute_unit(ring + stage * kUnitBytes, cx, g, t, Wt, yA, yB);
+    __syncwarp();
+    request(stage);
+    stage = stage + 1 == S ? 0 : stage + 1;
+    const int tile = ctile;
+    cku += kWarps;
+    if (cku < p.nku) {
+      cx += kWarps * kUnitX;
+    } else {
+      do {
+        cku -= p.nku;
+        ++ctile;
+      } while (cku >= p.nku);
+      cx = xs_s + cku * kUnitX;
+    }
+    if (ctile != tile || i + kWarps >= n) {  // this warp is done with `tile`
+      float vA = yA + __shfl_xor_sync(0xffffffffu, yA, 1);
+      float vB = yB + __shfl_xor_sync(0xffffffffu, yB, 1);
+      vA += __shfl_xor_sync(0xffffffffu, vA, 2);
+      vB += __shfl_xor_sync(0xffffffffu, vB, 2);
+      yA = 0.f;
+      yB = 0.f;
+      if (t == 0) {
+        float* sl = slots + (tile * kWarps + warp) * 16;
+        sl[g] = vA;
+        sl[g + 8] = vB;
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  for (int tl = warp; tl < ntl; tl += kWarps) {
+    if (lane < 16) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) sum += slots[(tl * kWarps + w) * 16 + lane];
+      const int row = (T0 + tl) * 16 + lane;
+      if (row < p.rows) p.y[row] = sum;
+    }
+  }
+}
+
+struct Layout {
+  int warps, ctas, stages, x_off, slot_off, smem;
+};
+
+Layout layout(int64_t rows, int64_t cols, const GemvLaunch& L) {
+  Layout o;
+  const int nku = (int)(cols / 256), ntiles = (int)((rows + 15) / 16);
+  o.ctas = ntiles < L.sm_count ? ntiles : L.sm_count;
+  const int max_tiles = (ntiles + o.ctas - 1) / o.ctas;
+  bool large = o.ctas < L.sm_count || (long long)ntiles * nku >= 64LL * o.ctas;
+  const int xbytes = nku * kUnitX;
+  if (large && xbytes + max_tiles * 16 * 64 + 16 * 2 * kUnitBytes > kSmemMax) large = false;
+  o.warps = large ? 16 : 8;
+  const int fixed = xbytes + max_tiles * o.warps * 64;
+  o.stages = 3;
+  while (o.stages > 2 && fixed + o.warps * o.stages * kUnitBytes > kCoresidentSmem) --o.stages;
+  o.x_off = o.warps * o.stages * kUnitBytes;
+  o.slot_off = o.x_off + xbytes;
+  o.smem = o.slot_off + max_tiles * o.warps * 64;
+  return o;
+}
+
+int launch(float* y, const float* x, const uint8_t* w, int64_t rows, int64_t cols, const GemvLaunch& L,
+           cudaStream_t stream) {
+  const Layout o = layout(rows, cols, L);
+  if (o.smem > kSmemMax) return -4;
+  Params p;
+  p.w = w;
+  p.y = y;
+  p.x = x;
+  p.rowb = (cols / 32) * 34;
+  p.rows = (int)rows;
+  p.nku = (int)(cols / 256);
+  p.ntiles = (int)((rows + 15) / 16);
+  p.ctas = o.ctas;
+  p.x_off = o.x_off;
+  p.slot_off = o.slot_off;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(o.ctas);
+  cfg.blockDim = dim3(o.warps * 32);
+  cfg.dynamicSmemBytes = o.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = L.pdl ? 1 : 0;
+  cudaError_t e;
+  switch ((o.warps == 16 ? 10 : 0) + o.stages) {
+    case 2: e = cudaLaunchKernelEx(&cfg, gemv_q80m_kernel<8, 2>, p); break;
+    case 3: e = cudaLaunchKernelEx(&cfg, gemv_q80m_kernel<8, 3>, p); break;
+    case 12: e = cudaLaunchKernelEx(&cfg, gemv_q80m_kernel<16, 2>, p); break;
+    case 13: e = cudaLaunchKernelEx(&cfg, gemv_q80m_kernel<16, 3>, p); break;
+    default: return -4;
+  }
+  return e == cudaSuccess ? 0 : -5;
+}
+
+template <int W, int S>
+cudaError_t prepare_one() {
+  cudaError_t e = cudaFuncSetAttribute(gemv_q80m_kernel<W, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  return e == cudaSuccess ? set_max_shared_carveout(gemv_q80m_kernel<W, S>) : e;
+}
+
+int prepare() {
+  cudaError_t e = prepare_one<8, 2>();
+  if (e == cudaSuccess) e = prepare_one<8, 3>();
+  if (e == cudaSuccess) e = prepare_one<16, 2>();
+  if (e == cudaSuccess) e = prepare_one<16, 3>();
+  return e == cudaSuccess ? 0 : -5;
+}
+}  // namespace q80m
+
 // ---------------------------------------------------------------------------
 // Shared helpers of the 4-rows-per-warp fp32 kernels (Q8_0, Q6_K).
 namespace rowwarp {
@@ -1053,6 +1349,7 @@ int gemv_prepare_device() {
   if (q4k::prepare() != 0) return -5;
   if (set_max_shared_carveout(q80::gemv_q80_kernel) != cudaSuccess) return -5;
   if (q80::prepare_ring() != 0) return -5;
+  if (q80m::prepare() != 0) return -5;
   if (q6k::prepare_ring() != 0) return -5;
   if (set_max_shared_carveout(q6k::gemv_q6k_kernel) != cudaSuccess) return -5;
   return 0;
@@ -1129,7 +1426,11 @@ int gemv_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
       if ((reinterpret_cast<uintptr_t>(w) & 15) != 0) return -4;
       return q4k::launch(1, &y, x, &w, &rows, cols, L, stream);
     case kTypeQ8_0:
-      if (cols % 256 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) return q80::launch_ring(y, x, wb, rows, cols, L, stream);
+      if (cols % 256 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
+        const int r = q80m::launch(y, x, wb, rows, cols, L, stream);
+        if (r != -4) return r;  // -4: the activation staging does not fit; the ring kernel takes it
+        return q80::launch_ring(y, x, wb, rows, cols, L, stream);
+      }
       return launch_rowwarp(q80::gemv_q80_kernel, rows, L, stream, y, x, wb, wb + w_bytes,
                             (long long)rb, (int)rows, (int)(cols / 32));
     case kTypeQ6_K:
