@@ -11,11 +11,15 @@
 // ones requested before the kernel waits on its predecessor) and take exact
 // integer dot products on the int8 tensor cores (see namespace q4k).
 //
-// Q8_0 / Q6_K kernels: 2 or 4 rows per warp, fp32 CUDA-core dot products.
-// Their 34- and 210-byte blocks are only 2-byte aligned; rows whose length
-// keeps 32-block (Q8_0) or 8-super-block (Q6_K) chunks 16-byte aligned are
-// streamed through per-warp two-stage cp.async rings, other rows are staged
-// with aligned 128-bit loads; words are realigned with funnel shifts.
+// Q8_0 kernel (rows of whole 256-column groups): the Q4_K structure with one
+// exact int8 tensor-core MMA per 32-element block (see namespace q80m).
+//
+// Q6_K kernels and the remaining Q8_0 rows: 2 or 4 rows per warp, fp32
+// CUDA-core dot products.  Their 34- and 210-byte blocks are only 2-byte
+// aligned; rows whose length keeps 32-block (Q8_0) or 8-super-block (Q6_K)
+// chunks 16-byte aligned are streamed through per-warp two-stage cp.async
+// rings, other rows are staged with aligned 128-bit loads; words are
+// realigned with funnel shifts.
 #include "common.cuh"
 #include "gemv.cuh"
 
