@@ -121,80 +121,80 @@ __global__ void add_kernel(float* __restrict__ y, const float* __restrict__ b, i
   if (i < n) y[i] = __fadd_rn(y[i], b[i]);
 }
 
-// ---- RoPE (kernels.go:22-36) on q and k, then the KV-cache write ------------
-// (forward.go:226-238).  rope[pos][i] = (cos, sin) of pos / theta^(2i/hd),
-// computed in double on the host and rounded to float32 as the reference does.
-__global__ void rope_kv_kernel(const StepState* __restrict__ st, float* __restrict__ q, const float* __restrict__ k,
-                               const float* __restrict__ v, const float2* __restrict__ rope, float* __restrict__ kc,
-                               float* __restrict__ vc, int n_heads, int n_kv_heads, int hd, int kv_dim,
-                               uint32_t max_pos, int* error) {
-  griddep_wait();
-  griddep_launch_dependents();
-  const int half = hd >> 1;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  const uint32_t pos = st->pos, slot = st->slot;
-  if (pos >= max_pos) {  // past the RoPE table: report, touch nothing
-    if (i == 0) atomicExch(error, 1);
-    return;
-  }
-  const int nq = n_heads * half, nk = n_kv_heads * half;
-  float* krow = kc + (size_t)slot * kv_dim;
-  float* vrow = vc + (size_t)slot * kv_dim;
-  if (i < nq + nk) {
-    const bool isq = i < nq;
-    const int p = isq ? i : i - nq;
-    const int h = p / half, j = p % half;
-    const float2 cs = rope[(size_t)pos * half + j];
-    const float* src = isq ? q : k;
-    const float v0 = src[h * hd + j], v1 = src[h * hd + j + half];
-    const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
-    const float r1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
-    if (isq) {
-      q[h * hd + j] = r0;
-      q[h * hd + j + half] = r1;
-    } else {
-      krow[h * hd + j] = r0;
-      krow[h * hd + j + half] = r1;
-    }
-  } else if (i < nq + nk + kv_dim) {
-    const int e = i - nq - nk;
-    vrow[e] = v[e];
-  }
-}
-
-// ---- attention with GQA (forward.go:241-266), split over KV positions -------
-// CTA (kv head g, chunk c) handles the kv_mul query heads of g against
-// positions [32c, 32c + 32) of the active context: it stages the chunk's K
-// and V rows and the queries in shared memory (all loads in flight at once),
-// then writes, per query head, (max, sum of exp, unnormalised output) for
-// attn_combine_kernel.  Scores use the float64 exp of kernels.go:60.
+// ---- attention with GQA (forward.go:226-266), split over KV positions -------
+// CTA (kv head g, chunk c) handles the kv_mul query heads of g against the
+// cache slots [32c, 32c + 32) of the active context.  It applies RoPE
+// (kernels.go:22-36; rope[pos][i] = (cos, sin) of pos / theta^(2i/hd),
+// computed in double on the host and rounded to float32) to its queries as
+// it stages them; the CTA whose chunk holds this step's slot also rotates
+// k, and writes k and v into the cache (forward.go:226-238) — no other CTA
+// reads that slot.  It stages the chunk's K and V rows in shared memory
+// (all loads in flight at once), then writes, per query head, (max, sum of
+// exp, unnormalised output) for attn_combine_kernel.  Scores use the float64
+// exp of kernels.go:60.
 __global__ void __launch_bounds__(256) attn_partial_kernel(const StepState* __restrict__ st,
-                                                           const float* __restrict__ q, const float* __restrict__ kc,
-                                                           const float* __restrict__ vc, float* __restrict__ part,
-                                                           int kv_mul, int hd, int kv_dim, int splits, float scale) {
+                                                           const float* __restrict__ q, const float* __restrict__ k,
+                                                           const float* __restrict__ v,
+                                                           const float2* __restrict__ rope, float* __restrict__ kc,
+                                                           float* __restrict__ vc, float* __restrict__ part,
+                                                           int kv_mul, int hd, int kv_dim, int splits, float scale,
+                                                           uint32_t max_pos, int* error) {
   extern __shared__ __align__(16) float sm[];
   griddep_wait();
   griddep_launch_dependents();
   const int g = blockIdx.x, c = blockIdx.y;
+  const uint32_t pos = st->pos, slot = st->slot;
+  if (pos >= max_pos) {  // past the RoPE table: report, touch nothing
+    if (g == 0 && c == 0 && threadIdx.x == 0) atomicExch(error, 1);
+    return;
+  }
   const int active = (int)st->active;
   const int t0 = c * kAttChunk;
   const int nt = max(0, min(kAttChunk, active - t0));
-  const int hd4 = hd >> 2;
+  const int half = hd >> 1, hd4 = hd >> 2;
   float* qs = sm;                          // [kv_mul][hd]
   float* ks = qs + kv_mul * hd;            // [kAttChunk][hd]
   float* vs = ks + kAttChunk * hd;         // [kAttChunk][hd]
   float* sc = vs + kAttChunk * hd;         // [kv_mul][kAttChunk]
   float* mx = sc + kv_mul * kAttChunk;     // [kv_mul][2]
-  float4* qs4 = reinterpret_cast<float4*>(qs);
+  const float2* cs = rope + (size_t)pos * half;
+  // queries of g's heads, rotated (r0 = v0 c - v1 s, r1 = v0 s + v1 c)
+  const float* qg = q + (size_t)g * kv_mul * hd;
+  for (int i = threadIdx.x; i < kv_mul * half; i += blockDim.x) {
+    const int h = i / half, j = i - h * half;
+    const float2 r = cs[j];
+    const float v0 = qg[h * hd + j], v1 = qg[h * hd + j + half];
+    qs[h * hd + j] = __fsub_rn(__fmul_rn(v0, r.x), __fmul_rn(v1, r.y));
+    qs[h * hd + j + half] = __fadd_rn(__fmul_rn(v0, r.y), __fmul_rn(v1, r.x));
+  }
+  const int cur = (int)slot - t0;  // this step's slot in the chunk, if it is here
   float4* ks4 = reinterpret_cast<float4*>(ks);
   float4* vs4 = reinterpret_cast<float4*>(vs);
-  const float4* q4 = reinterpret_cast<const float4*>(q + (size_t)g * kv_mul * hd);
-  for (int i = threadIdx.x; i < kv_mul * hd4; i += blockDim.x) qs4[i] = __ldg(q4 + i);
   for (int i = threadIdx.x; i < nt * hd4; i += blockDim.x) {
     const int t = i / hd4, d4 = i - t * hd4;
+    if (t == cur) continue;
     const size_t off = ((size_t)(t0 + t) * kv_dim + (size_t)g * hd) / 4 + d4;
     ks4[i] = __ldg(reinterpret_cast<const float4*>(kc) + off);
     vs4[i] = __ldg(reinterpret_cast<const float4*>(vc) + off);
+  }
+  if (cur >= 0 && cur < nt) {
+    float* krow = kc + (size_t)slot * kv_dim + (size_t)g * hd;
+    float* vrow = vc + (size_t)slot * kv_dim + (size_t)g * hd;
+    for (int j = threadIdx.x; j < half; j += blockDim.x) {
+      const float2 r = cs[j];
+      const float v0 = k[g * hd + j], v1 = k[g * hd + j + half];
+      const float r0 = __fsub_rn(__fmul_rn(v0, r.x), __fmul_rn(v1, r.y));
+      const float r1 = __fadd_rn(__fmul_rn(v0, r.y), __fmul_rn(v1, r.x));
+      ks[cur * hd + j] = r0;
+      ks[cur * hd + j + half] = r1;
+      krow[j] = r0;
+      krow[j + half] = r1;
+    }
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+      const float val = v[g * hd + d];
+      vs[cur * hd + d] = val;
+      vrow[d] = val;
+    }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -620,14 +620,9 @@ int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
     if (Ly.bk && e == cudaSuccess) e = launch(pdl, blocks(kv_dim, 256), dim3(256), 0, s, add_kernel, k_, Ly.bk, kv_dim);
     if (Ly.bv && e == cudaSuccess) e = launch(pdl, blocks(kv_dim, 256), dim3(256), 0, s, add_kernel, v_, Ly.bv, kv_dim);
     if (e != cudaSuccess) return -5;
-    const int nrope = (c.n_heads + c.n_kv_heads) * (hd / 2) + kv_dim;
-    e = launch(pdl, blocks(nrope, 256), dim3(256), 0, s, rope_kv_kernel, (const StepState*)st_, q_,
-               (const float*)k_, (const float*)v_, (const float2*)rope_, kc, vc, c.n_heads, c.n_kv_heads, hd, kv_dim,
-               (uint32_t)c.max_pos, scratch_.error);
-    if (e != cudaSuccess) return -5;
     e = launch(pdl, dim3(c.n_kv_heads, att_splits_), dim3(256), att_smem, s, attn_partial_kernel,
-               (const StepState*)st_, (const float*)q_, (const float*)kc, (const float*)vc, part_, kv_mul, hd, kv_dim,
-               att_splits_, c.attn_scale);
+               (const StepState*)st_, (const float*)q_, (const float*)k_, (const float*)v_, (const float2*)rope_, kc,
+               vc, part_, kv_mul, hd, kv_dim, att_splits_, c.attn_scale, (uint32_t)c.max_pos, scratch_.error);
     if (e != cudaSuccess) return -5;
     e = launch(pdl, dim3(c.n_heads), dim3(hd), 0, s, attn_combine_kernel, (const float*)part_, att_, hd, att_splits_);
     if (e != cudaSuccess) return -5;
