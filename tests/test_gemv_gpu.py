@@ -110,7 +110,8 @@ def test_config_shapes_match_oracle(what, qt, rows, cols, ws, xs):
 
 
 @pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
-@pytest.mark.parametrize("rows,cols", [(1, 256), (17, 256), (33, 512), (16, 4096), (100, 1280), (3, 11008)])
+@pytest.mark.parametrize("rows,cols", [(1, 256), (17, 256), (33, 512), (16, 4096), (100, 1280), (3, 11008),
+                                       (4100, 256)])  # many short rows: 8 warps, 3 ring stages
 def test_small_and_ragged_shapes(qt, rows, cols):
     w = seeded_weights(rows * 7 + cols, rows, cols)
     raw = G.quantize(qt, w)
