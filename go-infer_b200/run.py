@@ -9,6 +9,8 @@ generated token.
 
     python go-infer_b200/run.py decode --model llama2-7b --prompt 128 --steps 64
     python go-infer_b200/run.py decode --model llama3-70b --prompt 40 --steps 2
+    python go-infer_b200/run.py decode --gguf model.gguf --prompt 16 --steps 32
+    python go-infer_b200/run.py export --model llama2-7b --layers 2 --out small.gguf
     python go-infer_b200/run.py prefill --type q4_k --rows 4096 --cols 4096 --batch 512 --reps 3
 """
 from __future__ import annotations
@@ -30,11 +32,18 @@ TYPES = {"q4_k": G.TYPE_Q4_K, "q6_k": G.TYPE_Q6_K, "q8_0": G.TYPE_Q8_0}
 
 
 def decode(args) -> None:
-    cfg = MODELS[args.model]
-    if args.layers:
-        cfg = dataclasses.replace(cfg, n_layers=args.layers)
-    cfg = dataclasses.replace(cfg, max_seq=max(cfg.max_seq, args.prompt + args.steps))
-    dev = synth.DeviceModel.synth_on_device(cfg, seed=args.seed)
+    if args.gguf:  # a GGUF file (Q4_K / Q6_K / Q8_0 / F32 tensors under go-infer's names)
+        import gguf
+        with gguf.GGUFReader(args.gguf) as r:
+            host = gguf.host_model(r, max_seq=args.prompt + args.steps)
+            dev = synth.DeviceModel(host)
+        cfg = dev.cfg
+    else:
+        cfg = MODELS[args.model]
+        if args.layers:
+            cfg = dataclasses.replace(cfg, n_layers=args.layers)
+        cfg = dataclasses.replace(cfg, max_seq=max(cfg.max_seq, args.prompt + args.steps))
+        dev = synth.DeviceModel.synth_on_device(cfg, seed=args.seed)
     model = dev.model()
     try:
         prompt = np.random.default_rng(args.seed * 10).integers(0, cfg.vocab, args.prompt).astype(np.int32)
@@ -45,6 +54,16 @@ def decode(args) -> None:
     finally:
         model.close()
         dev.close()
+
+
+def export(args) -> None:
+    """Write the seeded synthetic model (drawn on the host) as a GGUF file."""
+    import gguf
+    cfg = MODELS[args.model]
+    if args.layers:
+        cfg = dataclasses.replace(cfg, n_layers=args.layers)
+    gguf.save_model(synth.synth_model(cfg, seed=args.seed), args.out)
+    print(f"wrote {args.out}")
 
 
 def prefill(args) -> None:
@@ -84,6 +103,12 @@ def main() -> None:
     d.add_argument("--prompt", type=int, default=128)
     d.add_argument("--steps", type=int, default=64)
     d.add_argument("--seed", type=int, default=4)
+    d.add_argument("--gguf", default="", help="decode the model of this GGUF file instead")
+    x = sub.add_parser("export")
+    x.add_argument("--model", choices=sorted(MODELS), default="llama2-7b")
+    x.add_argument("--layers", type=int, default=0, help="override the layer count")
+    x.add_argument("--seed", type=int, default=4)
+    x.add_argument("--out", required=True)
     p = sub.add_parser("prefill")
     p.add_argument("--type", choices=sorted(TYPES), default="q4_k")
     p.add_argument("--rows", type=int, default=4096)
@@ -92,6 +117,9 @@ def main() -> None:
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--seed", type=int, default=8)
     args = ap.parse_args()
+    if args.cmd == "export":  # host only
+        export(args)
+        return
     G.Init(0)
     if not G.IsAvailable():
         raise SystemExit("libgoinfer_cuda: no CUDA device")

@@ -183,3 +183,30 @@ def test_70b_widths_two_layers_match_oracle():
     finally:
         model.close()
         dev.close()
+
+
+def test_model_from_gguf_file(tmp_path):
+    """A model read from a GGUF file (go-infer_b200/gguf.py, the format of
+    pkg/gguf) decodes the same ids as the in-memory synthetic model it was
+    written from, and as the oracle."""
+    import gguf
+    host = synth.synth_model(SMALL, seed=15)
+    path = str(tmp_path / "small.gguf")
+    gguf.save_model(host, path)
+    prompt = np.random.default_rng(16).integers(0, SMALL.vocab, 8)
+    with gguf.GGUFReader(path) as r:
+        dev = synth.DeviceModel(gguf.host_model(r))
+    model = dev.model()
+    try:
+        ids = check_greedy(model, O.RefModel(host.cfg, host.tensors), prompt, 8)
+        mem = synth.DeviceModel(host)
+        m2 = mem.model()
+        try:
+            ids2, _l, _ms = m2.generate(prompt, 8)
+        finally:
+            m2.close()
+            mem.close()
+        assert np.array_equal(ids, ids2)
+    finally:
+        model.close()
+        dev.close()

@@ -1,0 +1,124 @@
+"""GGUF reader and writer (go-infer_b200/gguf.py) on CPU: the format as
+go-infer's pkg/gguf parses it, mirrored from pkg/gguf/gguf_test.go (corrupted
+headers, metadata helpers), plus round trips of the seeded synthetic models,
+the alignment rule, Engine's configuration keys and defaults
+(pkg/engine/engine.go:71-127), and the oracle's decode over tensors read
+from a file matching the decode over the in-memory model."""
+import os
+import struct
+
+import numpy as np
+import pytest
+
+import gguf
+import oracle as O
+import synth
+
+SMALL = synth.LlamaConfig(n_layers=2, dim=256, hidden=512, n_heads=4, n_kv_heads=2, vocab=300, max_seq=32,
+                          rope_theta=10000.0)
+
+
+def test_corrupted_headers_are_rejected(tmp_path):  # gguf_test.go:10-34
+    trunc = tmp_path / "trunc.gguf"
+    trunc.write_bytes(bytes([0x47, 0x47, 0x55, 0x46]))
+    with pytest.raises(ValueError):
+        gguf.GGUFReader(str(trunc))
+    bad = tmp_path / "badmagic.gguf"
+    bad.write_bytes(struct.pack("<IIQQ", 0x12345678, 3, 0, 0))
+    with pytest.raises(ValueError, match="magic"):
+        gguf.GGUFReader(str(bad))
+    ver = tmp_path / "version.gguf"
+    ver.write_bytes(struct.pack("<IIQQ", gguf.MAGIC, 7, 0, 0))
+    with pytest.raises(ValueError, match="version"):
+        gguf.GGUFReader(str(ver))
+    empty = tmp_path / "empty.gguf"
+    empty.write_bytes(b"")
+    with pytest.raises(ValueError):
+        gguf.GGUFReader(str(empty))
+
+
+def test_metadata_helpers(tmp_path):  # gguf_test.go:36-60
+    p = str(tmp_path / "meta.gguf")
+    gguf.write_gguf(p, {"uint_val": gguf.Typed(gguf.T_U64, 42), "float_val": gguf.Typed(gguf.T_F64, 3.1415),
+                        "string_val": "test_string", "flag": True,
+                        "names": ["a", "b", "c"]}, [])
+    with gguf.GGUFReader(p) as r:
+        assert r.get_uint("uint_val", 0) == 42
+        assert r.get_uint("missing_val", 99) == 99
+        assert r.get_float("float_val", 0.0) == 3.1415
+        assert r.get_float("missing_val", 1.0) == 1.0
+        assert r.get_string("string_val", "") == "test_string"
+        assert r.get_string("missing_val", "x") == "x"
+        assert r.get_bool("flag") is True
+        assert r.metadata["names"] == ["a", "b", "c"]
+        assert r.version == 3 and r.tensors == {}
+
+
+def test_synthetic_model_round_trip(tmp_path):
+    host = synth.synth_model(SMALL, seed=7)
+    p = str(tmp_path / "m.gguf")
+    gguf.save_model(host, p)
+    with gguf.GGUFReader(p) as r:
+        assert r.data_offset % 32 == 0
+        cfg = gguf.model_config(r)
+        for f in ("n_layers", "dim", "hidden", "n_heads", "n_kv_heads", "vocab", "max_seq"):
+            assert getattr(cfg, f) == getattr(SMALL, f), f
+        assert np.float32(cfg.eps) == np.float32(SMALL.eps) and cfg.rope_theta == SMALL.rope_theta
+        assert set(r.tensors) == set(host.tensors)
+        for name, (qt, arr) in host.tensors.items():
+            info = r.tensors[name]
+            assert info.type == qt
+            assert np.array_equal(r.tensor_data(name).view(np.uint8), np.asarray(arr).view(np.uint8).reshape(-1))
+        # GGML dimension order: dims[0] is the row length
+        assert r.tensors["blk.0.wq.weight"].dims == [SMALL.dim, SMALL.q_dim]
+        assert r.tensors["blk.0.ffn_down.weight"].dims == [SMALL.hidden, SMALL.dim]
+        assert r.tensors["token_embd.weight"].dims == [SMALL.dim, SMALL.vocab]
+
+
+def test_alignment_and_bounds(tmp_path):
+    p = str(tmp_path / "a.gguf")
+    data = np.arange(64, dtype=np.float32)
+    gguf.write_gguf(p, {"general.architecture": "llama"},
+                    [("a", gguf.GGML_F32, [64], data), ("b", gguf.GGML_F32, [8, 8], data * 2)], alignment=64)
+    with gguf.GGUFReader(p) as r:
+        assert r.get_uint("general.alignment") == 64 and r.data_offset % 64 == 0
+        assert np.array_equal(r.tensor_data("a"), data)
+        assert np.array_equal(r.tensor_data("b"), data * 2)
+        with pytest.raises(KeyError):
+            r.tensor_data("missing")
+    # a tensor whose bytes run past the end of the file is refused
+    raw = bytearray(open(p, "rb").read())
+    with open(p, "wb") as f:
+        f.write(raw[:-100])
+    with gguf.GGUFReader(p) as r:
+        with pytest.raises(ValueError, match="exceeds"):
+            r.tensor_data("b")
+
+
+def test_engine_defaults_and_fallbacks(tmp_path):
+    p = str(tmp_path / "d.gguf")
+    emb = np.zeros((10, 4), np.float32)
+    gguf.write_gguf(p, {"general.architecture": "qwen2", "llama.embedding_length": 4,
+                        "qwen2.attention.head_count": 2},
+                    [("token_embd.weight", gguf.GGML_F32, [4, 10], emb)])
+    with gguf.GGUFReader(p) as r:
+        c = gguf.model_config(r)
+        assert c.dim == 4                          # llama.* fallback
+        assert c.n_heads == 2 and c.n_kv_heads == 2  # <arch>.* first; kv defaults to heads
+        assert (c.hidden, c.n_layers) == (5632, 16)
+        assert c.rope_theta == 500000.0 and np.float32(c.eps) == np.float32(1e-5)
+        assert c.vocab == 10                       # token_embd dim 1
+        assert c.max_seq == 2048
+
+
+def test_oracle_decode_from_file_matches_memory(tmp_path):
+    host = synth.synth_model(SMALL, seed=9)
+    p = str(tmp_path / "o.gguf")
+    gguf.save_model(host, p)
+    prompt = [3, 141, 59, 26]
+    want, _m, want_logits = O.RefModel(SMALL, host.tensors).greedy(prompt, 4)
+    with gguf.GGUFReader(p) as r:
+        loaded = gguf.host_model(r)
+        ids, _m2, logits = O.RefModel(loaded.cfg, loaded.tensors).greedy(prompt, 4)
+    assert list(ids) == list(want)
+    assert np.array_equal(logits, want_logits)
