@@ -226,6 +226,14 @@ GI_DEVINL uint32_t lds16(uint32_t addr) {
   return r;
 }
 
+// Four 8x8 b16 matrices (lanes 8i..8i+7 give the row addresses of matrix
+// i); register i of lane l holds matrix i, row l/4, bytes 4(l%4)..+3.
+GI_DEVINL void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
 GI_DEVINL uint64_t lds64(uint32_t addr) {
   uint64_t r;
   asm volatile("ld.shared.u64 %0, [%1];" : "=l"(r) : "r"(addr));

@@ -69,7 +69,7 @@ namespace q4k {
 // (more warps hide more of the per-warp dependency chains), else 8.
 constexpr int kWarpsSmall = 8, kWarpsLarge = 16;
 constexpr int kUnitX = 1104;       // staged activation bytes per unit (see stage_unit)
-constexpr int kStageBytes = 2304;  // qs: [16 rows][4 chunks, swizzled][32 B], headers: [16 rows][16 B]
+constexpr int kStageBytes = 2304;  // qs: [16 rows][8 x 16 B, piece q at slot q ^ (row & 7)], headers: [16 rows][16 B]
 constexpr int kMaxCols = 45056;
 constexpr int kSmemMax = 227 * 1024 - 256;  // dynamic; the rest is static (the RMSNorm reduction)
 constexpr int kCoresidentSmem = 110 * 1024;  // fits two CTAs (this kernel and the next) per SM
@@ -115,15 +115,18 @@ GI_DEVINL uint32_t gather_byte(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w
 }
 
 // Activations of one unit (256 columns) in shared memory at xu:
-//   [0, 1024)    int8 limbs, [sub-block j][limb n][element l], limb 0 the
+//   [0, 1024)    int8 limbs, [sub-block j][limb n][32 positions], limb 0 the
 //                most significant; sub-block j covers columns
-//                64*(j/2) + 32*(j%2) + l, as Q4_K's getScaleMin indexes them;
+//                64*(j/2) + 32*(j%2) + l, as Q4_K's getScaleMin indexes them,
+//                and positions 8q..8q+7 hold its elements 4q..4q+3 and
+//                16+4q..16+4q+3: the k order of an m16n8k32 B fragment, so
+//                lane t of the MMA reads its two B registers with one load;
 //   [1024, 1088) min-MMA B fragments: for t = 0..3, 8 bytes:
 //                f16 (X_t hi, X_t lo, X_{t+4} hi, X_{t+4} lo), X_j the sum
 //                of sub-block j scaled by 2^em;
 //   [1088, 1096) float 2^-e, float 2^-em.
-// One warp stages a unit; lane L owns elements 8*(L%4) .. +7 of
-// sub-block L/4 (a: the first four, b: the next four).
+// One warp stages a unit; lane L owns elements 4q..4q+3 (a) and
+// 16+4q..16+4q+3 (b) of sub-block L/4, q = L%4.
 GI_DEVINL void stage_unit(uint8_t* xu, float4 a, float4 b, int lane) {
   float m = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
                   fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
@@ -185,7 +188,7 @@ template <int W, bool F>
 __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int j = lane >> 2, q = lane & 3;
-  const int off = 64 * (j >> 1) + 32 * (j & 1) + 8 * q;
+  const int offA = 64 * (j >> 1) + 32 * (j & 1) + 4 * q, offB = offA + 16;  // stage_unit's a, b
   const int nku = p.nku;
   const float* __restrict__ x = p.x;
   float scale = 1.f;
@@ -214,11 +217,11 @@ __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
     for (int k = 0; k < 4; ++k) {
       const int u = u0 + k * W;
       if (u < nku) {
-        a[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off));
-        b[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + off + 4));
+        a[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + offA));
+        b[k] = __ldg(reinterpret_cast<const float4*>(x + u * 256 + offB));
         if (F && p.xmode == kXNorm) {
-          a[k] = mul3(a[k], scale, __ldg(reinterpret_cast<const float4*>(p.x2 + u * 256 + off)));
-          b[k] = mul3(b[k], scale, __ldg(reinterpret_cast<const float4*>(p.x2 + u * 256 + off + 4)));
+          a[k] = mul3(a[k], scale, __ldg(reinterpret_cast<const float4*>(p.x2 + u * 256 + offA)));
+          b[k] = mul3(b[k], scale, __ldg(reinterpret_cast<const float4*>(p.x2 + u * 256 + offB)));
         }
       }
     }
@@ -232,9 +235,12 @@ __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
 }
 
 // One unit: rows g and g+8 of a 16-row tile, 256 columns.  stage: the raw
-// super-blocks in shared memory; xu: the unit's staged activations; xl: this
-// lane's B fragment in them (limb g of sub-block 0, or for g >= 4 limb g-4
-// of sub-block 1).
+// super-blocks in shared memory (qs of row r at r*128, its 16-byte piece p
+// at slot p ^ (r & 7), so the eight rows of one ldmatrix read hit eight
+// different bank groups; headers at 2048 + r*16); lofs: this lane's
+// ldmatrix row address in a stage for chunk 0 (chunk c: lofs ^ 32c); xu:
+// the unit's staged activations; xl: this lane's B fragment in them (limb g
+// of sub-block 0, or for g >= 4 limb g-4 of sub-block 1).
 //
 // Each 64-column chunk c takes two MMAs with the same B: its columns 0-3
 // hold the limbs of sub-block 2c (the low nibbles' activations), columns 4-7
@@ -244,8 +250,8 @@ __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
 // high-nibble products.  Lanes t = 0, 1 hold columns 0-3 and lanes 2, 3
 // columns 4-7; each scales its accumulators by its sub-block's scale, so the
 // integer sums stay exact and every column of both MMAs is used.
-GI_DEVINL void compute_unit(uint32_t stage, uint32_t xu, uint32_t xl, int g, int t, uint32_t sh8, uint32_t selE,
-                            uint32_t selO, float W0, float W1, float& yA, float& yB) {
+GI_DEVINL void compute_unit(uint32_t stage, uint32_t lofs, uint32_t xu, uint32_t xl, int g, int t, uint32_t sh8,
+                            uint32_t selE, uint32_t selO, float W0, float W1, float& yA, float& yB) {
   const uint4 hA = lds128(stage + 2048 + g * 16);
   const uint4 hB = lds128(stage + 2048 + (g + 8) * 16);
   // 6-bit scales sc0..sc7 as bytes (getScaleMin, pkg/quant/quant.go:228-235)
@@ -253,18 +259,16 @@ GI_DEVINL void compute_unit(uint32_t stage, uint32_t xu, uint32_t xl, int g, int
   const uint32_t sA47 = (hA.w & 0x0F0F0F0Fu) | ((hA.y >> 2) & 0x30303030u);
   const uint32_t sB47 = (hB.w & 0x0F0F0F0Fu) | ((hB.y >> 2) & 0x30303030u);
   int lA0 = 0, lA1 = 0, lB0 = 0, lB1 = 0, fA0 = 0, fA1 = 0, fB0 = 0, fB1 = 0;
-  const uint32_t rowA = stage + g * 128 + 8 * t, rowB = rowA + 8 * 128;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    const uint32_t off = 32u * ((uint32_t)c ^ (uint32_t)(g & 3));
-    const uint64_t qa = lds64(rowA + off), qb = lds64(rowB + off);
+    // A fragment of chunk c: rows g, g+8 x bytes 4t..4t+3 and 16+4t..16+4t+3
+    uint32_t a0, a1, a2, a3;
+    ldsm_x4(stage + (lofs ^ (32u * (uint32_t)c)), a0, a1, a2, a3);
     const uint64_t xv = lds64(xl + (2 * c) * 128);
-    const uint32_t a0 = (uint32_t)qa, a1 = (uint32_t)(qa >> 32);
-    const uint32_t b0 = (uint32_t)qb, b1 = (uint32_t)(qb >> 32);
     int dl[4] = {0, 0, 0, 0}, df[4] = {0, 0, 0, 0};
-    imma_16832(dl, a0 & 0x0F0F0F0Fu, b0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, b1 & 0x0F0F0F0Fu, (uint32_t)xv,
+    imma_16832(dl, a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu, a3 & 0x0F0F0F0Fu, (uint32_t)xv,
                (uint32_t)(xv >> 32));
-    imma_16832(df, a0, b0, a1, b1, (uint32_t)xv, (uint32_t)(xv >> 32));
+    imma_16832(df, a0, a1, a2, a3, (uint32_t)xv, (uint32_t)(xv >> 32));
     // this lane's sub-block scale: byte (2c & 3) + (t >= 2) of the word
     const uint32_t sel = (c & 1) ? selO : selE;
     const int sA = (int)prmt(c < 2 ? sA03 : sA47, 0u, sel), sB = (int)prmt(c < 2 ? sB03 : sB47, 0u, sel);
@@ -332,9 +336,12 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
   // stream neighbouring super-blocks of the same 16 rows (one long run of
   // bytes per row), which keeps DRAM pages open.  Request cursor: unit
   // `next` = (tile ltile, column block lku); pa, pb: its super-blocks in
-  // rows g and g + 8, advanced in place while the tile stays the same.
+  // rows g and g + 8, advanced in place, also across tiles while they stay
+  // whole tiles of one matrix (global tiles below fast_end); seek() places
+  // them anew (first unit, a new matrix, a tile whose last rows are clamped,
+  // interleaved SwiGLU tiles).
   int ltile = warp / p.nku, lku = warp - ltile * p.nku;
-  int next = warp;
+  int next = warp, fast_end = 0;
   const uint8_t* pa = nullptr;
   const uint8_t* pb = nullptr;
   auto seek = [&]() {
@@ -343,31 +350,45 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
     const int r0 = lt * 16, rl = p.rows[m] - 1;
     pa = p.w[m] + (long long)min(r0 + g, rl) * p.rowb + lku * 144;
     pb = p.w[m] + (long long)min(r0 + g + 8, rl) * p.rowb + lku * 144;
+    fast_end = (F && p.ymode == kYSwiGLU) ? 0 : p.tstart[m] + (p.rows[m] >> 4);
   };
   if (next < n) seek();
-  // this lane's destinations in a stage: chunk t of rows g, g + 8 (swizzled)
-  // and, for t < 2, the header of row g + 8t
-  const uint32_t dst = ring + g * 128 + 32u * ((uint32_t)t ^ (uint32_t)(g & 3));
+  // Moving from column block lku + kWarps - dt*nku of a row to column block
+  // lku of the row 16*dt further on is dt * 15 rows of bytes.
+  const long long step15 = 15 * p.rowb;
+  // this lane's destinations in a stage: 16-byte pieces 2t, 2t+1 of rows g,
+  // g + 8 (piece q of row r at slot q ^ (r & 7)) and, for t < 2, the header
+  // of row g + 8t
+  const uint32_t dst0 = ring + g * 128 + 16u * ((2u * (uint32_t)t) ^ (uint32_t)g);
+  const uint32_t dst1 = ring + g * 128 + 16u * ((2u * (uint32_t)t + 1u) ^ (uint32_t)g);
   const uint32_t dsth = ring + 2048 + (g + 8 * (t & 1)) * 16;
   auto request = [&](int stage) {  // always commits one group (possibly empty)
     if (next < n) {
       const uint32_t o = (uint32_t)stage * kStageBytes;
-      cp_async16_hint(dst + o, pa + 16 + 32 * t, pol);
-      cp_async16_hint(dst + o + 16, pa + 32 + 32 * t, pol);
-      cp_async16_hint(dst + o + 1024, pb + 16 + 32 * t, pol);
-      cp_async16_hint(dst + o + 1040, pb + 32 + 32 * t, pol);
+      cp_async16_hint(dst0 + o, pa + 16 + 32 * t, pol);
+      cp_async16_hint(dst1 + o, pa + 32 + 32 * t, pol);
+      cp_async16_hint(dst0 + o + 1024, pb + 16 + 32 * t, pol);
+      cp_async16_hint(dst1 + o + 1024, pb + 32 + 32 * t, pol);
       if (t < 2) cp_async16_hint(dsth + o, t ? pb : pa, pol);
       next += kWarps;
       lku += kWarps;
-      if (lku < p.nku) {
-        pa += kWarps * 144;
-        pb += kWarps * 144;
-      } else {
+      pa += kWarps * 144;
+      pb += kWarps * 144;
+      if (lku >= p.nku) {
+        int dt = 0;
         do {
           lku -= p.nku;
-          ++ltile;
+          ++dt;
         } while (lku >= p.nku);
-        if (next < n) seek();
+        ltile += dt;
+        if (next < n) {
+          if (T0 + ltile < fast_end) {
+            pa += dt * step15;
+            pb += dt * step15;
+          } else {
+            seek();
+          }
+        }
       }
     }
     cp_async_commit();
@@ -387,6 +408,10 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
   const float W0 = t == 0 ? 16777216.f : (t == 1 ? 256.f : (t == 2 ? 1048576.f : 16.f));
   const float W1 = t == 0 ? 65536.f : (t == 1 ? 1.f : (t == 2 ? 4096.f : 0.0625f));
   const uint32_t xlo = (uint32_t)((g & 3) * 32 + 8 * t + (g >= 4 ? 128 : 0));
+  // ldmatrix rows: lanes 8i..8i+7 address matrix i = (rows 0-7 | 8-15) x
+  // (bytes 0-15 | 16-31) of a chunk
+  const uint32_t lrow = (uint32_t)((lane & 7) + 8 * ((lane >> 3) & 1));
+  const uint32_t lofs = lrow * 128u + 16u * ((uint32_t)(lane >> 4) ^ (lrow & 7u));
   int ctile = warp / p.nku, cku = warp - ctile * p.nku;
   uint32_t cx = xs_s + cku * kUnitX;  // the computed unit's staged activations
   float yA = 0.f, yB = 0.f;
@@ -394,7 +419,7 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
   for (int i = warp; i < n; i += kWarps) {
     cp_async_wait<S - 1>();
     __syncwarp();
-    compute_unit(ring + stage * kStageBytes, cx, cx + xlo, g, t, sh8, selE, selO, W0, W1, yA, yB);
+    compute_unit(ring + stage * kStageBytes, lofs, cx, cx + xlo, g, t, sh8, selE, selO, W0, W1, yA, yB);
     __syncwarp();
     request(stage);
     stage = stage + 1 == S ? 0 : stage + 1;

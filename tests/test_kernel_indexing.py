@@ -1,0 +1,91 @@
+"""CPU replay of the Q4_K decode GEMV's request cursor
+(go-infer_b200/csrc/gemv.cu, gemv_q4k_kernel): the weight addresses it
+advances in place, across tiles of one matrix by dt * 15 rows, must equal
+the direct address of every unit (matrix, 16-row tile with clamped last
+rows, column block) for every CTA and warp, over matrix boundaries,
+ragged row counts, the interleaved SwiGLU tiles and warps-per-CTA both
+above and below the column-block count."""
+import pytest
+
+
+def direct(rows, nku, T, u_lku, g, swiglu, tstart, base):
+    if swiglu:
+        m, lt = T & 1, T >> 1
+    else:
+        m = sum(T >= s for s in tstart[1:len(rows)])
+        lt = T - tstart[m]
+    r0, rl, rowb = lt * 16, rows[m] - 1, nku * 144
+    return (base[m] + min(r0 + g, rl) * rowb + u_lku * 144, base[m] + min(r0 + g + 8, rl) * rowb + u_lku * 144)
+
+
+def replay(rows, nku, W, ctas, swiglu=False):
+    tiles = [(r + 15) // 16 for r in rows]
+    tstart = [0]
+    for k in tiles:
+        tstart.append(tstart[-1] + k)
+    ntiles = tstart[-1]
+    base = [10 ** 9 * (m + 1) for m in range(len(rows))]
+    rowb = nku * 144
+    gran = 2 if swiglu else 1
+    nun = ntiles // gran
+    checked = 0
+    for c in range(ctas):
+        T0, T1 = gran * (nun * c // ctas), gran * (nun * (c + 1) // ctas)
+        n = (T1 - T0) * nku
+        for warp in range(W):
+            for g in range(8):
+                ltile, lku = warp // nku, warp % nku
+                nxt, fast_end = warp, 0
+                pa = pb = None
+
+                def seek():
+                    nonlocal pa, pb, fast_end
+                    T = T0 + ltile
+                    pa, pb = direct(rows, nku, T, lku, g, swiglu, tstart, base)
+                    if swiglu:
+                        fast_end = 0
+                    else:
+                        m = sum(T >= s for s in tstart[1:len(rows)])
+                        fast_end = tstart[m] + (rows[m] >> 4)
+
+                if nxt < n:
+                    seek()
+                while nxt < n:
+                    want = direct(rows, nku, T0 + nxt // nku, nxt % nku, g, swiglu, tstart, base)
+                    assert (pa, pb) == want, (rows, nku, W, ctas, c, warp, g, nxt)
+                    checked += 1
+                    nxt += W
+                    lku += W
+                    pa += W * 144
+                    pb += W * 144
+                    if lku >= nku:
+                        dt = 0
+                        while lku >= nku:
+                            lku -= nku
+                            dt += 1
+                        ltile += dt
+                        if nxt < n:
+                            if T0 + ltile < fast_end:
+                                pa += dt * 15 * rowb
+                                pb += dt * 15 * rowb
+                            else:
+                                seek()
+    return checked
+
+
+@pytest.mark.parametrize("rows,nku,W,ctas", [
+    ([11008, 11008], 16, 16, 148),   # gate + up, config 2
+    ([4096], 43, 16, 148),           # down, config 2
+    ([4096], 16, 8, 296),
+    ([100, 37], 8, 16, 5),           # ragged tails, nku < W
+    ([4100, 256], 3, 8, 7),
+    ([40, 48, 24], 5, 16, 3),        # three matrices
+    ([17], 1, 16, 1),
+])
+def test_cursor_matches_direct_addressing(rows, nku, W, ctas):
+    assert replay(rows, nku, W, ctas) > 0
+
+
+def test_cursor_swiglu_interleave():
+    assert replay([96, 96], 4, 8, 3, swiglu=True) > 0
+    assert replay([100, 100], 16, 16, 5, swiglu=True) > 0

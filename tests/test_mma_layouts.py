@@ -120,3 +120,76 @@ def test_q8_0_aligned_words_give_exact_block_dots():
                 assert max(abs(v01), abs(v23)) < 2 ** 31
                 X = sum(L[n, 32 * b:32 * b + 32] * 256 ** (3 - n) for n in range(4))
                 assert v01 * 65536 + v23 == int(q @ X)
+
+
+def test_q4k_stage_swizzle_and_ldmatrix_fragments():
+    """The Q4_K kernel's stage as its cp.async requests fill it (16-byte
+    piece q of row r at slot q ^ (r & 7)), read back by ldmatrix.x4 at each
+    lane's lofs ^ 32c, against activations staged in B-fragment k order: the
+    two MMAs per chunk give the exact sub-block limb dots, every address is a
+    16-byte-aligned offset inside the 2304-byte stage, and each ldmatrix
+    phase (eight rows of one matrix) touches eight distinct bank groups."""
+    rng = np.random.default_rng(3)
+    x = rng.normal(0, 1, 256).astype(np.float32)
+    e = exponent(x)
+    L = limbs_of(x, e)
+    # staged activations: stage_x / stage_unit, lane (j, q) -> positions 8q..8q+7
+    xs = np.zeros((8, 4, 32), np.int64)  # [sub-block j][limb n][position]
+    for lane in range(32):
+        j, q = lane >> 2, lane & 3
+        offA = 64 * (j >> 1) + 32 * (j & 1) + 4 * q
+        offB = offA + 16
+        for n in range(4):
+            xs[j, n, 8 * q:8 * q + 4] = L[n, offA:offA + 4]
+            xs[j, n, 8 * q + 4:8 * q + 8] = L[n, offB:offB + 4]
+    xflat = xs.reshape(-1)
+    for _ in range(5):
+        unit = rng.integers(0, 256, (16, 144), dtype=np.int64)  # 16 rows of one Q4_K super-block
+        stage = np.full(2304, -1, np.int64)
+        for lane in range(32):  # request(): the cp.async destinations
+            g, t = lane >> 2, lane & 3
+            dst0 = g * 128 + 16 * ((2 * t) ^ g)
+            dst1 = g * 128 + 16 * ((2 * t + 1) ^ g)
+            for d, row, src in ((dst0, g, 16 + 32 * t), (dst1, g, 32 + 32 * t),
+                                (dst0 + 1024, g + 8, 16 + 32 * t), (dst1 + 1024, g + 8, 32 + 32 * t)):
+                assert d % 16 == 0 and 0 <= d and d + 16 <= 2048
+                stage[d:d + 16] = unit[row, src:src + 16]
+            if t < 2:
+                dh = 2048 + (g + 8 * (t & 1)) * 16
+                stage[dh:dh + 16] = unit[g + 8 * t, 0:16]
+        assert (stage >= 0).all()
+        for c in range(4):
+            # ldmatrix.x4: lanes 8i..8i+7 give the rows of matrix i
+            addr = []
+            for lane in range(32):
+                lrow = (lane & 7) + 8 * ((lane >> 3) & 1)
+                lofs = lrow * 128 + 16 * ((lane >> 4) ^ (lrow & 7))
+                a = lofs ^ (32 * c)
+                assert a % 16 == 0 and 0 <= a and a + 16 <= 2048
+                addr.append(a)
+            for i in range(4):
+                banks = {(addr[8 * i + r] % 128) // 16 for r in range(8)}
+                assert len(banks) == 8
+            A = np.zeros((16, 32), np.int64)
+            for lane in range(32):
+                g, t = lane >> 2, lane & 3
+                for i in range(4):
+                    row16 = stage[addr[8 * i + g]:addr[8 * i + g] + 16]
+                    word = row16[4 * t:4 * t + 4]                 # register i of this lane
+                    r = g + (8 if i in (1, 3) else 0)              # a0, a2: row g; a1, a3: row g + 8
+                    k0 = 4 * t + (16 if i >= 2 else 0)             # a0, a1: k 4t..; a2, a3: k 16+4t..
+                    A[r, k0:k0 + 4] = word
+            assert np.array_equal(A, unit[:, 16 + 32 * c:16 + 32 * c + 32])  # qs bytes of chunk c
+            B = np.zeros((32, 8), np.int64)
+            for lane in range(32):
+                g, t = lane >> 2, lane & 3
+                xl = (g & 3) * 32 + 8 * t + (128 if g >= 4 else 0) + 256 * c
+                v = xflat[xl:xl + 8]
+                B[4 * t:4 * t + 4, g] = v[:4]        # b0: k 4t..4t+3, column g
+                B[16 + 4 * t:20 + 4 * t, g] = v[4:]  # b1: k 16+4t..
+            lo, whole = A & 0x0F, A
+            Dl, Df = lo @ B, whole @ B
+            xlo = L[:, 64 * c:64 * c + 32]
+            xhi = L[:, 64 * c + 32:64 * c + 64]
+            assert np.array_equal(Dl[:, 0:4], lo @ xlo.T)
+            assert np.array_equal((Df - Dl)[:, 4:8], 16 * ((A >> 4) @ xhi.T))
