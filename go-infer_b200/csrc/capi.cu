@@ -5,8 +5,8 @@
 // a process-wide device/queue, weight buffers created once per tensor, and
 // int-returning GEMV/GEMM entry points that block unless a batch is open.
 // Here the process-wide state is one CUDA stream on one device plus the
-// scratch the stream-K GEMV needs; host-pointer calls stage x/y through a
-// device arena on that stream.
+// mapped error word that the kernels' bounded waits report through;
+// host-pointer calls stage x/y through a device arena on that stream.
 #include <cuda_runtime.h>
 
 #include <cstdio>
