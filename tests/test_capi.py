@@ -37,6 +37,44 @@ def test_header_compiles_as_c():
                         "-o", os.path.join(d, "t")], check=True)
 
 
+def test_c_program_links_and_calls_the_library(tmp_path):
+    """What cgo does with INTEGRATION.md's preamble: compile C against the
+    header, link libgoinfer_cuda.so, call entry points that answer without
+    a device (row sizes of pkg/math/gemv.go, the nil handle of
+    metal.CreateBuffer before Init)."""
+    import subprocess
+    src = tmp_path / "use.c"
+    src.write_text(
+        '#include <stdio.h>\n#include "goinfer_cuda.h"\n'
+        "int main(void) {\n"
+        "  if (gi_quant_row_bytes(GI_TYPE_Q4_K, 4096) != 16 * 144) return 2;\n"
+        "  if (gi_quant_row_bytes(GI_TYPE_Q6_K, 11008) != 43 * 210) return 3;\n"
+        "  if (gi_quant_row_bytes(GI_TYPE_Q8_0, 4096) != 128 * 34) return 4;\n"
+        "  if (gi_quant_row_bytes(3, 4096) != -1) return 5;\n"
+        "  if (gi_cuda_is_available()) return 0;  /* bound elsewhere: nothing more to check */\n"
+        "  unsigned char w[16] = {0};\n"
+        "  if (gi_cuda_create_buffer(w, sizeof w) != NULL) return 6;\n"
+        "  printf(\"%s\\n\", gi_cuda_last_error());\n"
+        "  return 0;\n}\n")
+    lib_dir = os.path.dirname(G.LIB_PATH)
+    exe = tmp_path / "use"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe),
+                    "-L", lib_dir, "-lgoinfer_cuda", "-Wl,-rpath," + lib_dir], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
+
+
+def test_integration_binding_names_declared_functions():
+    """Every C function and type INTEGRATION.md's cgo code uses is declared
+    in the header."""
+    text = open(HEADER).read()
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    used = set(re.findall(r"\bC\.(gi_\w+)", doc))
+    assert used
+    for name in used:
+        assert re.search(r"\b" + name + r"\b", text), name
+
+
 def test_row_bytes_follow_gemv_go():
     # pkg/math/gemv.go:99,135,171
     assert G.row_bytes(G.TYPE_Q8_0, 4096) == 128 * 34
