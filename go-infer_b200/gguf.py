@@ -306,15 +306,68 @@ def model_config(reader: GGUFReader, max_seq: int = 8192):
                              eps=float(np.float32(eps)), rope_theta=float(np.float32(f("rope.freq_base", 500000.0))))
 
 
-def host_model(reader: GGUFReader, max_seq: int = 8192):
-    """A synth.HostModel over the file's tensors (views of the mapped file:
-    keep the reader open while they are used; DeviceModel copies them)."""
+def matrix_role(name: str):
+    """Tensor-parallel role of a tensor (a key of synth.shard_slices): the
+    layer matrices by their GGUF names, token_embd and output; the Q, K and
+    V biases take their matrix's rows.  None for what every rank keeps
+    whole (norms)."""
+    import synth
+
+    parts = name.split(".")
+    if len(parts) == 4 and parts[0] == "blk":
+        role = {v: k for k, v in synth.TENSOR_NAMES.items()}.get(parts[2])
+        if parts[3] == "weight":
+            return role
+        if parts[3] == "bias" and role in ("wq", "wk", "wv"):
+            return role
+        return None
+    return {"token_embd.weight": "token_embd", "output.weight": "output"}.get(name)
+
+
+def shard_matrix(qtype: int, data: np.ndarray, rows: int, cols: int, r0: int, nr: int, c0: int, nc: int):
+    """Rows [r0, r0 + nr) x columns [c0, c0 + nc) of a row-major GGUF matrix
+    as contiguous raw blocks (uint8, or float32 for F32); the column range
+    must fall on block boundaries."""
+    per, nbytes = _BLOCKS[qtype]
+    if cols % per or c0 % per or nc % per or not (0 <= r0 and r0 + nr <= rows and 0 <= c0 and c0 + nc <= cols):
+        raise ValueError(f"shard rows [{r0}, {r0 + nr}) cols [{c0}, {c0 + nc}) of a {rows}x{cols} matrix "
+                         f"of type {qtype} (blocks of {per})")
+    rb = cols // per * nbytes
+    raw = np.asarray(data).view(np.uint8).reshape(rows, rb)
+    out = np.ascontiguousarray(raw[r0:r0 + nr, c0 // per * nbytes:(c0 + nc) // per * nbytes]).reshape(-1)
+    return out.view(np.float32) if qtype == GGML_F32 else out
+
+
+def host_model(reader: GGUFReader, max_seq: int = 8192, rank: int = 0, world: int = 1):
+    """A synth.HostModel over the file's tensors.  world == 1: views of the
+    mapped file (keep the reader open while they are used; DeviceModel
+    copies them).  world > 1: rank's Megatron shard of every matrix
+    (synth.shard_slices: rows of Q, K, V, gate, up and the output head with
+    the Q/K/V biases, columns of the attention output and down projections;
+    the token table and the norms whole) under the shard's configuration,
+    as copies."""
     import synth
 
     cfg = model_config(reader, max_seq)
-    m = synth.HostModel(cfg)
+    if world <= 1:
+        m = synth.HostModel(cfg)
+        for name, info in reader.tensors.items():
+            m.tensors[name] = (info.type, reader.tensor_data(name))
+        return m
+    sl = synth.shard_slices(cfg, rank, world)
+    m = synth.HostModel(synth.shard_config(cfg, world))
     for name, info in reader.tensors.items():
-        m.tensors[name] = (info.type, reader.tensor_data(name))
+        data = reader.tensor_data(name)
+        role = matrix_role(name)
+        if role is None:
+            m.tensors[name] = (info.type, data.copy())
+            continue
+        r0, nr, c0, nc = sl[role]
+        if name.endswith(".bias"):
+            m.tensors[name] = (info.type, np.ascontiguousarray(data[r0:r0 + nr]))
+            continue
+        cols, rows = int(info.dims[0]), int(info.dims[1])
+        m.tensors[name] = (info.type, shard_matrix(info.type, data, rows, cols, r0, nr, c0, nc))
     return m
 
 
@@ -334,8 +387,7 @@ def save_model(host, path: str) -> None:
             rows = {"token_embd.weight": c.vocab, "output.weight": c.vocab}.get(name)
             if rows is None:
                 import synth
-                key = name.split(".")[2] if name.startswith("blk.") else None
-                rows = synth.layer_shapes(c)[key][0]
+                rows = synth.layer_shapes(c)[matrix_role(name)][0]
             per, nbytes = _BLOCKS[qt]
             cols = arr.size // rows // nbytes * per
             dims = [cols, rows]

@@ -61,6 +61,16 @@ LLAMA3_70B = LlamaConfig(n_layers=80, dim=8192, hidden=28672, n_heads=64, n_kv_h
 
 LAYER_MATS = ("wq", "wk", "wv", "wo", "ffn_gate", "ffn_up", "ffn_down")
 
+# GGUF tensor name of each layer matrix role (pkg/engine/forward.go:146-152,
+# engine_test.go:43-56); the roles are the field names of the layer table.
+TENSOR_NAMES = {"wq": "attn_q", "wk": "attn_k", "wv": "attn_v", "wo": "attn_output", "ffn_gate": "ffn_gate",
+                "ffn_up": "ffn_up", "ffn_down": "ffn_down"}
+
+
+def layer_tensor(l: int, role: str) -> str:
+    """GGUF name of layer l's matrix `role` (e.g. blk.3.attn_q.weight)."""
+    return f"blk.{l}.{TENSOR_NAMES[role]}.weight"
+
 
 def layer_shapes(cfg: LlamaConfig) -> dict:
     """rows x cols of each layer matrix (rows = output features)."""
@@ -74,9 +84,6 @@ class HostModel:
     """Raw tensors of a model: {name: (ggml type, uint8/float32 array)}."""
     cfg: LlamaConfig
     tensors: dict = field(default_factory=dict)
-
-    def layer(self, l: int, name: str):
-        return self.tensors[f"blk.{l}.{name}"]
 
 
 def shard_config(cfg: LlamaConfig, world: int) -> LlamaConfig:
@@ -119,7 +126,7 @@ def synth_model(cfg: LlamaConfig, seed: int, threads: int = 0, rank: int = 0, wo
     for l in range(cfg.n_layers):
         for name in LAYER_MATS:
             r, c = shapes[name]
-            m.tensors[f"blk.{l}.{name}.weight"] = draw(cfg.wtype, name, r, c)
+            m.tensors[layer_tensor(l, name)] = draw(cfg.wtype, name, r, c)
         for name in ("attn_norm", "ffn_norm"):
             m.tensors[f"blk.{l}.{name}.weight"] = (G.TYPE_F32, np.ones(cfg.dim, np.float32))
     m.tensors["output_norm.weight"] = (G.TYPE_F32, np.ones(cfg.dim, np.float32))
@@ -165,7 +172,7 @@ class DeviceModel:
             for l in range(cfg.n_layers):
                 for name in LAYER_MATS:
                     r, c = shapes[name]
-                    draw(f"blk.{l}.{name}.weight", cfg.wtype, name, r, c)
+                    draw(layer_tensor(l, name), cfg.wtype, name, r, c)
                 for name in ("attn_norm", "ffn_norm"):
                     bufs[f"blk.{l}.{name}.weight"] = G.CreateBuffer(ones)
                     types[f"blk.{l}.{name}.weight"] = G.TYPE_F32
@@ -188,7 +195,7 @@ class DeviceModel:
         for l in range(self.cfg.n_layers):
             d = {}
             for name in LAYER_MATS:
-                key = f"blk.{l}.{name}.weight"
+                key = layer_tensor(l, name)
                 d[name] = self.bufs[key]
                 d[name + "_type"] = self.types[key]
             d["attn_norm"] = self.bufs[f"blk.{l}.attn_norm.weight"]

@@ -256,8 +256,8 @@ class RefModel:
         layers = (RefLayer * cfg.n_layers)()
         for l in range(cfg.n_layers):
             p = f"blk.{l}."
-            layers[l] = RefLayer(mat(p + "wq.weight"), mat(p + "wk.weight"), mat(p + "wv.weight"),
-                                 mat(p + "wo.weight"), mat(p + "ffn_gate.weight"), mat(p + "ffn_up.weight"),
+            layers[l] = RefLayer(mat(p + "attn_q.weight"), mat(p + "attn_k.weight"), mat(p + "attn_v.weight"),
+                                 mat(p + "attn_output.weight"), mat(p + "ffn_gate.weight"), mat(p + "ffn_up.weight"),
                                  mat(p + "ffn_down.weight"), vec(p + "attn_norm.weight"),
                                  vec(p + "ffn_norm.weight"))
         self._layers = layers

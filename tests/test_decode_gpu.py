@@ -110,7 +110,7 @@ def test_synthetic_engine_model():
     for name, (r, c) in [("token_embd.weight", (cfg.vocab, cfg.dim)), ("output.weight", (cfg.vocab, cfg.dim))]:
         T[name] = (G.TYPE_F32, np.full((r, c), 0.1, np.float32))
     for name, (r, c) in synth.layer_shapes(cfg).items():
-        T[f"blk.0.{name}.weight"] = (G.TYPE_F32, np.full((r, c), 0.1, np.float32))
+        T[synth.layer_tensor(0, name)] = (G.TYPE_F32, np.full((r, c), 0.1, np.float32))
     for name in ("blk.0.attn_norm.weight", "blk.0.ffn_norm.weight", "output_norm.weight"):
         T[name] = (G.TYPE_F32, np.full(cfg.dim, 0.1, np.float32))
     dev = synth.DeviceModel(synth.HostModel(cfg, T))

@@ -4,6 +4,7 @@ headers, metadata helpers), plus round trips of the seeded synthetic models,
 the alignment rule, Engine's configuration keys and defaults
 (pkg/engine/engine.go:71-127), and the oracle's decode over tensors read
 from a file matching the decode over the in-memory model."""
+import dataclasses
 import os
 import struct
 
@@ -70,7 +71,8 @@ def test_synthetic_model_round_trip(tmp_path):
             assert info.type == qt
             assert np.array_equal(r.tensor_data(name).view(np.uint8), np.asarray(arr).view(np.uint8).reshape(-1))
         # GGML dimension order: dims[0] is the row length
-        assert r.tensors["blk.0.wq.weight"].dims == [SMALL.dim, SMALL.q_dim]
+        assert r.tensors["blk.0.attn_q.weight"].dims == [SMALL.dim, SMALL.q_dim]
+        assert r.tensors["blk.0.attn_output.weight"].dims == [SMALL.q_dim, SMALL.dim]
         assert r.tensors["blk.0.ffn_down.weight"].dims == [SMALL.hidden, SMALL.dim]
         assert r.tensors["token_embd.weight"].dims == [SMALL.dim, SMALL.vocab]
 
@@ -122,3 +124,68 @@ def test_oracle_decode_from_file_matches_memory(tmp_path):
         ids, _m2, logits = O.RefModel(loaded.cfg, loaded.tensors).greedy(prompt, 4)
     assert list(ids) == list(want)
     assert np.array_equal(logits, want_logits)
+
+
+TP = synth.LlamaConfig(n_layers=2, dim=512, hidden=1024, n_heads=4, n_kv_heads=2, vocab=300, max_seq=32,
+                       rope_theta=10000.0)
+
+
+@pytest.mark.parametrize("world", [2])
+def test_sharded_load_equals_the_seeded_shards(tmp_path, world):
+    """Rank r's shard sliced out of the whole model's file equals the shard
+    synth_model draws for rank r directly (the same seeded streams), byte
+    for byte, under the same shard configuration."""
+    p = str(tmp_path / "tp.gguf")
+    gguf.save_model(synth.synth_model(TP, seed=21), p)
+    with gguf.GGUFReader(p) as r:
+        for rank in range(world):
+            got = gguf.host_model(r, rank=rank, world=world)
+            want = synth.synth_model(TP, seed=21, rank=rank, world=world)
+            # eps is stored as float32 in the file
+            assert got.cfg == dataclasses.replace(want.cfg, eps=float(np.float32(want.cfg.eps)))
+            assert set(got.tensors) == set(want.tensors)
+            for name, (qt, arr) in want.tensors.items():
+                gq, ga = got.tensors[name]
+                assert gq == qt, name
+                assert np.array_equal(np.asarray(ga).view(np.uint8).reshape(-1),
+                                      np.asarray(arr).view(np.uint8).reshape(-1)), (rank, name)
+
+
+def test_shard_roles_and_block_boundaries():
+    assert gguf.matrix_role("blk.3.attn_q.weight") == "wq"
+    assert gguf.matrix_role("blk.3.attn_output.weight") == "wo"
+    assert gguf.matrix_role("blk.0.ffn_down.weight") == "ffn_down"
+    assert gguf.matrix_role("blk.0.attn_k.bias") == "wk"
+    assert gguf.matrix_role("blk.0.attn_norm.weight") is None
+    assert gguf.matrix_role("output_norm.weight") is None
+    assert gguf.matrix_role("output.weight") == "output"
+    w = np.arange(4 * 2 * 144, dtype=np.uint8)  # 4 rows x 2 Q4_K super-blocks
+    s = gguf.shard_matrix(gguf.GGML_Q4_K, w, 4, 512, 1, 2, 256, 256)
+    assert np.array_equal(s, w.reshape(4, 288)[1:3, 144:].reshape(-1))
+    with pytest.raises(ValueError):
+        gguf.shard_matrix(gguf.GGML_Q4_K, w, 4, 512, 0, 4, 128, 256)  # not on a super-block
+    with pytest.raises(ValueError):
+        gguf.shard_matrix(gguf.GGML_Q4_K, w, 4, 512, 3, 2, 0, 256)    # past the last row
+
+
+def test_device_model_wiring_uses_gguf_names(monkeypatch):
+    """DeviceModel's layer table takes every layer matrix and norm by its
+    GGUF name (the library's buffer calls stubbed: no device needed)."""
+    import goinfer_cuda as G
+
+    class Buf:
+        def __init__(self, arr):
+            self.arr, self.handle = arr, id(arr)
+
+    tables = []
+    monkeypatch.setattr(G, "CreateBuffer", lambda arr: Buf(arr))
+    monkeypatch.setattr(G, "layer_table", lambda layers: tables.append(layers) or layers)
+    host = synth.synth_model(SMALL, seed=5)
+    dev = synth.DeviceModel(host)
+    (layers,) = tables
+    assert len(layers) == SMALL.n_layers
+    for l, d in enumerate(layers):
+        for role in synth.LAYER_MATS:
+            qt, arr = host.tensors[synth.layer_tensor(l, role)]
+            assert d[role].arr is arr and d[role + "_type"] == qt
+        assert d["attn_norm"].arr is host.tensors[f"blk.{l}.attn_norm.weight"][1]

@@ -99,9 +99,9 @@ def py_forward(cfg, W, kc, vc, token, pos):
     for l in range(cfg.n_layers):
         p = f"blk.{l}."
         xb = rms(x, W[p + "attn_norm.weight"][1])
-        q = mm(p + "wq.weight", xb, cfg.q_dim)
-        k = mm(p + "wk.weight", xb, cfg.kv_dim)
-        v = mm(p + "wv.weight", xb, cfg.kv_dim)
+        q = mm(p + "attn_q.weight", xb, cfg.q_dim)
+        k = mm(p + "attn_k.weight", xb, cfg.kv_dim)
+        v = mm(p + "attn_v.weight", xb, cfg.kv_dim)
         for h in range(cfg.n_heads):
             seg = q[h * hd:(h + 1) * hd]; rope(seg, pos); q[h * hd:(h + 1) * hd] = seg
         for h in range(cfg.n_kv_heads):
@@ -126,7 +126,7 @@ def py_forward(cfg, W, kc, vc, token, pos):
             for t in range(active):
                 for d in range(hd):
                     att[h * hd + d] = f32(att[h * hd + d] + f32(sc[t] * vc[l][t][g * hd + d]))
-        proj = mm(p + "wo.weight", att, dim)
+        proj = mm(p + "attn_output.weight", att, dim)
         x = [f32(a + b) for a, b in zip(x, proj)]
         xb = rms(x, W[p + "ffn_norm.weight"][1])
         gt = mm(p + "ffn_gate.weight", xb, cfg.hidden)
@@ -144,7 +144,7 @@ def f32_model(cfg, seed):
     T = {"token_embd.weight": (G.TYPE_F32, rng.normal(0, 0.5, (cfg.vocab, cfg.dim)).astype(np.float32))}
     for l in range(cfg.n_layers):
         for name, (r, c) in synth.layer_shapes(cfg).items():
-            T[f"blk.{l}.{name}.weight"] = (G.TYPE_F32, rng.normal(0, 0.2, (r, c)).astype(np.float32))
+            T[synth.layer_tensor(l, name)] = (G.TYPE_F32, rng.normal(0, 0.2, (r, c)).astype(np.float32))
         for name in ("attn_norm", "ffn_norm"):
             T[f"blk.{l}.{name}.weight"] = (G.TYPE_F32, rng.uniform(0.5, 1.5, cfg.dim).astype(np.float32))
     T["output_norm.weight"] = (G.TYPE_F32, np.ones(cfg.dim, np.float32))
@@ -186,7 +186,7 @@ def synthetic_engine_model():
     for name, (r, c) in [("token_embd.weight", (cfg.vocab, cfg.dim)), ("output.weight", (cfg.vocab, cfg.dim))]:
         T[name] = (G.TYPE_F32, np.full((r, c), 0.1, np.float32))
     for name, (r, c) in synth.layer_shapes(cfg).items():
-        T[f"blk.0.{name}.weight"] = (G.TYPE_F32, np.full((r, c), 0.1, np.float32))
+        T[synth.layer_tensor(0, name)] = (G.TYPE_F32, np.full((r, c), 0.1, np.float32))
     for name in ("blk.0.attn_norm.weight", "blk.0.ffn_norm.weight", "output_norm.weight"):
         T[name] = (G.TYPE_F32, np.full(cfg.dim, 0.1, np.float32))
     return cfg, T

@@ -31,12 +31,12 @@ def _rank(rank, world, port, q):
         sl = synth.shard_slices(CFG, rank, world)
         res = {}
         for name, vec in (("wo", att), ("ffn_down", h)):
-            qt, w = shard.tensors[f"blk.0.{name}.weight"]
+            qt, w = shard.tensors[synth.layer_tensor(0, name)]
             _r0, nr, c0, nc = sl[name]
             part = O.matmul(qt, vec[c0:c0 + nc], w, nr, nc, nthreads=1)
             t = torch.from_numpy(part.copy())
             dist.all_reduce(t)
-            qf, wf = full.tensors[f"blk.0.{name}.weight"]
+            qf, wf = full.tensors[synth.layer_tensor(0, name)]
             want = O.matmul_f64(qf, vec, wf, nr, len(vec), nthreads=1)
             res[name] = float(np.abs(t.numpy() - want).max() / (np.abs(want).max() + 1e-30))
         logits = rng.normal(size=CFG.vocab).astype(np.float32)
