@@ -189,3 +189,29 @@ def test_device_model_wiring_uses_gguf_names(monkeypatch):
             qt, arr = host.tensors[synth.layer_tensor(l, role)]
             assert d[role].arr is arr and d[role + "_type"] == qt
         assert d["attn_norm"].arr is host.tensors[f"blk.{l}.attn_norm.weight"][1]
+
+
+def test_device_drawn_model_wiring(monkeypatch):
+    """synth_on_device names its buffers as synth_model names its tensors,
+    and the layer table finds them (library calls stubbed)."""
+    import goinfer_cuda as G
+
+    class Buf:
+        def __init__(self, key):
+            self.key, self.handle = key, hash(key)
+
+    drawn, tables = [], []
+    monkeypatch.setattr(G, "CreateBuffer", lambda arr: Buf(("ones", arr.size)))
+    monkeypatch.setattr(G, "synth_buffer",
+                        lambda qt, seed, std, rows, cols, row0=0, col0=0: drawn.append((seed, rows, cols)) or
+                        Buf((seed, rows, cols)))
+    monkeypatch.setattr(G, "layer_table", lambda layers: tables.append(layers) or layers)
+    dev = synth.DeviceModel.synth_on_device(TP, seed=3, rank=1, world=2)
+    assert set(dev.bufs) == set(synth.synth_model(TP, seed=3, rank=1, world=2).tensors)
+    (layers,) = tables
+    shard = synth.shard_config(TP, 2)
+    for l, d in enumerate(layers):
+        for role in synth.LAYER_MATS:
+            assert d[role] is dev.bufs[synth.layer_tensor(l, role)]
+    assert dev.bufs["blk.0.attn_q.weight"].key[1:] == (shard.q_dim, TP.dim)
+    assert dev.bufs["blk.0.attn_output.weight"].key[1:] == (TP.dim, shard.q_dim)
