@@ -200,6 +200,10 @@ class DeviceModel:
                 d[name + "_type"] = self.types[key]
             d["attn_norm"] = self.bufs[f"blk.{l}.attn_norm.weight"]
             d["ffn_norm"] = self.bufs[f"blk.{l}.ffn_norm.weight"]
+            # optional Q, K, V biases (Qwen 2; forward.go:211-225)
+            for key, bias in (("bq", "attn_q"), ("bk", "attn_k"), ("bv", "attn_v")):
+                if f"blk.{l}.{bias}.bias" in self.bufs:
+                    d[key] = self.bufs[f"blk.{l}.{bias}.bias"]
             layers.append(d)
         self.table = G.layer_table(layers)
 

@@ -478,6 +478,13 @@ int ref_forward(const ref_model* m, float* key, float* value, int token, int pos
     rc |= mm(m, &L->wq, q, xb, dim, dim);
     rc |= mm(m, &L->wk, k, xb, kv_dim, dim);
     rc |= mm(m, &L->wv, v, xb, kv_dim, dim);
+    /* forward.go:211-225: a.Q[i] += b for each bias that is present */
+    if (L->bq)
+      for (int i = 0; i < dim; i++) q[i] = q[i] + L->bq[i];
+    if (L->bk)
+      for (int i = 0; i < kv_dim; i++) k[i] = k[i] + L->bk[i];
+    if (L->bv)
+      for (int i = 0; i < kv_dim; i++) v[i] = v[i] + L->bv[i];
     for (int h = 0; h < m->n_heads; h++) ref_apply_rope(q + h * hd, pos, hd, m->rope_theta);
     for (int h = 0; h < m->n_kv_heads; h++) ref_apply_rope(k + h * hd, pos, hd, m->rope_theta);
     const int slot = pos % m->max_seq;

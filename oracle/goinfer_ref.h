@@ -105,6 +105,11 @@ typedef struct {
   ref_mat wq, wk, wv, wo, gate, up, down;
   const float* attn_norm; /* dim */
   const float* ffn_norm;  /* dim */
+  /* optional Q, K, V biases (NULL when absent; Qwen 2): dim, kv_dim, kv_dim
+   * floats added after the projections (forward.go:211-225) */
+  const float* bq;
+  const float* bk;
+  const float* bv;
 } ref_layer;
 
 typedef struct {

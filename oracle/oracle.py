@@ -174,7 +174,8 @@ class RefMat(ctypes.Structure):
 
 class RefLayer(ctypes.Structure):
     _fields_ = [("wq", RefMat), ("wk", RefMat), ("wv", RefMat), ("wo", RefMat), ("gate", RefMat),
-                ("up", RefMat), ("down", RefMat), ("attn_norm", ctypes.c_void_p), ("ffn_norm", ctypes.c_void_p)]
+                ("up", RefMat), ("down", RefMat), ("attn_norm", ctypes.c_void_p), ("ffn_norm", ctypes.c_void_p),
+                ("bq", ctypes.c_void_p), ("bk", ctypes.c_void_p), ("bv", ctypes.c_void_p)]
 
 
 class RefModelC(ctypes.Structure):
@@ -253,13 +254,21 @@ class RefModel:
             self._keep.append(arr)
             return arr.ctypes.data
 
+        def bias(name, n):  # optional (forward.go:211-225): NULL when the model has none
+            if name not in tensors:
+                return None
+            if np.asarray(tensors[name][1]).size != n:
+                raise ValueError(f"{name}: {np.asarray(tensors[name][1]).size} values, expected {n}")
+            return vec(name)
+
         layers = (RefLayer * cfg.n_layers)()
         for l in range(cfg.n_layers):
             p = f"blk.{l}."
             layers[l] = RefLayer(mat(p + "attn_q.weight"), mat(p + "attn_k.weight"), mat(p + "attn_v.weight"),
                                  mat(p + "attn_output.weight"), mat(p + "ffn_gate.weight"), mat(p + "ffn_up.weight"),
                                  mat(p + "ffn_down.weight"), vec(p + "attn_norm.weight"),
-                                 vec(p + "ffn_norm.weight"))
+                                 vec(p + "ffn_norm.weight"), bias(p + "attn_q.bias", cfg.q_dim),
+                                 bias(p + "attn_k.bias", cfg.kv_dim), bias(p + "attn_v.bias", cfg.kv_dim))
         self._layers = layers
         self.c = RefModelC(cfg.n_layers, cfg.dim, cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.vocab, cfg.max_seq,
                            cfg.eps, cfg.rope_theta, mat("token_embd.weight"), vec("output_norm.weight"),

@@ -181,6 +181,8 @@ def test_device_model_wiring_uses_gguf_names(monkeypatch):
     monkeypatch.setattr(G, "CreateBuffer", lambda arr: Buf(arr))
     monkeypatch.setattr(G, "layer_table", lambda layers: tables.append(layers) or layers)
     host = synth.synth_model(SMALL, seed=5)
+    bq = np.ones(SMALL.q_dim, np.float32)
+    host.tensors["blk.0.attn_q.bias"] = (gguf.GGML_F32, bq)  # layer 0 only, as a Qwen 2 model has
     dev = synth.DeviceModel(host)
     (layers,) = tables
     assert len(layers) == SMALL.n_layers
@@ -189,6 +191,8 @@ def test_device_model_wiring_uses_gguf_names(monkeypatch):
             qt, arr = host.tensors[synth.layer_tensor(l, role)]
             assert d[role].arr is arr and d[role + "_type"] == qt
         assert d["attn_norm"].arr is host.tensors[f"blk.{l}.attn_norm.weight"][1]
+        assert "bk" not in d and "bv" not in d
+    assert layers[0]["bq"].arr is bq and "bq" not in layers[1]
 
 
 def test_device_drawn_model_wiring(monkeypatch):

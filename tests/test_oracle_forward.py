@@ -10,6 +10,7 @@ restatement of Engine.Forward (forward.go:140-297) on a small model.
 import math
 
 import numpy as np
+import pytest
 
 import goinfer_cuda as G
 import oracle as O
@@ -102,6 +103,10 @@ def py_forward(cfg, W, kc, vc, token, pos):
         q = mm(p + "attn_q.weight", xb, cfg.q_dim)
         k = mm(p + "attn_k.weight", xb, cfg.kv_dim)
         v = mm(p + "attn_v.weight", xb, cfg.kv_dim)
+        for vec, bname in ((q, "attn_q.bias"), (k, "attn_k.bias"), (v, "attn_v.bias")):  # forward.go:211-225
+            if p + bname in W:
+                for i, b in enumerate(W[p + bname][1]):
+                    vec[i] = f32(vec[i] + f32(b))
         for h in range(cfg.n_heads):
             seg = q[h * hd:(h + 1) * hd]; rope(seg, pos); q[h * hd:(h + 1) * hd] = seg
         for h in range(cfg.n_kv_heads):
@@ -163,6 +168,31 @@ def test_forward_matches_python_restatement():
         got = ref.forward(tok, pos)
         want = py_forward(cfg, W, kc, vc, tok, pos)
         assert np.array_equal(got, want), f"pos {pos}: max diff {np.abs(got - want).max()}"
+
+
+def test_forward_with_qkv_biases_matches_python_restatement():
+    """Qwen 2-style Q/K/V biases (forward.go:211-225), added after the
+    projections in both restatements; they change the logits."""
+    cfg = synth.LlamaConfig(n_layers=2, dim=16, hidden=24, n_heads=4, n_kv_heads=2, vocab=11, max_seq=4,
+                            rope_theta=10000.0)
+    W = f32_model(cfg, 6)
+    rng = np.random.default_rng(8)
+    plain = O.RefModel(cfg, dict(W), nthreads=1)
+    for l in range(cfg.n_layers):
+        for name, n in (("attn_q", cfg.q_dim), ("attn_k", cfg.kv_dim), ("attn_v", cfg.kv_dim)):
+            W[f"blk.{l}.{name}.bias"] = (G.TYPE_F32, rng.normal(0, 0.5, n).astype(np.float32))
+    ref = O.RefModel(cfg, W, nthreads=2)
+    kc = [[[f32(0)] * cfg.kv_dim for _ in range(cfg.max_seq)] for _ in range(cfg.n_layers)]
+    vc = [[[f32(0)] * cfg.kv_dim for _ in range(cfg.max_seq)] for _ in range(cfg.n_layers)]
+    for pos, tok in enumerate([4, 1, 9, 3, 0]):
+        got = ref.forward(tok, pos)
+        want = py_forward(cfg, W, kc, vc, tok, pos)
+        assert np.array_equal(got, want), f"pos {pos}: max diff {np.abs(got - want).max()}"
+        assert not np.array_equal(got, plain.forward(tok, pos))
+    bad = dict(W)
+    bad["blk.0.attn_k.bias"] = (G.TYPE_F32, np.zeros(cfg.kv_dim + 1, np.float32))
+    with pytest.raises(ValueError):
+        O.RefModel(cfg, bad)
 
 
 def test_kv_cache_wrap_slot():  # engine_test.go:194-217: pos 9 of a 4-slot cache lands in slot 1
