@@ -489,6 +489,63 @@ int gi_cuda_gemm_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t 
   return run_host_io(quant_type, y, x, b->dptr, b->bytes, batch_size, rows, cols);
 }
 
+// Gate and up of one FFN against the same host activations, SwiGLU'd:
+// batch 1 is one fused GEMV launch (the decode step's gate/up kernel,
+// silu(g) * u in its epilogue); larger batches run the two dequant-GEMMs of
+// the prefill path and the SwiGLU kernel over the products.
+int gi_cuda_gemm_fused_gate_up_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t gate_buf,
+                                   gi_cuda_buffer_t up_buf, uint32_t batch_size, uint32_t rows,
+                                   uint32_t cols) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  const Buffer* gb = as_buffer(gate_buf);
+  const Buffer* ub = as_buffer(up_buf);
+  if (!gb || !ub || !gb->dptr || !ub->dptr) return fail(-1, "null weight buffer");
+  if (quant_type != GI_TYPE_Q4_K) return fail(-2, "fused gate/up: Q4_K only");
+  if (!y || !x || batch_size == 0) return fail(-4, "null y or x, or batch_size 0");
+  int rc = gi::gemv_check(GI_TYPE_Q4_K, rows, cols);
+  if (rc) return fail(rc, "unsupported shape");
+  const size_t wneed = (size_t)gi::row_bytes(GI_TYPE_Q4_K, cols) * rows;
+  if (gb->bytes < wneed || ub->bytes < wneed) return fail(-4, "weight buffer smaller than rows x cols");
+  const int64_t batch = batch_size;
+  const size_t xbytes = ((sizeof(float) * batch * cols) + 255) & ~(size_t)255;
+  const size_t ybytes = ((sizeof(float) * batch * rows) + 255) & ~(size_t)255;
+  void* xd = nullptr;
+  if ((rc = arena_alloc(xbytes + 2 * ybytes, &xd))) return rc;
+  float* yd = reinterpret_cast<float*>(static_cast<uint8_t*>(xd) + xbytes);
+  float* ud = reinterpret_cast<float*>(static_cast<uint8_t*>(xd) + xbytes + ybytes);
+  GI_CUDA_TRY(cudaMemcpyAsync(xd, x, sizeof(float) * batch * cols, cudaMemcpyHostToDevice, g.stream),
+              "copy x to device");
+  if (batch == 1) {
+    float* ys[2] = {yd, ud};
+    const void* ws[2] = {gb->dptr, ub->dptr};
+    const size_t wb[2] = {gb->bytes, ub->bytes};
+    const int64_t rr[2] = {rows, rows};
+    gi::GemvFuse f;
+    f.ymode = gi::kYSwiGLU;
+    rc = gi::gemv_q4k_fused(2, ys, static_cast<const float*>(xd), ws, wb, rr, cols, f, launch_cfg(false), g.stream);
+  } else {
+    rc = run_dev(GI_TYPE_Q4_K, yd, static_cast<const float*>(xd), gb->dptr, gb->bytes, batch, rows, cols, g.stream,
+                 false);
+    if (!rc)
+      rc = run_dev(GI_TYPE_Q4_K, ud, static_cast<const float*>(xd), ub->dptr, ub->bytes, batch, rows, cols,
+                   g.stream, false);
+    if (!rc && gi::swiglu_launch(yd, ud, batch * rows, g.stream) != cudaSuccess) rc = -5;
+  }
+  if (rc) return fail(rc, rc == -4 ? "unsupported shape" : "kernel launch failed",
+                      rc == -5 ? cudaGetLastError() : cudaSuccess);
+  const size_t yb = sizeof(float) * batch * rows;
+  if (g.batch) {
+    size_t off;
+    if ((rc = pinned_alloc(yb, &off))) return rc;
+    GI_CUDA_TRY(cudaMemcpyAsync(g.pinned + off, yd, yb, cudaMemcpyDeviceToHost, g.stream), "copy y to host");
+    g.pending.push_back({y, off, yb});
+    return 0;
+  }
+  GI_CUDA_TRY(cudaMemcpyAsync(y, yd, yb, cudaMemcpyDeviceToHost, g.stream), "copy y to host");
+  return complete_locked();
+}
+
 #define GI_HOST_GEMV(name, qt)                                                            \
   int name(float* y, const float* x, const void* w, uint32_t rows, uint32_t cols) {        \
     std::lock_guard<std::mutex> lk(g.mu);                                                  \

@@ -278,6 +278,15 @@ __global__ void swiglu_kernel(float* __restrict__ gate, const float* __restrict_
   gate[i] = __fmul_rn(silu, up[i]);
 }
 
+}  // namespace
+
+cudaError_t swiglu_launch(float* gate, const float* up, int64_t n, cudaStream_t s) {
+  if (n <= 0 || n > INT32_MAX) return cudaErrorInvalidValue;
+  return launch(false, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, swiglu_kernel, gate, up, (int)n);
+}
+
+namespace {
+
 // ---- tensor-parallel exchange (TPCoordinator.AllReduce,
 // pkg/distributed/tensor_parallel.go:33-108) --------------------------------
 GI_DEVINL bool wait_flag(const uint32_t* f, uint32_t want, const int* error) {

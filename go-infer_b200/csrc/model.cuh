@@ -103,4 +103,7 @@ class DecodeModel {
 // 10-step Newton square root of forward.go:771-780.
 float attn_scale_for(int head_dim);
 
+// gate[i] = silu(gate[i]) * up[i] for i < n (kernels.go:39-46), on `s`.
+cudaError_t swiglu_launch(float* gate, const float* up, int64_t n, cudaStream_t s);
+
 }  // namespace gi

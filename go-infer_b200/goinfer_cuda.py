@@ -45,7 +45,7 @@ ERR_TIMEOUT = -6
 EXPORTS = (
     "gi_cuda_init", "gi_cuda_init_device", "gi_cuda_is_available", "gi_cuda_begin_batch",
     "gi_cuda_end_batch", "gi_cuda_create_buffer", "gi_cuda_release_buffer", "gi_cuda_gemv_buf",
-    "gi_cuda_gemm_buf", "gi_cuda_gemv_q8_0", "gi_cuda_gemv_q4_k", "gi_cuda_gemv_q6_k",
+    "gi_cuda_gemm_buf", "gi_cuda_gemm_fused_gate_up_buf", "gi_cuda_gemv_q8_0", "gi_cuda_gemv_q4_k", "gi_cuda_gemv_q6_k",
     "gi_cuda_gemm_q8_0", "gi_cuda_gemm_q4_k", "gi_cuda_gemm_q6_k", "gi_cuda_gemv_dev",
     "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl",
     "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize", "gi_quantize_seeded",
@@ -111,6 +111,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "gi_cuda_release_buffer": ([vp], None),
         "gi_cuda_gemv_buf": ([i32, vp, vp, vp, u32, u32], i32),
         "gi_cuda_gemm_buf": ([i32, vp, vp, vp, u32, u32, u32], i32),
+        "gi_cuda_gemm_fused_gate_up_buf": ([i32, vp, vp, vp, vp, u32, u32, u32], i32),
         "gi_cuda_gemv_q8_0": ([f32p, f32p, vp, u32, u32], i32),
         "gi_cuda_gemv_q4_k": ([f32p, f32p, vp, u32, u32], i32),
         "gi_cuda_gemv_q6_k": ([f32p, f32p, vp, u32, u32], i32),
@@ -252,6 +253,16 @@ def MatMulBatchBuf(quant_type: int, y: np.ndarray, x: np.ndarray, buf: Buffer, b
         raise GoInferCudaError("gi_cuda_gemm_buf", ERR_UNAVAILABLE, "bad arguments")
     _err("gi_cuda_gemm_buf", load_library().gi_cuda_gemm_buf(quant_type, _f32_addr(y), _f32_addr(x), buf.handle,
                                                               batch, rows, cols))
+
+
+def MatMulFusedGateUpBatchBuf(quant_type: int, y: np.ndarray, x: np.ndarray, gate: Buffer, up: Buffer,
+                              batch: int, rows: int, cols: int) -> None:
+    """metal.MatMulFusedGateUpBatchBuf (metal_darwin.go:564):
+    y[b*rows + r] = silu(gate x_b)[r] * (up x_b)[r]; Q4_K only."""
+    if gate is None or up is None or y.size < batch * rows or x.size < batch * cols:
+        raise GoInferCudaError("gi_cuda_gemm_fused_gate_up_buf", ERR_UNAVAILABLE, "bad arguments")
+    _err("gi_cuda_gemm_fused_gate_up_buf", load_library().gi_cuda_gemm_fused_gate_up_buf(
+        quant_type, _f32_addr(y), _f32_addr(x), gate.handle, up.handle, batch, rows, cols))
 
 
 def _host_gemv(name: str, y, x, raw, rows, cols):

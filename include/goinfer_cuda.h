@@ -86,6 +86,17 @@ int gi_cuda_gemv_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t 
 int gi_cuda_gemm_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t w_buf,
                      uint32_t batch_size, uint32_t rows, uint32_t cols);
 
+/* Replaces int metal_gemm_fused_gate_up_buf(int quant_type, float* y,
+ * const float* x, metal_buffer_t gate_buf, metal_buffer_t up_buf,
+ * uint32_t batch_size, uint32_t rows, uint32_t cols), metal_bridge.h:51:
+ * Y[b][r] = silu(G x_b)[r] * (U x_b)[r] (SwiGLU of kernels.go:39-46) with
+ * host y/x and device-resident gate/up buffers of rows x cols.  Q4_K only,
+ * as the reference (-2 for other types, metal_bridge_darwin.m:3547); -1
+ * for a null buffer. */
+int gi_cuda_gemm_fused_gate_up_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t gate_buf,
+                                   gi_cuda_buffer_t up_buf, uint32_t batch_size, uint32_t rows,
+                                   uint32_t cols);
+
 /* Replace metal_gemv_q8_0 / metal_gemv_q4_k / metal_gemv_q6_k,
  * metal_bridge.h:181-183: host y, x and host weight bytes (copied per call). */
 int gi_cuda_gemv_q8_0(float* y, const float* x, const void* w, uint32_t rows, uint32_t cols);
