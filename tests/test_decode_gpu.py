@@ -210,3 +210,27 @@ def test_model_from_gguf_file(tmp_path):
     finally:
         model.close()
         dev.close()
+
+
+def test_qkv_biases_match_oracle():
+    """Qwen 2-style Q/K/V biases (forward.go:211-225) through the device
+    decode loop: ids identical to the oracle's, logits within the bar, and
+    the biases change the logits."""
+    cfg = synth.LlamaConfig(n_layers=2, dim=512, hidden=1024, n_heads=8, n_kv_heads=2, vocab=1000, max_seq=64)
+    host = synth.synth_model(cfg, seed=31)
+    rng = np.random.default_rng(32)
+    for l in range(cfg.n_layers):
+        for name, n in (("attn_q", cfg.q_dim), ("attn_k", cfg.kv_dim), ("attn_v", cfg.kv_dim)):
+            host.tensors[f"blk.{l}.{name}.bias"] = (G.TYPE_F32, rng.normal(0, 0.3, n).astype(np.float32))
+    dev = synth.DeviceModel(host)
+    model = dev.model()
+    try:
+        prompt = rng.integers(0, cfg.vocab, 6)
+        check_greedy(model, O.RefModel(cfg, host.tensors), prompt, 8)
+        plain = {k: v for k, v in host.tensors.items() if not k.endswith(".bias")}
+        _w, _m, plain_logits = O.RefModel(cfg, plain).greedy(prompt, 8)
+        _w, _m, bias_logits = O.RefModel(cfg, host.tensors).greedy(prompt, 8)
+        assert not np.allclose(plain_logits, bias_logits)
+    finally:
+        model.close()
+        dev.close()

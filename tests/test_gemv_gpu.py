@@ -295,3 +295,29 @@ def test_pinned_host_output_written_directly(qt):
             assert np.array_equal(yb_pin.view(np.uint32), yb_page.view(np.uint32))
     finally:
         G.ReleaseBuffer(buf)
+
+
+@pytest.mark.parametrize("batch", [1, 3, 16])
+def test_fused_gate_up_swiglu_matches_oracle(batch):
+    """gi_cuda_gemm_fused_gate_up_buf (metal_gemm_fused_gate_up_buf,
+    metal_bridge.h:51): y[b*rows + r] = silu(G x_b)[r] * (U x_b)[r], the
+    SwiGLU of kernels.go:39-46; one fused GEMV for a single token, the
+    prefill GEMMs for a batch; Q4_K only (-2 otherwise, as the reference)."""
+    rows, cols = 100, 512
+    graw = G.quantize(G.TYPE_Q4_K, seeded_weights(51, rows, cols))
+    uraw = G.quantize(G.TYPE_Q4_K, seeded_weights(52, rows, cols))
+    x = np.stack([seeded_x(60 + b, cols) for b in range(batch)])
+    gb, ub = G.CreateBuffer(graw), G.CreateBuffer(uraw)
+    try:
+        y = np.full(batch * rows, np.nan, np.float32)
+        G.MatMulFusedGateUpBatchBuf(G.TYPE_Q4_K, y, x.reshape(-1), gb, ub, batch, rows, cols)
+        for b in range(batch):
+            want = O.swiglu(O.matmul(G.TYPE_Q4_K, x[b], graw, rows, cols),
+                            O.matmul(G.TYPE_Q4_K, x[b], uraw, rows, cols))
+            assert_parity(y[b * rows:(b + 1) * rows], want, what=f"token {b}")
+        with pytest.raises(G.GoInferCudaError) as e:
+            G.MatMulFusedGateUpBatchBuf(G.TYPE_Q8_0, y, x.reshape(-1), gb, ub, batch, rows, cols)
+        assert e.value.code == G.ERR_UNSUPPORTED_TYPE
+    finally:
+        G.ReleaseBuffer(gb)
+        G.ReleaseBuffer(ub)
