@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "../../include/goinfer_cuda.h"
+#include "batch_alias.h"
 #include "gemm.cuh"
 #include "gemv.cuh"
 #include "model.cuh"
@@ -41,12 +42,6 @@ struct Buffer {
   int device = -1;
 };
 
-struct Pending {
-  float* host_y;
-  size_t off;  // in the pinned staging area
-  size_t bytes;
-};
-
 struct Ctx {
   std::mutex mu;
   bool ready = false;
@@ -58,11 +53,15 @@ struct Ctx {
   int* err_host = nullptr;  // mapped pinned word the kernels set when a bounded wait gives up
   uint8_t* arena = nullptr;  // device activations of host-pointer calls
   size_t arena_cap = 0, arena_used = 0;
-  uint8_t* pinned = nullptr;  // D2H staging while a batch is open
-  size_t pinned_cap = 0, pinned_used = 0;
+  uint8_t* pinned = nullptr;  // D2H staging of a batch's outputs
+  size_t pinned_cap = 0;
   bool batch = false;
   bool pdl = false;
-  std::vector<Pending> pending;
+  // Outputs of the open batch: still in device memory, copied back to their
+  // host buffers when the batch ends; later calls of the batch read them there.
+  gi::PendingOutputs pending;
+  std::vector<void*> spill;  // arena overflow blocks of the open batch
+  size_t spill_bytes = 0;
 };
 
 Ctx g;
@@ -126,7 +125,17 @@ int ensure_ready() {
 int arena_alloc(size_t bytes, void** out) {
   bytes = (bytes + 255) & ~(size_t)255;
   if (g.arena_used + bytes > g.arena_cap) {
-    if (g.arena_used != 0) return fail(-3, "activation arena exhausted inside a batch");
+    if (g.arena_used != 0 && g.batch) {
+      // Earlier calls of the batch keep their data where it is: a separate
+      // block until the batch ends (the arena then grows to the batch's size).
+      void* p = nullptr;
+      GI_CUDA_TRY(cudaMalloc(&p, bytes), "cudaMalloc batch activations");
+      g.spill.push_back(p);
+      g.spill_bytes += bytes;
+      *out = p;
+      return 0;
+    }
+    if (g.arena_used != 0) return fail(-3, "activation arena exhausted");
     if (g.arena) cudaFree(g.arena);
     g.arena = nullptr;
     size_t cap = g.arena_cap ? g.arena_cap : (size_t)8 << 20;
@@ -139,21 +148,88 @@ int arena_alloc(size_t bytes, void** out) {
   return 0;
 }
 
-int pinned_alloc(size_t bytes, size_t* off) {
-  bytes = (bytes + 255) & ~(size_t)255;
-  if (g.pinned_used + bytes > g.pinned_cap) {
-    if (g.pinned_used != 0) return fail(-3, "pinned staging exhausted inside a batch");
+// Copy the batch's pending outputs back to their host buffers, in call
+// order, after everything queued so far; the list is empty afterwards.
+int flush_pending_locked() {
+  if (g.pending.empty()) return 0;
+  const std::vector<gi::PendingOutput> list = g.pending.list();
+  g.pending.clear();
+  size_t total = 0;
+  for (const gi::PendingOutput& p : list) total += (p.bytes + 255) & ~(size_t)255;
+  if (total > g.pinned_cap) {
     if (g.pinned) cudaFreeHost(g.pinned);
     g.pinned = nullptr;
-    size_t cap = g.pinned_cap ? g.pinned_cap : (size_t)8 << 20;
-    while (cap < bytes) cap *= 2;
-    GI_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&g.pinned), cap, cudaHostAllocDefault),
-                "cudaHostAlloc");
+    g.pinned_cap = 0;
+    size_t cap = (size_t)8 << 20;
+    while (cap < total) cap *= 2;
+    GI_CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&g.pinned), cap, cudaHostAllocDefault), "cudaHostAlloc");
     g.pinned_cap = cap;
   }
-  *off = g.pinned_used;
-  g.pinned_used += bytes;
+  size_t off = 0;
+  for (const gi::PendingOutput& p : list) {
+    GI_CUDA_TRY(cudaMemcpyAsync(g.pinned + off, p.dev, p.bytes, cudaMemcpyDeviceToHost, g.stream), "copy y to host");
+    off += (p.bytes + 255) & ~(size_t)255;
+  }
+  GI_CUDA_TRY(cudaStreamSynchronize(g.stream), "batched kernels");
+  off = 0;
+  for (const gi::PendingOutput& p : list) {
+    std::memcpy(const_cast<void*>(p.host), g.pinned + off, p.bytes);
+    off += (p.bytes + 255) & ~(size_t)255;
+  }
   return 0;
+}
+
+// A host input of a call inside a batch: *dev = the device copy of the
+// pending output holding its newest bytes, or nullptr when the host bytes
+// are current (outside a batch, untouched by the batch, or made current by
+// flushing outputs that the range straddles).
+int batch_input(const void* host, size_t bytes, const void** dev) {
+  *dev = nullptr;
+  if (!g.batch) return 0;
+  switch (g.pending.resolve(host, bytes, dev)) {
+    case gi::Resolve::kHost:
+    case gi::Resolve::kDevice:
+      return 0;
+    case gi::Resolve::kFlush:
+      *dev = nullptr;
+      return flush_pending_locked();
+  }
+  return 0;
+}
+
+// Input x of a batched call on the device: a pending output read in place
+// (copied into `slot` when it is not 16-byte aligned), else the host bytes
+// copied into `slot`.
+int stage_input(const float* x, size_t bytes, void* slot, const float** xd) {
+  const void* fwd = nullptr;
+  if (int rc = batch_input(x, bytes, &fwd)) return rc;
+  if (fwd && (reinterpret_cast<uintptr_t>(fwd) & 15) == 0) {
+    *xd = static_cast<const float*>(fwd);
+    return 0;
+  }
+  GI_CUDA_TRY(cudaMemcpyAsync(slot, fwd ? fwd : static_cast<const void*>(x), bytes,
+                              fwd ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, g.stream),
+              "copy x to device");
+  *xd = static_cast<const float*>(slot);
+  return 0;
+}
+
+// After a batch: nothing is in flight; overflow blocks are freed and the
+// arena grows to hold what the batch needed.
+void release_batch_memory_locked() {
+  cudaStreamSynchronize(g.stream);
+  for (void* p : g.spill) cudaFree(p);
+  g.spill.clear();
+  if (g.spill_bytes) {
+    const size_t cap = (g.arena_cap + g.spill_bytes + ((size_t)1 << 20) - 1) & ~(((size_t)1 << 20) - 1);
+    if (g.arena) cudaFree(g.arena);
+    g.arena = nullptr;
+    g.arena_cap = 0;
+    if (cudaMalloc(reinterpret_cast<void**>(&g.arena), cap) == cudaSuccess) g.arena_cap = cap;
+    else g.arena = nullptr;
+    g.spill_bytes = 0;
+  }
+  g.arena_used = 0;
 }
 
 // Finish the host-pointer call: outside a batch wait for the stream.
@@ -212,7 +288,8 @@ int run_host_io(int qtype, float* y, const float* x, const void* wdev, size_t w_
   int rc = batch == 1 ? gi::gemv_check(qtype, rows, cols) : gi::gemm_check(qtype, batch, rows, cols);
   if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : "unsupported shape");
   void *xd, *yd;
-  // One reservation for x and y: the arena can only grow while it is empty.
+  // One reservation for x and y (the arena grows only while it is empty;
+  // inside a batch an overflow takes a block of its own).
   const size_t xbytes = ((sizeof(float) * batch * cols) + 255) & ~(size_t)255;
   if ((rc = arena_alloc(xbytes + sizeof(float) * batch * rows, &xd))) return rc;
   yd = static_cast<uint8_t*>(xd) + xbytes;
@@ -229,19 +306,21 @@ int run_host_io(int qtype, float* y, const float* x, const void* wdev, size_t w_
       cudaGetLastError();
     }
   }
-  GI_CUDA_TRY(cudaMemcpyAsync(xd, x, sizeof(float) * batch * cols, cudaMemcpyHostToDevice, g.stream),
-              "copy x to device");
-  rc = run_dev(qtype, ydirect ? ydirect : static_cast<float*>(yd), static_cast<const float*>(xd), wdev, w_bytes,
-               batch, rows, cols, g.stream, false);
+  const float* xin = static_cast<const float*>(xd);
+  if (g.batch) {  // x may be an output of an earlier call of the batch
+    if ((rc = stage_input(x, sizeof(float) * batch * cols, xd, &xin))) return rc;
+  } else {
+    GI_CUDA_TRY(cudaMemcpyAsync(xd, x, sizeof(float) * batch * cols, cudaMemcpyHostToDevice, g.stream),
+                "copy x to device");
+  }
+  rc = run_dev(qtype, ydirect ? ydirect : static_cast<float*>(yd), xin, wdev, w_bytes, batch, rows, cols,
+               g.stream, false);
   if (rc) return fail(rc, rc == -4 ? "unsupported shape or buffer too small" : "kernel launch failed",
                       rc == -5 ? cudaGetLastError() : cudaSuccess);
   if (ydirect) return complete_locked();
   const size_t yb = sizeof(float) * batch * rows;
-  if (g.batch) {
-    size_t off;
-    if ((rc = pinned_alloc(yb, &off))) return rc;
-    GI_CUDA_TRY(cudaMemcpyAsync(g.pinned + off, yd, yb, cudaMemcpyDeviceToHost, g.stream), "copy y to host");
-    g.pending.push_back({y, off, yb});
+  if (g.batch) {  // y reaches the host when the batch ends
+    g.pending.add(y, yb, yd);
     return 0;
   }
   GI_CUDA_TRY(cudaMemcpyAsync(y, yd, yb, cudaMemcpyDeviceToHost, g.stream), "copy y to host");
@@ -418,14 +497,9 @@ void gi_cuda_end_batch(void) {
   if (!g.ready || !g.batch) return;
   g.batch = false;
   cudaSetDevice(g.device);
-  const cudaError_t e = cudaStreamSynchronize(g.stream);
-  if (e != cudaSuccess) fail(-5, "batched kernels", e);
-  else
-    for (const Pending& p : g.pending) std::memcpy(p.host_y, g.pinned + p.off, p.bytes);
+  flush_pending_locked();  // on failure the reason is in gi_cuda_last_error
+  release_batch_memory_locked();
   check_device_error();
-  g.pending.clear();
-  g.pinned_used = 0;
-  g.arena_used = 0;
 }
 
 gi_cuda_buffer_t gi_cuda_create_buffer(const void* ptr, size_t bytes) {
@@ -514,8 +588,13 @@ int gi_cuda_gemm_fused_gate_up_buf(int quant_type, float* y, const float* x, gi_
   if ((rc = arena_alloc(xbytes + 2 * ybytes, &xd))) return rc;
   float* yd = reinterpret_cast<float*>(static_cast<uint8_t*>(xd) + xbytes);
   float* ud = reinterpret_cast<float*>(static_cast<uint8_t*>(xd) + xbytes + ybytes);
-  GI_CUDA_TRY(cudaMemcpyAsync(xd, x, sizeof(float) * batch * cols, cudaMemcpyHostToDevice, g.stream),
-              "copy x to device");
+  const float* xin = static_cast<const float*>(xd);
+  if (g.batch) {  // x may be an output of an earlier call of the batch
+    if ((rc = stage_input(x, sizeof(float) * batch * cols, xd, &xin))) return rc;
+  } else {
+    GI_CUDA_TRY(cudaMemcpyAsync(xd, x, sizeof(float) * batch * cols, cudaMemcpyHostToDevice, g.stream),
+                "copy x to device");
+  }
   if (batch == 1) {
     float* ys[2] = {yd, ud};
     const void* ws[2] = {gb->dptr, ub->dptr};
@@ -523,27 +602,70 @@ int gi_cuda_gemm_fused_gate_up_buf(int quant_type, float* y, const float* x, gi_
     const int64_t rr[2] = {rows, rows};
     gi::GemvFuse f;
     f.ymode = gi::kYSwiGLU;
-    rc = gi::gemv_q4k_fused(2, ys, static_cast<const float*>(xd), ws, wb, rr, cols, f, launch_cfg(false), g.stream);
+    rc = gi::gemv_q4k_fused(2, ys, xin, ws, wb, rr, cols, f, launch_cfg(false), g.stream);
   } else {
-    rc = run_dev(GI_TYPE_Q4_K, yd, static_cast<const float*>(xd), gb->dptr, gb->bytes, batch, rows, cols, g.stream,
-                 false);
-    if (!rc)
-      rc = run_dev(GI_TYPE_Q4_K, ud, static_cast<const float*>(xd), ub->dptr, ub->bytes, batch, rows, cols,
-                   g.stream, false);
+    rc = run_dev(GI_TYPE_Q4_K, yd, xin, gb->dptr, gb->bytes, batch, rows, cols, g.stream, false);
+    if (!rc) rc = run_dev(GI_TYPE_Q4_K, ud, xin, ub->dptr, ub->bytes, batch, rows, cols, g.stream, false);
     if (!rc && gi::swiglu_launch(yd, ud, batch * rows, g.stream) != cudaSuccess) rc = -5;
   }
   if (rc) return fail(rc, rc == -4 ? "unsupported shape" : "kernel launch failed",
                       rc == -5 ? cudaGetLastError() : cudaSuccess);
   const size_t yb = sizeof(float) * batch * rows;
-  if (g.batch) {
-    size_t off;
-    if ((rc = pinned_alloc(yb, &off))) return rc;
-    GI_CUDA_TRY(cudaMemcpyAsync(g.pinned + off, yd, yb, cudaMemcpyDeviceToHost, g.stream), "copy y to host");
-    g.pending.push_back({y, off, yb});
+  if (g.batch) {  // y reaches the host when the batch ends
+    g.pending.add(y, yb, yd);
     return 0;
   }
   GI_CUDA_TRY(cudaMemcpyAsync(y, yd, yb, cudaMemcpyDeviceToHost, g.stream), "copy y to host");
   return complete_locked();
+}
+
+// a[i] = a[i] + b[i] (metal_add_residual) or silu(a[i]) * b[i] (metal_swiglu)
+// over host arrays.  Inside a batch, operands that earlier calls of the
+// batch produced are read from the device, and a reaches the host when the
+// batch ends; a that is itself such an output is updated in place there.
+static int host_elementwise(float* a, const float* b, uint32_t n, bool swiglu) {
+  if (!a || !b || n == 0) return fail(-4, "null operand or zero length");
+  const size_t bytes = sizeof(float) * n, slot = (bytes + 255) & ~(size_t)255;
+  void* base = nullptr;
+  int rc = arena_alloc(2 * slot, &base);
+  if (rc) return rc;
+  // b first: a lookup may flush the batch's outputs to the host, and a's
+  // device copy must be taken after the last flush (an in-place update of a
+  // flushed output would not reach the host).  A flush frees nothing, so a
+  // device copy of b found before it stays valid.
+  const void* fb = nullptr;
+  if ((rc = batch_input(b, bytes, &fb))) return rc;
+  const void* fa = nullptr;
+  if ((rc = batch_input(a, bytes, &fa))) return rc;
+  float* ad = fa ? const_cast<float*>(static_cast<const float*>(fa)) : static_cast<float*>(base);
+  if (!fa)
+    GI_CUDA_TRY(cudaMemcpyAsync(ad, a, bytes, cudaMemcpyHostToDevice, g.stream), "copy operand to device");
+  if (!fb) {
+    GI_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(base) + slot, b, bytes, cudaMemcpyHostToDevice, g.stream),
+                "copy operand to device");
+    fb = static_cast<uint8_t*>(base) + slot;
+  }
+  const cudaError_t e = swiglu ? gi::swiglu_launch(ad, static_cast<const float*>(fb), n, g.stream)
+                               : gi::add_launch(ad, static_cast<const float*>(fb), n, g.stream);
+  if (e != cudaSuccess) return fail(-5, swiglu ? "swiglu launch" : "residual add launch", e);
+  if (g.batch) {
+    if (!fa) g.pending.add(a, bytes, ad);
+    return 0;
+  }
+  GI_CUDA_TRY(cudaMemcpyAsync(a, ad, bytes, cudaMemcpyDeviceToHost, g.stream), "copy result to host");
+  return complete_locked();
+}
+
+int gi_cuda_add_residual(float* x, const float* proj, uint32_t dim) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  return host_elementwise(x, proj, dim, false);
+}
+
+int gi_cuda_swiglu(float* gate, const float* up, uint32_t hidden_dim) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  return host_elementwise(gate, up, hidden_dim, true);
 }
 
 #define GI_HOST_GEMV(name, qt)                                                            \
@@ -647,6 +769,8 @@ int gi_cuda_forward_transformer(const float* initial_x, float* out_logits, uint3
   if (int rc = ensure_ready()) return rc;
   Mirror& M = g_mirror;
   if (!M.set) return fail(-1, "gi_cuda_alloc_buffers has not been called");
+  // a synchronous call: inside a batch, initial_x may be an earlier output
+  if (int rc = flush_pending_locked()) return rc;
   if (dim != M.dim || hidden_dim != M.hidden || kv_dim != M.kv_dim || vocab_size != M.vocab ||
       num_layers != M.layers || max_seq != M.max_seq)
     return fail(-4, "sizes differ from gi_cuda_alloc_buffers");

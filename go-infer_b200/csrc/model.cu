@@ -285,6 +285,11 @@ cudaError_t swiglu_launch(float* gate, const float* up, int64_t n, cudaStream_t 
   return launch(false, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, swiglu_kernel, gate, up, (int)n);
 }
 
+cudaError_t add_launch(float* x, const float* p, int64_t n, cudaStream_t s) {
+  if (n <= 0 || n > INT32_MAX) return cudaErrorInvalidValue;
+  return launch(false, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, add_kernel, x, p, (int)n);
+}
+
 namespace {
 
 // ---- tensor-parallel exchange (TPCoordinator.AllReduce,

@@ -105,5 +105,7 @@ float attn_scale_for(int head_dim);
 
 // gate[i] = silu(gate[i]) * up[i] for i < n (kernels.go:39-46), on `s`.
 cudaError_t swiglu_launch(float* gate, const float* up, int64_t n, cudaStream_t s);
+// x[i] += p[i] for i < n (float32 adds, forward.go's residual), on `s`.
+cudaError_t add_launch(float* x, const float* p, int64_t n, cudaStream_t s);
 
 }  // namespace gi

@@ -45,7 +45,8 @@ ERR_TIMEOUT = -6
 EXPORTS = (
     "gi_cuda_init", "gi_cuda_init_device", "gi_cuda_is_available", "gi_cuda_begin_batch",
     "gi_cuda_end_batch", "gi_cuda_create_buffer", "gi_cuda_release_buffer", "gi_cuda_gemv_buf",
-    "gi_cuda_gemm_buf", "gi_cuda_gemm_fused_gate_up_buf", "gi_cuda_gemv_q8_0", "gi_cuda_gemv_q4_k", "gi_cuda_gemv_q6_k",
+    "gi_cuda_gemm_buf", "gi_cuda_gemm_fused_gate_up_buf", "gi_cuda_add_residual", "gi_cuda_swiglu",
+    "gi_cuda_gemv_q8_0", "gi_cuda_gemv_q4_k", "gi_cuda_gemv_q6_k",
     "gi_cuda_gemm_q8_0", "gi_cuda_gemm_q4_k", "gi_cuda_gemm_q6_k", "gi_cuda_gemv_dev",
     "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl",
     "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize", "gi_quantize_seeded",
@@ -112,6 +113,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "gi_cuda_gemv_buf": ([i32, vp, vp, vp, u32, u32], i32),
         "gi_cuda_gemm_buf": ([i32, vp, vp, vp, u32, u32, u32], i32),
         "gi_cuda_gemm_fused_gate_up_buf": ([i32, vp, vp, vp, vp, u32, u32, u32], i32),
+        "gi_cuda_add_residual": ([vp, vp, u32], i32),
+        "gi_cuda_swiglu": ([vp, vp, u32], i32),
         "gi_cuda_gemv_q8_0": ([f32p, f32p, vp, u32, u32], i32),
         "gi_cuda_gemv_q4_k": ([f32p, f32p, vp, u32, u32], i32),
         "gi_cuda_gemv_q6_k": ([f32p, f32p, vp, u32, u32], i32),
@@ -263,6 +266,22 @@ def MatMulFusedGateUpBatchBuf(quant_type: int, y: np.ndarray, x: np.ndarray, gat
         raise GoInferCudaError("gi_cuda_gemm_fused_gate_up_buf", ERR_UNAVAILABLE, "bad arguments")
     _err("gi_cuda_gemm_fused_gate_up_buf", load_library().gi_cuda_gemm_fused_gate_up_buf(
         quant_type, _f32_addr(y), _f32_addr(x), gate.handle, up.handle, batch, rows, cols))
+
+
+def AddResidual(x: np.ndarray, proj: np.ndarray, dim: int) -> None:
+    """metal.AddResidual (metal_darwin.go:743): x[:dim] += proj[:dim], in
+    the open batch's order."""
+    if x.size < dim or proj.size < dim:
+        raise GoInferCudaError("gi_cuda_add_residual", ERR_SHAPE, "bad arguments")
+    _err("gi_cuda_add_residual", load_library().gi_cuda_add_residual(_f32_addr(x), _f32_addr(proj), dim))
+
+
+def SwiGLU(gate: np.ndarray, up: np.ndarray, hidden_dim: int) -> None:
+    """metal.SwiGLU (metal_darwin.go:730): gate = silu(gate) * up over the
+    first hidden_dim values, in the open batch's order."""
+    if gate.size < hidden_dim or up.size < hidden_dim:
+        raise GoInferCudaError("gi_cuda_swiglu", ERR_SHAPE, "bad arguments")
+    _err("gi_cuda_swiglu", load_library().gi_cuda_swiglu(_f32_addr(gate), _f32_addr(up), hidden_dim))
 
 
 def _host_gemv(name: str, y, x, raw, rows, cols):

@@ -59,7 +59,11 @@ bool gi_cuda_is_available(void);
 
 /* Replace void metal_begin_batch(void) / metal_end_batch(void),
  * metal_bridge.h:19-20: between the two calls the host-pointer entry points
- * enqueue without waiting; their y outputs are written at end_batch. */
+ * enqueue without waiting; their outputs reach the host buffers at
+ * end_batch, in call order.  As with Metal's shared memory, a call inside
+ * the batch that reads a host slice an earlier call of the batch wrote sees
+ * that result (it is read from the device; a slice that straddles several
+ * outputs is first written back). */
 void gi_cuda_begin_batch(void);
 void gi_cuda_end_batch(void);
 
@@ -96,6 +100,17 @@ int gi_cuda_gemm_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t 
 int gi_cuda_gemm_fused_gate_up_buf(int quant_type, float* y, const float* x, gi_cuda_buffer_t gate_buf,
                                    gi_cuda_buffer_t up_buf, uint32_t batch_size, uint32_t rows,
                                    uint32_t cols);
+
+/* Replaces int metal_add_residual(float* x, const float* proj, uint32_t dim),
+ * metal_bridge.h:199: x[i] += proj[i] for i < dim (float32 adds).  The
+ * engine calls it on outputs of the same batch without checking the status
+ * (pkg/engine/forward.go:590, 639), so it honours the batch order above. */
+int gi_cuda_add_residual(float* x, const float* proj, uint32_t dim);
+
+/* Replaces int metal_swiglu(float* gate, const float* up, uint32_t hidden_dim),
+ * metal_bridge.h:198: gate[i] = silu(gate[i]) * up[i] with kernels.go:39-46's
+ * roundings (float64 exp); batch order as above (forward.go:624). */
+int gi_cuda_swiglu(float* gate, const float* up, uint32_t hidden_dim);
 
 /* Replace metal_gemv_q8_0 / metal_gemv_q4_k / metal_gemv_q6_k,
  * metal_bridge.h:181-183: host y, x and host weight bytes (copied per call). */

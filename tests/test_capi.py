@@ -98,6 +98,8 @@ def test_no_device_status_codes():
     assert G.CreateBuffer(raw) is None  # nil handle, as metal.CreateBuffer
     assert lib.gi_cuda_gemm_fused_gate_up_buf(G.TYPE_Q4_K, y.ctypes.data, x.ctypes.data, None, None, 1, 16,
                                               256) == G.ERR_UNAVAILABLE
+    assert lib.gi_cuda_add_residual(y.ctypes.data, y.ctypes.data, 16) == G.ERR_UNAVAILABLE
+    assert lib.gi_cuda_swiglu(y.ctypes.data, y.ctypes.data, 16) == G.ERR_UNAVAILABLE
     with pytest.raises(G.GoInferCudaError) as e:
         G.MatMulQ4_K(y, x, raw, 16, 256)
     assert e.value.code == G.ERR_UNAVAILABLE
