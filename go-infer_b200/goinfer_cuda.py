@@ -388,8 +388,30 @@ class Weights:
         MatMulBuf(qtype, y, x, self.bufs[name], rows, cols)
 
     def MatMulBatch(self, y: np.ndarray, x: np.ndarray, name: str, batch: int, rows: int, cols: int) -> bool:
+        """weights.go:328-350: False (the caller then loops MatMul per
+        token) when the tensor is unknown or the batched call fails."""
+        if name not in self.meta or self.bufs.get(name) is None:
+            return False
         qtype, _r, _c = self.meta[name]
-        MatMulBatchBuf(qtype, y, x, self.bufs[name], batch, rows, cols)
+        try:
+            MatMulBatchBuf(qtype, y, x, self.bufs[name], batch, rows, cols)
+        except GoInferCudaError:
+            return False
+        return True
+
+    def MatMulFusedGateUpBatch(self, y: np.ndarray, x: np.ndarray, gate: str, up: str, batch: int, rows: int,
+                               cols: int) -> bool:
+        """weights.go:352-385: y = silu(gate x) * (up x) per token when both
+        tensors are on the device with the same type, else False (the
+        caller then runs gate, up and SwiGLU separately)."""
+        if gate not in self.meta or up not in self.meta:
+            return False
+        if self.meta[gate][0] != self.meta[up][0] or self.bufs.get(gate) is None or self.bufs.get(up) is None:
+            return False
+        try:
+            MatMulFusedGateUpBatchBuf(self.meta[gate][0], y, x, self.bufs[gate], self.bufs[up], batch, rows, cols)
+        except GoInferCudaError:
+            return False
         return True
 
     def Close(self) -> None:

@@ -104,3 +104,37 @@ def test_no_device_status_codes():
         G.MatMulQ4_K(y, x, raw, 16, 256)
     assert e.value.code == G.ERR_UNAVAILABLE
     assert "init" in lib.gi_cuda_last_error().decode()
+
+
+def test_weights_mirror_batch_fallbacks(monkeypatch):
+    """weights.go's MatMulBatch / MatMulFusedGateUpBatch report false (the
+    engine then loops per token, or runs gate, up and SwiGLU apart) for an
+    unknown tensor, mismatched gate/up types or a failing call (library
+    calls stubbed: no device)."""
+    calls = []
+
+    def fake_batch(qt, y, x, buf, batch, rows, cols):
+        calls.append(("batch", qt, buf, batch, rows, cols))
+        if qt == G.TYPE_Q8_0:
+            raise G.GoInferCudaError("gi_cuda_gemm_buf", G.ERR_SHAPE)
+
+    def fake_fused(qt, y, x, gb, ub, batch, rows, cols):
+        calls.append(("fused", qt, gb, ub, batch, rows, cols))
+        if qt != G.TYPE_Q4_K:
+            raise G.GoInferCudaError("gi_cuda_gemm_fused_gate_up_buf", G.ERR_UNSUPPORTED_TYPE)
+
+    monkeypatch.setattr(G, "MatMulBatchBuf", fake_batch)
+    monkeypatch.setattr(G, "MatMulFusedGateUpBatchBuf", fake_fused)
+    w = G.Weights()
+    w.meta = {"g": (G.TYPE_Q4_K, 8, 256), "u": (G.TYPE_Q4_K, 8, 256), "u6": (G.TYPE_Q6_K, 8, 256),
+              "q8": (G.TYPE_Q8_0, 8, 256), "g6": (G.TYPE_Q6_K, 8, 256)}
+    w.bufs = {k: f"buf-{k}" for k in w.meta}
+    y, x = np.zeros(16), np.zeros(512)
+    assert w.MatMulBatch(y, x, "g", 2, 8, 256) and calls[-1] == ("batch", G.TYPE_Q4_K, "buf-g", 2, 8, 256)
+    assert not w.MatMulBatch(y, x, "q8", 2, 8, 256)          # the call failed
+    assert not w.MatMulBatch(y, x, "missing", 2, 8, 256)
+    n = len(calls)
+    assert not w.MatMulFusedGateUpBatch(y, x, "g", "u6", 2, 8, 256) and len(calls) == n  # types differ: no call
+    assert w.MatMulFusedGateUpBatch(y, x, "g", "u", 2, 8, 256)
+    assert calls[-1] == ("fused", G.TYPE_Q4_K, "buf-g", "buf-u", 2, 8, 256)
+    assert not w.MatMulFusedGateUpBatch(y, x, "g6", "u6", 2, 8, 256)  # Q6_K: -2, as the reference
