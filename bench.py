@@ -17,7 +17,9 @@ matrix from HBM.
   roofline the Q4_K GEMV kernel: algorithmic bytes per launch / average
            launch time, against the measured HBM copy bandwidth;
   cpu_baseline  the CPU restatement of go-infer's GEMVEngine.MatMulQ4_K on
-           the host cores (rank 0, N=1 only).
+           the host cores (rank 0, N=1 only);
+  step_distribution  p10 / p50 / p90 of the step time over 20 replays of a
+           100-step graph, taken after the timed region (this rank).
 
 --impl reference times go-infer's CPU path (the C restatement in oracle/;
 the Go code cannot be built here) on the same workload and prints the same
@@ -355,6 +357,32 @@ def decode_section(args, world, rank, local, pg):
     return out
 
 
+def step_distribution(capture, steps_per_replay=100, replays=20):
+    """Spread of the step time, outside the timed region: `replays` replays
+    of a graph of `steps_per_replay` steps, each timed with CUDA events on
+    the launching stream (this rank).  An optional statistic: a failure is
+    reported in the line, never raised."""
+    import torch
+    try:
+        g = capture(steps_per_replay)
+        g.replay()
+        torch.cuda.synchronize()
+        per_step = []
+        for _ in range(replays):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            b.synchronize()
+            per_step.append(a.elapsed_time(b) * 1e3 / steps_per_replay)
+        del g
+        p10, p50, p90 = np.percentile(per_step, [10, 50, 90])
+        return {"us_per_step_p10": round(float(p10), 3), "us_per_step_p50": round(float(p50), 3),
+                "us_per_step_p90": round(float(p90), 3), "replays": replays, "steps_per_replay": steps_per_replay}
+    except Exception as exc:  # noqa: BLE001
+        return {"error": f"{type(exc).__name__}: {exc}"[:200]}
+
+
 def run_ours(args):
     import torch
     import goinfer_cuda as G
@@ -427,6 +455,7 @@ def run_ours(args):
     launch_ms = ms / (2 * args.steps)  # this rank's average Q4_K GEMV launch
     achieved = (STEP_BYTES / 2) / (launch_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
+    dist = step_distribution(capture)
 
     # e2e through the reference-facing C ABI: host x/y, resident weights
     bufs = {k: G.CreateBuffer(v) for k, v in raws.items()}
@@ -484,6 +513,7 @@ def run_ours(args):
                     "d2h_bytes_per_step": 4 * (2 * GATE[0] + DOWN[0]),
                     "api": "gi_cuda_gemv_buf (host y/x, pinned: x copied in, y stored by the kernel)", "steps": e2e_steps},
             "gpu_launches": 2 * args.steps,
+            "step_distribution": dist,
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
             "decode": decode,
