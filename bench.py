@@ -220,7 +220,7 @@ def run_reference(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
         "config": {"workload": WORKLOAD, "rows_sampled": frac},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "nproc": os.cpu_count(), "cpu_model": cpu_model()},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -294,7 +294,8 @@ def decode_section(args, world, rank, local, pg):
             nsteps += 1
         cpu_s = (time.perf_counter() - t0) / nsteps
         out["config4"]["cpu_baseline"] = {"tok_s": round(1.0 / cpu_s, 4), "cores": os.cpu_count(), "kind": "port",
-                                          "sample": f"{nsteps} decode steps of the same model (oracle ref_forward)"}
+                                          "sample": f"{nsteps} decode steps of the same model (oracle ref_forward)",
+                                          "cpu_model": cpu_model()}
         del tensors, ref
     model.close()
     dm.close()
@@ -355,6 +356,19 @@ def decode_section(args, world, rank, local, pg):
         G.ReleaseBuffer(wb)
     out["prefill_config3"] = pre
     return out
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (recorded beside every CPU baseline)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
 
 
 def step_distribution(capture, steps_per_replay=100, replays=20):
@@ -492,7 +506,8 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, cores, sample = cpu_port_gemv_gbs(args.cpu_seconds)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample,
+               "nproc": os.cpu_count(), "cpu_model": cpu_model()}
 
     if rank == 0:
         line = {
