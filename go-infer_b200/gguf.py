@@ -66,9 +66,26 @@ class TensorInfo:
         return n if self.dims else 0
 
 
+_MAX_DEPTH = 8  # nesting of metadata arrays
+_MAX_DIMS = 4   # GGML tensors have at most four dimensions
+
+
+def _min_size(vtype: int) -> int:
+    """Fewest bytes a metadata value of this type occupies."""
+    if vtype in _SCALAR:
+        return struct.calcsize(_SCALAR[vtype])
+    return {T_BOOL: 1, T_STR: 8, T_ARR: 12}.get(vtype, 1)
+
+
 class _Cursor:
     def __init__(self, buf):
         self.buf, self.pos = buf, 0
+
+    def room(self, count: int, each: int, what: str) -> None:
+        """Refuse a count that cannot fit in the bytes left (a corrupted
+        header would otherwise be parsed from the tensor data)."""
+        if count * each > len(self.buf) - self.pos:
+            raise ValueError(f"GGUF {what} count {count} exceeds the file")
 
     def take(self, fmt: str):
         size = struct.calcsize(fmt)
@@ -86,7 +103,7 @@ class _Cursor:
         self.pos += n
         return s
 
-    def value(self, vtype: int):
+    def value(self, vtype: int, depth: int = 0):
         if vtype in _SCALAR:
             return self.take(_SCALAR[vtype])
         if vtype == T_BOOL:
@@ -94,8 +111,11 @@ class _Cursor:
         if vtype == T_STR:
             return self.string()
         if vtype == T_ARR:
+            if depth >= _MAX_DEPTH:
+                raise ValueError("GGUF metadata arrays nested too deeply")
             etype, count = self.take("<I"), self.take("<Q")
-            return [self.value(etype) for _ in range(count)]
+            self.room(count, _min_size(etype), "array")
+            return [self.value(etype, depth + 1) for _ in range(count)]
         raise ValueError(f"unsupported GGUF metadata type {vtype}")
 
 
@@ -126,14 +146,19 @@ class GGUFReader:
         if self.version not in VERSIONS:
             raise ValueError(f"unsupported GGUF version {self.version}")
         n_tensors, n_kv = c.take("<Q"), c.take("<Q")
+        c.room(n_kv, 8 + 4 + 1, "metadata")
         self.metadata = {}
         for _ in range(n_kv):
             key = c.string()
             self.metadata[key] = c.value(c.take("<I"))
+        c.room(n_tensors, 8 + 4 + 4 + 8, "tensor")
         self.tensors = {}
         for _ in range(n_tensors):
             name = c.string()
-            dims = [c.take("<Q") for _ in range(c.take("<I"))]
+            n_dims = c.take("<I")
+            if n_dims > _MAX_DIMS:
+                raise ValueError(f"tensor {name}: {n_dims} dimensions")
+            dims = [c.take("<Q") for _ in range(n_dims)]
             self.tensors[name] = TensorInfo(name, dims, c.take("<I"), c.take("<Q"))
         align = self.metadata.get("general.alignment")
         align = align if isinstance(align, int) and align > 0 else 32
@@ -224,9 +249,11 @@ def _guess_type(value) -> tuple:
         return T_F32, value
     if isinstance(value, str):
         return T_STR, value
-    if isinstance(value, (list, tuple)):
-        et, _ = _guess_type(value[0]) if value else (T_U32, 0)
-        return T_ARR, (et, list(value))
+    if isinstance(value, (list, tuple)):  # homogeneous, typed by the first element; nested arrays too
+        if not value:
+            return T_ARR, (T_U32, [])
+        et, _ = _guess_type(value[0])
+        return T_ARR, (et, [_guess_type(v)[1] for v in value])
     raise TypeError(f"cannot store {type(value)} in GGUF metadata")
 
 

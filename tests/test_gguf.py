@@ -219,3 +219,66 @@ def test_device_drawn_model_wiring(monkeypatch):
             assert d[role] is dev.bufs[synth.layer_tensor(l, role)]
     assert dev.bufs["blk.0.attn_q.weight"].key[1:] == (shard.q_dim, TP.dim)
     assert dev.bufs["blk.0.attn_output.weight"].key[1:] == (TP.dim, shard.q_dim)
+
+
+def test_damaged_files_raise_value_error(tmp_path):
+    """Truncations, flipped bytes and huge counts in a valid file either
+    still parse or raise ValueError -- never another exception, a deep
+    recursion or a header parsed out of the tensor data."""
+    import random
+    good = tmp_path / "good.gguf"
+    gguf.write_gguf(str(good), {"general.architecture": "llama", "llama.block_count": 2,
+                                "names": ["a", "bb", "ccc"], "nested": [[1, 2], [3]],
+                                "f": 0.5},
+                    [("t", gguf.GGML_F32, [8, 2], np.arange(16, dtype=np.float32))])
+    with gguf.GGUFReader(str(good)) as r:
+        assert r.metadata["nested"] == [[1, 2], [3]] and r.metadata["names"] == ["a", "bb", "ccc"]
+    raw = good.read_bytes()
+    rng = random.Random(5)
+    bad = tmp_path / "bad.gguf"
+    outcomes = {"ok": 0, "value_error": 0}
+    for i in range(1500):
+        b = bytearray(raw)
+        kind = i % 3
+        if kind == 0:
+            b = b[:rng.randrange(len(b))]
+        elif kind == 1:
+            for _ in range(rng.randrange(1, 4)):
+                b[rng.randrange(len(b))] = rng.randrange(256)
+        else:  # a huge little-endian count somewhere in the header
+            pos = rng.randrange(0, min(len(b), 200) - 8)
+            b[pos:pos + 8] = rng.choice([2 ** 63 - 1, 2 ** 40, 2 ** 32 + 1, 10 ** 6]).to_bytes(8, "little")
+        bad.write_bytes(bytes(b))
+        try:
+            with gguf.GGUFReader(str(bad)) as r:
+                for name in r.tensors:
+                    try:
+                        r.tensor_data(name)
+                    except (ValueError, KeyError):
+                        pass
+            outcomes["ok"] += 1
+        except ValueError:
+            outcomes["value_error"] += 1
+    assert outcomes["value_error"] > 500 and outcomes["ok"] > 0, outcomes
+
+
+def test_nested_arrays_are_bounded(tmp_path):
+    p = tmp_path / "deep.gguf"
+    body = struct.pack("<IIQQ", gguf.MAGIC, 3, 0, 1) + struct.pack("<Q", 1) + b"k" + struct.pack("<I", gguf.T_ARR)
+    for _ in range(50):  # arrays of one array each, 50 deep
+        body += struct.pack("<IQ", gguf.T_ARR, 1)
+    body += struct.pack("<IQ", gguf.T_U8, 0)
+    p.write_bytes(body)
+    with pytest.raises(ValueError, match="nested"):
+        gguf.GGUFReader(str(p))
+
+
+def test_impossible_counts_are_refused_up_front(tmp_path):
+    p = tmp_path / "count.gguf"
+    p.write_bytes(struct.pack("<IIQQ", gguf.MAGIC, 3, 10 ** 12, 0) + b"\0" * 64)  # 10^12 tensors in 64 bytes
+    with pytest.raises(ValueError, match="exceeds the file"):
+        gguf.GGUFReader(str(p))
+    p.write_bytes(struct.pack("<IIQQ", gguf.MAGIC, 3, 0, 1) + struct.pack("<Q", 1) + b"k"
+                  + struct.pack("<IIQ", gguf.T_ARR, gguf.T_U64, 2 ** 40))  # 2^40 u64 values in 0 bytes
+    with pytest.raises(ValueError, match="exceeds the file"):
+        gguf.GGUFReader(str(p))
