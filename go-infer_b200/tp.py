@@ -35,6 +35,16 @@ def build(cfg: synth.LlamaConfig, seed: int, rank: int, world: int, max_pos: int
     return dev, dev.model(max_pos, tp_rank=rank, tp_world=world)
 
 
+def build_gguf(path: str, rank: int, world: int, max_pos: int = 0, max_seq: int = 8192):
+    """This rank's shard of the model in a GGUF file, sliced at load
+    (gguf.host_model with rank/world), on the device."""
+    import gguf
+
+    with gguf.GGUFReader(path) as r:  # world 1: views of the mapped file, copied to the device here
+        dev = synth.DeviceModel(gguf.host_model(r, max_seq=max_seq, rank=rank, world=world))
+    return dev, dev.model(max_pos, tp_rank=rank, tp_world=world)
+
+
 def greedy(model: G.Model, prompt, n_gen: int):
     """Greedy decode on every rank (identical ids on all ranks)."""
     ids, _logits, ms = model.generate(np.asarray(prompt, np.int32), n_gen)

@@ -282,3 +282,31 @@ def test_impossible_counts_are_refused_up_front(tmp_path):
                   + struct.pack("<IIQ", gguf.T_ARR, gguf.T_U64, 2 ** 40))  # 2^40 u64 values in 0 bytes
     with pytest.raises(ValueError, match="exceeds the file"):
         gguf.GGUFReader(str(p))
+
+
+def test_tp_build_from_gguf_wires_the_rank_shard(tmp_path, monkeypatch):
+    """tp.build_gguf loads rank r's shard of a GGUF file into the device
+    model under the shard configuration (library calls stubbed)."""
+    import goinfer_cuda as G
+    import tp
+
+    p = str(tmp_path / "tp.gguf")
+    gguf.save_model(synth.synth_model(TP, seed=23), p)
+
+    class Buf:
+        def __init__(self, arr):
+            self.arr, self.handle = arr, id(arr)
+
+    made = []
+    monkeypatch.setattr(G, "CreateBuffer", lambda arr: Buf(arr))
+    monkeypatch.setattr(G, "layer_table", lambda layers: layers)
+    monkeypatch.setattr(synth.DeviceModel, "model",
+                        lambda self, max_pos=0, tp_rank=0, tp_world=1: made.append((max_pos, tp_rank, tp_world)) or
+                        "model")
+    dev, model = tp.build_gguf(p, rank=1, world=2, max_pos=64, max_seq=32)
+    assert model == "model" and made == [(64, 1, 2)]
+    want = synth.synth_model(TP, seed=23, rank=1, world=2)
+    assert dev.cfg.q_dim == want.cfg.q_dim and dev.cfg.hidden == want.cfg.hidden
+    for name, (qt, arr) in want.tensors.items():
+        got = dev.bufs[name].arr
+        assert np.array_equal(np.asarray(got).view(np.uint8).reshape(-1), np.asarray(arr).view(np.uint8).reshape(-1))
