@@ -75,6 +75,47 @@ def test_integration_binding_names_declared_functions():
         assert re.search(r"\b" + name + r"\b", text), name
 
 
+def _split_args(text, start):
+    """Top-level comma-separated arguments of the call whose '(' is at start."""
+    depth, args, cur = 0, [], ""
+    for ch in text[start:]:
+        if ch in "([{":
+            depth += 1
+            if depth == 1:
+                continue
+        elif ch in ")]}":
+            depth -= 1
+            if depth == 0:
+                args.append(cur)
+                break
+        if depth == 1 and ch == ",":
+            args.append(cur)
+            cur = ""
+        elif depth >= 1:
+            cur += ch
+    return [a for a in (x.strip() for x in args) if a]
+
+
+def test_integration_binding_argument_counts():
+    """Each C.gi_*(...) call in INTEGRATION.md's Go code passes as many
+    arguments as include/goinfer_cuda.h declares."""
+    header = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    decl = {}
+    for m in re.finditer(r"\b(gi_\w+)\s*\(", header):
+        params = _split_args(header, m.end() - 1)
+        decl[m.group(1)] = 0 if params == ["void"] else len(params)
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    checked = 0
+    for m in re.finditer(r"\bC\.(gi_\w+)\(", doc):
+        name = m.group(1)
+        if name not in decl:
+            continue  # a type conversion such as C.gi_cuda_buffer_t(x)
+        n = len(_split_args(doc, m.end() - 1))
+        assert n == decl[name], f"{name}: {n} arguments in INTEGRATION.md, {decl[name]} declared"
+        checked += 1
+    assert checked >= 10
+
+
 def test_row_bytes_follow_gemv_go():
     # pkg/math/gemv.go:99,135,171
     assert G.row_bytes(G.TYPE_Q8_0, 4096) == 128 * 34
