@@ -1,0 +1,153 @@
+// attn.cuh -- decode attention with GQA over the rolling KV cache
+// (pkg/engine/forward.go:226-266), as device functions of one work item:
+// called by the attention kernels of model.cu (one CTA per item) and by the
+// persistent decode-layer kernel of layers.cu (items looped over its CTAs).
+#pragma once
+
+#include <math.h>
+
+#include "common.cuh"
+#include "model.cuh"
+
+namespace gi {
+
+constexpr int kAttChunk = 32;  // KV positions per attention work item
+
+inline size_t attn_smem_bytes(int kv_mul, int hd) {
+  return sizeof(float) * ((size_t)kv_mul * hd + 2 * (size_t)kAttChunk * hd + (size_t)kv_mul * kAttChunk + 2 * kv_mul);
+}
+
+// ---- attention with GQA (forward.go:226-266), split over KV positions -------
+// CTA (kv head g, chunk c) handles the kv_mul query heads of g against the
+// cache slots [32c, 32c + 32) of the active context.  It applies RoPE
+// (kernels.go:22-36; rope[pos][i] = (cos, sin) of pos / theta^(2i/hd),
+// computed in double on the host and rounded to float32) to its queries as
+// it stages them; the CTA whose chunk holds this step's slot also rotates
+// k, and writes k and v into the cache (forward.go:226-238) — no other CTA
+// reads that slot.  It stages the chunk's K and V rows in shared memory
+// (all loads in flight at once), then writes, per query head, (max, sum of
+// exp, unnormalised output) for attn_combine_kernel.  Scores use the float64
+// exp of kernels.go:60.
+// One (kv head g, chunk c) item, by every thread of the calling CTA; sm:
+// attn_smem_bytes(kv_mul, hd) of shared memory.
+GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* __restrict__ q,
+                                 const float* __restrict__ k, const float* __restrict__ v,
+                                 const float2* __restrict__ rope, float* __restrict__ kc, float* __restrict__ vc,
+                                 float* __restrict__ part, int kv_mul, int hd, int kv_dim, int splits, float scale,
+                                 uint32_t max_pos, int* error, int g, int c, float* sm) {
+  const uint32_t pos = st->pos, slot = st->slot;
+  if (pos >= max_pos) {  // past the RoPE table: report, touch nothing
+    if (g == 0 && c == 0 && threadIdx.x == 0) atomicExch(error, 1);
+    return;
+  }
+  const int active = (int)st->active;
+  const int t0 = c * kAttChunk;
+  const int nt = max(0, min(kAttChunk, active - t0));
+  const int half = hd >> 1, hd4 = hd >> 2;
+  float* qs = sm;                          // [kv_mul][hd]
+  float* ks = qs + kv_mul * hd;            // [kAttChunk][hd]
+  float* vs = ks + kAttChunk * hd;         // [kAttChunk][hd]
+  float* sc = vs + kAttChunk * hd;         // [kv_mul][kAttChunk]
+  float* mx = sc + kv_mul * kAttChunk;     // [kv_mul][2]
+  const float2* cs = rope + (size_t)pos * half;
+  // queries of g's heads, rotated (r0 = v0 c - v1 s, r1 = v0 s + v1 c)
+  const float* qg = q + (size_t)g * kv_mul * hd;
+  for (int i = threadIdx.x; i < kv_mul * half; i += blockDim.x) {
+    const int h = i / half, j = i - h * half;
+    const float2 r = cs[j];
+    const float v0 = qg[h * hd + j], v1 = qg[h * hd + j + half];
+    qs[h * hd + j] = __fsub_rn(__fmul_rn(v0, r.x), __fmul_rn(v1, r.y));
+    qs[h * hd + j + half] = __fadd_rn(__fmul_rn(v0, r.y), __fmul_rn(v1, r.x));
+  }
+  const int cur = (int)slot - t0;  // this step's slot in the chunk, if it is here
+  float4* ks4 = reinterpret_cast<float4*>(ks);
+  float4* vs4 = reinterpret_cast<float4*>(vs);
+  for (int i = threadIdx.x; i < nt * hd4; i += blockDim.x) {
+    const int t = i / hd4, d4 = i - t * hd4;
+    if (t == cur) continue;
+    const size_t off = ((size_t)(t0 + t) * kv_dim + (size_t)g * hd) / 4 + d4;
+    ks4[i] = __ldg(reinterpret_cast<const float4*>(kc) + off);
+    vs4[i] = __ldg(reinterpret_cast<const float4*>(vc) + off);
+  }
+  if (cur >= 0 && cur < nt) {
+    float* krow = kc + (size_t)slot * kv_dim + (size_t)g * hd;
+    float* vrow = vc + (size_t)slot * kv_dim + (size_t)g * hd;
+    for (int j = threadIdx.x; j < half; j += blockDim.x) {
+      const float2 r = cs[j];
+      const float v0 = k[g * hd + j], v1 = k[g * hd + j + half];
+      const float r0 = __fsub_rn(__fmul_rn(v0, r.x), __fmul_rn(v1, r.y));
+      const float r1 = __fadd_rn(__fmul_rn(v0, r.y), __fmul_rn(v1, r.x));
+      ks[cur * hd + j] = r0;
+      ks[cur * hd + j + half] = r1;
+      krow[j] = r0;
+      krow[j + half] = r1;
+    }
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+      const float val = v[g * hd + d];
+      vs[cur * hd + d] = val;
+      vrow[d] = val;
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int p = warp; p < kv_mul * nt; p += nw) {  // one warp per (head, position)
+    const int h = p / nt, t = p - h * nt;
+    float s = 0.f;
+    for (int d = lane; d < hd; d += 32) s = fmaf(qs[h * hd + d], ks[t * hd + d], s);
+    s = warp_sum(s);
+    if (lane == 0) sc[h * kAttChunk + t] = __fmul_rn(s, scale);
+  }
+  __syncthreads();
+  for (int h = warp; h < kv_mul; h += nw) {  // local softmax statistics per head
+    float m = -INFINITY;
+    for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[h * kAttChunk + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < nt; t += 32) {
+      const float e = (float)exp((double)__fsub_rn(sc[h * kAttChunk + t], m));
+      sc[h * kAttChunk + t] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      mx[2 * h] = m;
+      mx[2 * h + 1] = l;
+    }
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < kv_mul * hd; o += blockDim.x) {  // thread per (head, d)
+    const int h = o / hd, d = o - h * hd;
+    float a0 = 0.f, a1 = 0.f;
+    int t = 0;
+    for (; t + 1 < nt; t += 2) {
+      a0 = fmaf(sc[h * kAttChunk + t], vs[t * hd + d], a0);
+      a1 = fmaf(sc[h * kAttChunk + t + 1], vs[(t + 1) * hd + d], a1);
+    }
+    if (t < nt) a0 = fmaf(sc[h * kAttChunk + t], vs[t * hd + d], a0);
+    float* pp = part + ((size_t)(g * kv_mul + h) * splits + c) * (hd + 2);
+    pp[2 + d] = a0 + a1;
+    if (d == 0) {
+      pp[0] = nt > 0 ? mx[2 * h] : -INFINITY;
+      pp[1] = nt > 0 ? mx[2 * h + 1] : 0.f;
+    }
+  }
+}
+
+// Output element (head h, dimension d): the splits' partials merged.
+GI_DEVINL void attn_combine_one(const float* __restrict__ part, float* __restrict__ att, int hd, int splits, int h,
+                                int d) {
+  const float* ph = part + (size_t)h * splits * (hd + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, ph[s * (hd + 2)]);
+  float L = 0.f, acc = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float m = ph[s * (hd + 2)];
+    if (m == -INFINITY) continue;
+    const float f = (float)exp((double)(m - M));
+    L = fmaf(ph[s * (hd + 2) + 1], f, L);
+    acc = fmaf(ph[s * (hd + 2) + 2 + d], f, acc);
+  }
+  if (d < hd) att[(size_t)h * hd + d] = L > 0.f ? acc / L : 0.f;
+}
+
+}  // namespace gi

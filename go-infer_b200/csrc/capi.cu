@@ -909,6 +909,22 @@ int gi_cuda_model_reset(gi_cuda_model_t model) {
   return 0;
 }
 
+int gi_cuda_model_set_persistent(gi_cuda_model_t model, int enable) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!model) return fail(-4, "null model");
+  ModelHandle* h = static_cast<ModelHandle*>(model);
+  GI_CUDA_TRY(cudaStreamSynchronize(g.stream), "persistent layers");
+  if (h->m.graph) {  // captured with the other kind of step
+    cudaGraphExecDestroy(h->m.graph);
+    h->m.graph = nullptr;
+  }
+  const int rc = h->m.set_persistent(enable != 0);
+  if (rc == -2) return fail(rc, "persistent layers need Q4_K layer matrices and no biases");
+  if (rc) return fail(rc, "persistent layer plan", rc == -5 ? cudaGetLastError() : cudaSuccess);
+  return 0;
+}
+
 int gi_cuda_model_generate(gi_cuda_model_t model, const int32_t* tokens, uint32_t n_tokens, uint32_t start_pos,
                            uint32_t n_gen, uint32_t* out_tokens, float* out_logits, float* decode_ms) {
   std::lock_guard<std::mutex> lk(g.mu);

@@ -14,13 +14,13 @@
 #include <cstring>
 #include <vector>
 
+#include "attn.cuh"
 #include "common.cuh"
+#include "layers.cuh"
 #include "model.cuh"
 
 namespace gi {
 namespace {
-
-constexpr int kAttChunk = 32;  // KV positions per attention CTA
 
 // Launch with programmatic dependent launch when `pdl` (every kernel here
 // waits for its predecessor before touching its outputs).
@@ -121,17 +121,7 @@ __global__ void add_kernel(float* __restrict__ y, const float* __restrict__ b, i
   if (i < n) y[i] = __fadd_rn(y[i], b[i]);
 }
 
-// ---- attention with GQA (forward.go:226-266), split over KV positions -------
-// CTA (kv head g, chunk c) handles the kv_mul query heads of g against the
-// cache slots [32c, 32c + 32) of the active context.  It applies RoPE
-// (kernels.go:22-36; rope[pos][i] = (cos, sin) of pos / theta^(2i/hd),
-// computed in double on the host and rounded to float32) to its queries as
-// it stages them; the CTA whose chunk holds this step's slot also rotates
-// k, and writes k and v into the cache (forward.go:226-238) — no other CTA
-// reads that slot.  It stages the chunk's K and V rows in shared memory
-// (all loads in flight at once), then writes, per query head, (max, sum of
-// exp, unnormalised output) for attn_combine_kernel.  Scores use the float64
-// exp of kernels.go:60.
+// ---- attention (attn.cuh): one CTA per work item ----------------------------
 __global__ void __launch_bounds__(256) attn_partial_kernel(const StepState* __restrict__ st,
                                                            const float* __restrict__ q, const float* __restrict__ k,
                                                            const float* __restrict__ v,
@@ -142,121 +132,14 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const StepState* __re
   extern __shared__ __align__(16) float sm[];
   griddep_wait();
   griddep_launch_dependents();
-  const int g = blockIdx.x, c = blockIdx.y;
-  const uint32_t pos = st->pos, slot = st->slot;
-  if (pos >= max_pos) {  // past the RoPE table: report, touch nothing
-    if (g == 0 && c == 0 && threadIdx.x == 0) atomicExch(error, 1);
-    return;
-  }
-  const int active = (int)st->active;
-  const int t0 = c * kAttChunk;
-  const int nt = max(0, min(kAttChunk, active - t0));
-  const int half = hd >> 1, hd4 = hd >> 2;
-  float* qs = sm;                          // [kv_mul][hd]
-  float* ks = qs + kv_mul * hd;            // [kAttChunk][hd]
-  float* vs = ks + kAttChunk * hd;         // [kAttChunk][hd]
-  float* sc = vs + kAttChunk * hd;         // [kv_mul][kAttChunk]
-  float* mx = sc + kv_mul * kAttChunk;     // [kv_mul][2]
-  const float2* cs = rope + (size_t)pos * half;
-  // queries of g's heads, rotated (r0 = v0 c - v1 s, r1 = v0 s + v1 c)
-  const float* qg = q + (size_t)g * kv_mul * hd;
-  for (int i = threadIdx.x; i < kv_mul * half; i += blockDim.x) {
-    const int h = i / half, j = i - h * half;
-    const float2 r = cs[j];
-    const float v0 = qg[h * hd + j], v1 = qg[h * hd + j + half];
-    qs[h * hd + j] = __fsub_rn(__fmul_rn(v0, r.x), __fmul_rn(v1, r.y));
-    qs[h * hd + j + half] = __fadd_rn(__fmul_rn(v0, r.y), __fmul_rn(v1, r.x));
-  }
-  const int cur = (int)slot - t0;  // this step's slot in the chunk, if it is here
-  float4* ks4 = reinterpret_cast<float4*>(ks);
-  float4* vs4 = reinterpret_cast<float4*>(vs);
-  for (int i = threadIdx.x; i < nt * hd4; i += blockDim.x) {
-    const int t = i / hd4, d4 = i - t * hd4;
-    if (t == cur) continue;
-    const size_t off = ((size_t)(t0 + t) * kv_dim + (size_t)g * hd) / 4 + d4;
-    ks4[i] = __ldg(reinterpret_cast<const float4*>(kc) + off);
-    vs4[i] = __ldg(reinterpret_cast<const float4*>(vc) + off);
-  }
-  if (cur >= 0 && cur < nt) {
-    float* krow = kc + (size_t)slot * kv_dim + (size_t)g * hd;
-    float* vrow = vc + (size_t)slot * kv_dim + (size_t)g * hd;
-    for (int j = threadIdx.x; j < half; j += blockDim.x) {
-      const float2 r = cs[j];
-      const float v0 = k[g * hd + j], v1 = k[g * hd + j + half];
-      const float r0 = __fsub_rn(__fmul_rn(v0, r.x), __fmul_rn(v1, r.y));
-      const float r1 = __fadd_rn(__fmul_rn(v0, r.y), __fmul_rn(v1, r.x));
-      ks[cur * hd + j] = r0;
-      ks[cur * hd + j + half] = r1;
-      krow[j] = r0;
-      krow[j + half] = r1;
-    }
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-      const float val = v[g * hd + d];
-      vs[cur * hd + d] = val;
-      vrow[d] = val;
-    }
-  }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int p = warp; p < kv_mul * nt; p += nw) {  // one warp per (head, position)
-    const int h = p / nt, t = p - h * nt;
-    float s = 0.f;
-    for (int d = lane; d < hd; d += 32) s = fmaf(qs[h * hd + d], ks[t * hd + d], s);
-    s = warp_sum(s);
-    if (lane == 0) sc[h * kAttChunk + t] = __fmul_rn(s, scale);
-  }
-  __syncthreads();
-  for (int h = warp; h < kv_mul; h += nw) {  // local softmax statistics per head
-    float m = -INFINITY;
-    for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[h * kAttChunk + t]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int t = lane; t < nt; t += 32) {
-      const float e = (float)exp((double)__fsub_rn(sc[h * kAttChunk + t], m));
-      sc[h * kAttChunk + t] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      mx[2 * h] = m;
-      mx[2 * h + 1] = l;
-    }
-  }
-  __syncthreads();
-  for (int o = threadIdx.x; o < kv_mul * hd; o += blockDim.x) {  // thread per (head, d)
-    const int h = o / hd, d = o - h * hd;
-    float a0 = 0.f, a1 = 0.f;
-    int t = 0;
-    for (; t + 1 < nt; t += 2) {
-      a0 = fmaf(sc[h * kAttChunk + t], vs[t * hd + d], a0);
-      a1 = fmaf(sc[h * kAttChunk + t + 1], vs[(t + 1) * hd + d], a1);
-    }
-    if (t < nt) a0 = fmaf(sc[h * kAttChunk + t], vs[t * hd + d], a0);
-    float* pp = part + ((size_t)(g * kv_mul + h) * splits + c) * (hd + 2);
-    pp[2 + d] = a0 + a1;
-    if (d == 0) {
-      pp[0] = nt > 0 ? mx[2 * h] : -INFINITY;
-      pp[1] = nt > 0 ? mx[2 * h + 1] : 0.f;
-    }
-  }
+  attn_partial_item(st, q, k, v, rope, kc, vc, part, kv_mul, hd, kv_dim, splits, scale, max_pos, error, blockIdx.x,
+                    blockIdx.y, sm);
 }
 
 __global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ att, int hd, int splits) {
   griddep_wait();
   griddep_launch_dependents();
-  const int h = blockIdx.x, d = threadIdx.x;
-  const float* ph = part + (size_t)h * splits * (hd + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, ph[s * (hd + 2)]);
-  float L = 0.f, acc = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    const float m = ph[s * (hd + 2)];
-    if (m == -INFINITY) continue;
-    const float f = (float)exp((double)(m - M));
-    L = fmaf(ph[s * (hd + 2) + 1], f, L);
-    acc = fmaf(ph[s * (hd + 2) + 2 + d], f, acc);
-  }
-  if (d < hd) att[(size_t)h * hd + d] = L > 0.f ? acc / L : 0.f;
+  attn_combine_one(part, att, hd, splits, blockIdx.x, threadIdx.x);
 }
 
 // ---- residual add (forward.go:271-273, 285-287) ------------------------------
@@ -443,10 +326,6 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   }
 }
 
-size_t attn_smem_bytes(int kv_mul, int hd) {
-  return sizeof(float) * ((size_t)kv_mul * hd + 2 * (size_t)kAttChunk * hd + (size_t)kv_mul * kAttChunk + 2 * kv_mul);
-}
-
 template <typename T>
 int dev_alloc(T** p, size_t n, size_t* total) {
   if (cudaMalloc(reinterpret_cast<void**>(p), sizeof(T) * (n ? n : 1)) != cudaSuccess) return -5;
@@ -468,6 +347,7 @@ float attn_scale_for(int head_dim) {
 
 DecodeModel::~DecodeModel() {
   if (graph) cudaGraphExecDestroy(graph);
+  layers_plan_free(plan_);
   for (void* p : {(void*)x_, (void*)xb_, (void*)q_, (void*)k_, (void*)v_, (void*)att_, (void*)proj_, (void*)gate_,
                   (void*)up_, (void*)logits_, (void*)kcache_, (void*)vcache_, (void*)part_, (void*)rope_, (void*)st_,
                   (void*)tokens_out_})
@@ -551,6 +431,16 @@ void DecodeModel::bind(const LayerRef* layers, const MatRef& tok_embd, const flo
   tok_embd_ = tok_embd;
   out_norm_ = out_norm;
   out_ = out;
+  if (plan_ && set_persistent(true)) set_persistent(false);  // the plan holds the weight pointers
+}
+
+int DecodeModel::set_persistent(bool on) {
+  layers_plan_free(plan_);
+  plan_ = nullptr;
+  if (!on) return 0;
+  if (int rc = layers_prepare_device()) return rc;
+  return layers_plan_build(layers_, n_layers_, cfg_, x_, q_, k_, v_, att_, gate_, up_,
+                           cfg_.tp_world > 1 ? &tp_ : nullptr, sm_count_, &plan_);
 }
 
 void DecodeModel::reset_cache(cudaStream_t s) {
@@ -606,7 +496,24 @@ int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
   }
   const size_t layer_kv = (size_t)c.max_seq * kv_dim;
   const size_t att_smem = attn_smem_bytes(kv_mul, hd);
-  for (int l = 0; l < n_layers_; ++l) {
+  if (plan_) {  // every layer in one persistent launch
+    LayersCfg a;
+    a.n_layers = n_layers_;
+    a.st = st_;
+    a.q = q_, a.k = k_, a.v = v_, a.att = att_, a.part = part_;
+    a.kcache = kcache_, a.vcache = vcache_;
+    a.rope = rope_;
+    a.layer_kv = layer_kv;
+    a.kv_mul = kv_mul, a.hd = hd, a.kv_dim = kv_dim, a.n_kv_heads = c.n_kv_heads, a.n_heads = c.n_heads;
+    a.splits = att_splits_;
+    a.scale = c.attn_scale;
+    a.max_pos = (uint32_t)c.max_pos;
+    a.error = scratch_.error;
+    rc = layers_enqueue(plan_, a, s);
+    if (rc) return rc;
+  }
+  const int n_launched = plan_ ? 0 : n_layers_;  // layers run by per-layer launches
+  for (int l = 0; l < n_launched; ++l) {
     const LayerRef& Ly = layers_[l];
     float* kc = kcache_ + l * layer_kv;
     float* vc = vcache_ + l * layer_kv;
@@ -702,7 +609,9 @@ int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
     }
     if (rc) return rc;
   }
-  e = launch(pdl, dim3(1), dim3(1024), 0, s, rmsnorm_kernel, (const float*)x_, out_norm_, xb_, c.dim, c.eps);
+  // after the cooperative layers kernel: plain stream order
+  e = launch(pdl && !plan_, dim3(1), dim3(1024), 0, s, rmsnorm_kernel, (const float*)x_, out_norm_, xb_, c.dim,
+             c.eps);
   if (e != cudaSuccess) return -5;
   rc = gemv_launch(out_.qtype, logits_, xb_, out_.w, out_.bytes, c.vocab, c.dim, scratch_, L, s);
   if (rc) return rc;

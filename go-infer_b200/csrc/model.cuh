@@ -12,6 +12,8 @@
 
 namespace gi {
 
+struct LayersPlan;  // layers.cuh
+
 // One weight matrix in device memory: raw GGUF rows (rows = outputs),
 // `qtype` a GGML id (F32 rows are float32).
 struct MatRef {
@@ -65,6 +67,12 @@ class DecodeModel {
   // Re-point the weights (same shapes) without touching the KV cache.
   void bind(const LayerRef* layers, const MatRef& tok_embd, const float* out_norm, const MatRef& out);
   int project_partial(const MatRef& W, const float* in, int cols, cudaStream_t s, bool pdl);
+  // Run the layers of each step as one persistent cooperative kernel
+  // (layers.cu) instead of six launches per layer: 0, or -2 when a layer
+  // matrix is not Q4_K or biases are present, -4 when its shared-memory
+  // layout does not fit, -5 on a CUDA error.  Off by default.
+  int set_persistent(bool on);
+  bool persistent() const { return plan_ != nullptr; }
 
   const ModelCfg& cfg() const { return cfg_; }
   float* x() const { return x_; }
@@ -97,6 +105,7 @@ class DecodeModel {
   int max_out_ = 0;
   int att_splits_ = 1;
   size_t dev_bytes_ = 0;
+  LayersPlan* plan_ = nullptr;
 };
 
 // attn_scale of forward.go:33: float32(1 / math_sqrt(headDim)) with the

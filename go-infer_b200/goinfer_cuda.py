@@ -51,7 +51,7 @@ EXPORTS = (
     "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl",
     "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize", "gi_quantize_seeded",
     "gi_cuda_alloc_buffers", "gi_cuda_forward_transformer", "gi_cuda_model_create", "gi_cuda_model_destroy",
-    "gi_cuda_model_reset", "gi_cuda_model_generate", "gi_cuda_tp_prepare", "gi_cuda_tp_connect", "gi_cuda_tp_close",
+    "gi_cuda_model_reset", "gi_cuda_model_set_persistent", "gi_cuda_model_generate", "gi_cuda_tp_prepare", "gi_cuda_tp_connect", "gi_cuda_tp_close",
     "gi_cuda_alloc_buffer", "gi_synth_weights", "gi_cuda_buffer_read",
 )
 
@@ -147,6 +147,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
                               ctypes.c_int64], i32),
         "gi_cuda_model_destroy": ([vp], None),
         "gi_cuda_model_reset": ([vp], i32),
+        "gi_cuda_model_set_persistent": ([vp, i32], i32),
         "gi_cuda_model_generate": ([vp, ctypes.POINTER(ctypes.c_int32), u32, u32, u32, ctypes.POINTER(u32), f32p,
                                     f32p], i32),
     }
@@ -500,6 +501,10 @@ class Model:
 
     def reset(self) -> None:
         _err("gi_cuda_model_reset", load_library().gi_cuda_model_reset(self.handle))
+
+    def set_persistent(self, enable: bool = True) -> None:
+        """Run each step's layers as one persistent kernel (Q4_K layers, no biases)."""
+        _err("gi_cuda_model_set_persistent", load_library().gi_cuda_model_set_persistent(self.handle, int(enable)))
 
     def close(self) -> None:
         if self.handle:

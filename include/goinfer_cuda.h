@@ -240,6 +240,17 @@ void gi_cuda_model_destroy(gi_cuda_model_t model);
 /* Zeroes the KV cache. */
 int gi_cuda_model_reset(gi_cuda_model_t model);
 
+/* Runs the layers of each decode step as one persistent cooperative kernel
+ * (one CTA per SM; the phases of every layer separated by grid-wide
+ * barriers, each projection's first weights requested before the barrier
+ * in front of it) instead of six launches per layer; enable = 0 returns to
+ * the per-layer launches.  No reference counterpart: the reference runs a
+ * step as separate Metal dispatches.  The arithmetic is the per-layer
+ * kernels' own.  Needs every layer matrix in Q4_K and no biases, else
+ * GI_ERR_UNSUPPORTED_TYPE (-2); off by default.  The step is captured again
+ * at the next gi_cuda_model_generate. */
+int gi_cuda_model_set_persistent(gi_cuda_model_t model, int enable);
+
 /* Runs tokens[0..n_tokens) at positions start_pos.. (one step each), then
  * greedy steps: out_tokens[0..n_gen) are the argmax after the last prompt
  * token and after each generated token (n_gen >= 1).  out_logits (host

@@ -80,6 +80,7 @@ cudaError_t cudaStreamBeginCapture(cudaStream_t s, cudaStreamCaptureMode m);
 cudaError_t cudaStreamEndCapture(cudaStream_t s, cudaGraph_t* g);
 cudaError_t cudaGraphInstantiate(cudaGraphExec_t* e, cudaGraph_t g, unsigned long long flags = 0);
 cudaError_t cudaGraphDestroy(cudaGraph_t g);
+cudaError_t cudaGraphExecDestroy(cudaGraphExec_t e);
 cudaError_t cudaGraphLaunch(cudaGraphExec_t e, cudaStream_t s);
 cudaError_t cudaIpcGetMemHandle(cudaIpcMemHandle_t* h, void* p);
 cudaError_t cudaIpcOpenMemHandle(void** p, cudaIpcMemHandle_t h, unsigned flags);

@@ -164,6 +164,7 @@ cudaError_t cudaStreamBeginCapture(cudaStream_t, cudaStreamCaptureMode) { return
 cudaError_t cudaStreamEndCapture(cudaStream_t, cudaGraph_t*) { return cudaErrorNotSupported; }
 cudaError_t cudaGraphInstantiate(cudaGraphExec_t*, cudaGraph_t, unsigned long long) { return cudaErrorNotSupported; }
 cudaError_t cudaGraphDestroy(cudaGraph_t) { return cudaSuccess; }
+cudaError_t cudaGraphExecDestroy(cudaGraphExec_t) { return cudaSuccess; }
 cudaError_t cudaGraphLaunch(cudaGraphExec_t, cudaStream_t) { return cudaErrorNotSupported; }
 cudaError_t cudaIpcGetMemHandle(cudaIpcMemHandle_t*, void*) { return cudaErrorNotSupported; }
 cudaError_t cudaIpcOpenMemHandle(void**, cudaIpcMemHandle_t, unsigned) { return cudaErrorNotSupported; }
@@ -288,5 +289,6 @@ int DecodeModel::enqueue_step(cudaStream_t, bool, bool) { return -1; }
 void DecodeModel::reset_cache(cudaStream_t) {}
 void DecodeModel::bind(const LayerRef*, const MatRef&, const float*, const MatRef&) {}
 int DecodeModel::project_partial(const MatRef&, const float*, int, cudaStream_t, bool) { return -1; }
+int DecodeModel::set_persistent(bool) { return -2; }
 
 }  // namespace gi
