@@ -76,7 +76,7 @@ GI_DEVINL bool grid_sync(unsigned* bar, unsigned target, int* error, int* flag) 
             break;
           }
           if (now_ns() - t0 > 2000000000ull) {
-            atomicExch(error, 1);
+            *(volatile int*)error = 1;
             ok = 0;
             break;
           }
