@@ -35,7 +35,10 @@ decode   (the metric's second half) greedy decode tokens/s of the Llama-
          512-token prompt, 64 steps) tensor-parallel over the N ranks, and at
          N=1 config 4 (Llama-2-7B shape, 128-token prompt, 64 steps) with a
          bounded CPU-oracle sample of the same decode step; prefill (config
-         3, 512 tokens x 4096 columns) at N=1.
+         3, 512 tokens x 4096 columns) at N=1.  --persistent adds, under
+         "persistent", the same generations with every layer of a step in
+         one persistent launch (gi_cuda_model_set_persistent), and whether
+         their ids equal the per-layer launches'.
 """
 from __future__ import annotations
 
@@ -243,6 +246,18 @@ def decode_section(args, world, rank, local, pg):
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
         return float(t.item())
 
+    def persistent_run(model, prompt, ids_ref):
+        """The same generation with every layer of a step in one persistent launch."""
+        model.set_persistent(True)
+        model.reset()
+        model.generate(prompt, 64)
+        model.reset()
+        ids_p, _l, ms_p = model.generate(prompt, 64)
+        ms_p = max_over_ranks(ms_p)
+        model.set_persistent(False)
+        return {"tok_s": round(63 / (ms_p / 1e3), 2), "ms_per_token": round(ms_p / 63, 4),
+                "ids_equal_per_layer": bool(np.array_equal(ids_p, ids_ref))}
+
     # config 5: Llama-3-70B shape, weights drawn on the device (seeded)
     cfg5 = synth.LLAMA3_70B
     if world > 1:
@@ -255,6 +270,7 @@ def decode_section(args, world, rank, local, pg):
     ids, _l, ms = model.generate(prompt5, 64)
     ms = max_over_ranks(ms)
     w_bytes = sum(b.nbytes for b in dm.bufs.values()) - dm.bufs["token_embd.weight"].nbytes
+    pers5 = persistent_run(model, prompt5, ids) if args.persistent else None
     model.close()
     dm.close()
     if world > 1:
@@ -266,6 +282,8 @@ def decode_section(args, world, rank, local, pg):
                       "ms_per_token": round(ms / 63, 4),
                       "weight_bytes_per_token_per_gpu": int(w_bytes),
                       "ids_head": [int(i) for i in ids[:8]]}
+    if pers5:
+        out["config5"]["persistent"] = pers5
     if world > 1:
         return out
     # config 4: Llama-2-7B shape
@@ -281,6 +299,8 @@ def decode_section(args, world, rank, local, pg):
                       "prompt": 128, "steps": 64, "tok_s": round(63 / (ms4 / 1e3), 2),
                       "ms_per_token": round(ms4 / 63, 4), "weight_bytes_per_token": int(w_bytes),
                       "effective_gbs": round(w_bytes / (ms4 / 63 / 1e3) / 1e9, 1)}
+    if args.persistent:
+        out["config4"]["persistent"] = persistent_run(model, prompt4, ids4)
     if not args.no_cpu_baseline:
         # the CPU restatement of Engine.Forward on the same bytes, a bounded sample
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -549,6 +569,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / prefill section")
+    ap.add_argument("--persistent", action="store_true",
+                    help="also time configs 4 and 5 with the persistent layers kernel (Model.set_persistent)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
