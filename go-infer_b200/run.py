@@ -46,6 +46,8 @@ def decode(args) -> None:
         dev = synth.DeviceModel.synth_on_device(cfg, seed=args.seed)
     model = dev.model()
     try:
+        if args.persistent:
+            model.set_persistent(True)
         prompt = np.random.default_rng(args.seed * 10).integers(0, cfg.vocab, args.prompt).astype(np.int32)
         ids, _logits, ms = model.generate(prompt, args.steps)
         per = ms / max(args.steps - 1, 1)
@@ -104,6 +106,7 @@ def main() -> None:
     d.add_argument("--steps", type=int, default=64)
     d.add_argument("--seed", type=int, default=4)
     d.add_argument("--gguf", default="", help="decode the model of this GGUF file instead")
+    d.add_argument("--persistent", action="store_true", help="every layer of a step in one persistent launch")
     x = sub.add_parser("export")
     x.add_argument("--model", choices=sorted(MODELS), default="llama2-7b")
     x.add_argument("--layers", type=int, default=0, help="override the layer count")
