@@ -38,7 +38,8 @@ decode   (the metric's second half) greedy decode tokens/s of the Llama-
          3, 512 tokens x 4096 columns) at N=1.  --persistent adds, under
          "persistent", the same generations with every layer of a step in
          one persistent launch (gi_cuda_model_set_persistent), and whether
-         their ids equal the per-layer launches'.
+         their ids equal the per-layer launches'.  --q6k-mma adds the Q6_K
+         lm_head shapes on the int8 tensor-core kernel (gemv_other, "_mma").
 """
 from __future__ import annotations
 
@@ -323,9 +324,14 @@ def decode_section(args, world, rank, local, pg):
     # plain decode GEMV, rotating weight copies past the L2, graph + PDL
     peak, _kind = measured_peak()
     other = {}
-    for name, qt, rows, cols in (("q8_0_config1_4096x4096", G.TYPE_Q8_0, 4096, 4096),
-                                 ("q6_k_lm_head_32000x4096", G.TYPE_Q6_K, 32000, 4096),
-                                 ("q6_k_lm_head_128256x8192", G.TYPE_Q6_K, 128256, 8192)):
+    shapes = [("q8_0_config1_4096x4096", G.TYPE_Q8_0, 4096, 4096, False),
+              ("q6_k_lm_head_32000x4096", G.TYPE_Q6_K, 32000, 4096, False),
+              ("q6_k_lm_head_128256x8192", G.TYPE_Q6_K, 128256, 8192, False)]
+    if args.q6k_mma:  # the same Q6_K shapes on the int8 tensor-core kernel
+        shapes += [(n + "_mma", qt, r, c, True) for n, qt, r, c, _m in shapes if qt == G.TYPE_Q6_K]
+    for name, qt, rows, cols, mma in shapes:
+        if args.q6k_mma:
+            G.set_q6k_mma(mma)
         wbytes = rows * G.row_bytes(qt, cols)
         ncopy = max(2, int(2 * 126e6 / wbytes) + 1)
         bufs = [G.synth_buffer(qt, 20 + c, 0.02, rows, cols) for c in range(ncopy)]
@@ -351,6 +357,8 @@ def decode_section(args, world, rank, local, pg):
         del graph
         for b in bufs:
             G.ReleaseBuffer(b)
+    if args.q6k_mma:
+        G.set_q6k_mma(False)
     out["gemv_other"] = other
     # config 3: prefill dequant-GEMM (512 tokens x 4096 columns)
     x = torch.randn(512, 4096, device=dev)
@@ -569,6 +577,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / prefill section")
+    ap.add_argument("--q6k-mma", action="store_true",
+                    help="also time the Q6_K lm_head shapes on the int8 tensor-core kernel (set_q6k_mma)")
     ap.add_argument("--persistent", action="store_true",
                     help="also time configs 4 and 5 with the persistent layers kernel (Model.set_persistent)")
     args = ap.parse_args()

@@ -57,6 +57,7 @@ struct Ctx {
   size_t pinned_cap = 0;
   bool batch = false;
   bool pdl = false;
+  bool q6k_mma = false;
   // Outputs of the open batch: still in device memory, copied back to their
   // host buffers when the batch ends; later calls of the batch read them there.
   gi::PendingOutputs pending;
@@ -253,6 +254,7 @@ gi::GemvLaunch launch_cfg(bool pdl) {
   gi::GemvLaunch L;
   L.sm_count = g.sm_count;
   L.pdl = pdl;
+  L.q6k_mma = g.q6k_mma;
   return L;
 }
 
@@ -1082,6 +1084,12 @@ int gi_cuda_gemv_multi_dev(int quant_type, int nmat, float* const* y, const floa
 int gi_cuda_set_pdl(int enable) {
   std::lock_guard<std::mutex> lk(g.mu);
   g.pdl = enable != 0;
+  return 0;
+}
+
+int gi_cuda_set_q6k_mma(int enable) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  g.q6k_mma = enable != 0;
   return 0;
 }
 

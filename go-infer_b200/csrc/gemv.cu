@@ -1110,6 +1110,354 @@ int prepare_ring() {
 }
 }  // namespace q6k
 
+// ------------------------ Q6_K on the int8 tensor cores ---------------------
+// Rows of whole 2048-column groups (rows then start on 16-byte boundaries:
+// 8 x 210 = 1680 = 105 x 16).  The Q4_K / Q8_0 structure: a unit is 16 rows
+// x 256 columns (one super-block per row), each CTA owns whole 16-row tiles,
+// units are dealt to the warps round-robin and streamed through per-warp
+// cp.async rings, every tile's per-warp partials are summed in fixed warp
+// order.  A super-block is only 2-byte aligned: a unit stages, per row, the
+// 14 aligned 16-byte chunks that cover it (224 bytes), so the block starts
+// at byte (2 b) mod 16 of its row slot (b = the column block); odd b leave
+// it 2 bytes off a word, and its words are read as two aligned words joined
+// by a funnel shift.
+//
+// Arithmetic (DequantizeQ6_K, pkg/quant/quant.go:256-291): element 128n +
+// 32j + l (n < 2, j < 4, l < 32) has q = 4 bits of ql[64n + 32(j&1) + l]
+// (low nibble for j < 2) | 2 bits of qh[32n + l] (shift 2j) << 4, weight
+// d * sc[8n + 2j + l/16] * (q - 32).  One m16n8k32 MMA (u8 x s8) per
+// chunk (n, j): A = the unsigned 6-bit q of 16 rows x 32 elements in their
+// natural order; B = the four balanced base-256 limbs of the 30-bit
+// fixed-point activation, columns 0-3 carrying the limbs of the chunk's
+// first sub-block (l < 16, zeros elsewhere), columns 4-7 those of the second
+// (l >= 16); the accumulator starts at -32 x the column's limb sum, so the
+// MMA yields the exact sum of (q - 32) * limb per (row, sub-block, limb).
+// Each lane holds two limb columns of one sub-block and scales them by that
+// sub-block's int8 scale in int32 (exact); a super-block leaves the integer
+// domain through 4 int->float conversions per lane, scaled by d and 2^-e.
+namespace q6m {
+constexpr int kRowSlot = 224;                 // 14 aligned 16-byte chunks cover a 210-byte block
+constexpr int kUnitBytes = 16 * kRowSlot;     // 3584
+constexpr int kUnitX = 1296;                  // [chunk][limb][32 B] 1024, limb sums 256, 2^-e 16
+constexpr int kSmemMax = 227 * 1024 - 256;
+constexpr int kCoresidentSmem = 110 * 1024;
+
+struct Params {
+  const uint8_t* w;
+  float* y;
+  const float* x;
+  long long rowb;
+  int rows, nku, ntiles, ctas;
+  int x_off, slot_off;
+};
+
+// Stage one unit (256 columns) of x at xu.  Chunk c = 4n + j holds the
+// elements 128n + 32j + l; lane L owns chunk L/4 and its elements 4t..4t+3
+// and 16+4t..16+4t+3 (t = L%4).  Layout: [c][limb][32 bytes, element order]
+// at c*128; at 1024 + 32c + 8t the int32 pair (-32 x limb sum) of the
+// chunk's columns 2t, 2t+1 (column k < 4: limb k over l < 16; k >= 4: limb
+// k-4 over l >= 16); the float 2^-e at 1280.
+GI_DEVINL void stage_unit(uint8_t* xu, const float* xunit, int lane) {
+  const int c = lane >> 2, t = lane & 3;
+  const int e0 = 128 * (c >> 2) + 32 * (c & 3);
+  const float4 a = *reinterpret_cast<const float4*>(xunit + e0 + 4 * t);
+  const float4 b = *reinterpret_cast<const float4*>(xunit + e0 + 16 + 4 * t);
+  float m = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
+                  fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+  m = warp_max(m);
+  int e = 0;
+  if (m > 0.f && m <= 3.0e38f) e = min(126, max(-126, 29 - ilogbf(m)));  // max |x| * 2^e < 2^30
+  const float s = exp2i(e);
+  uint32_t u[8];
+  u[0] = ((uint32_t)__float2int_rn(a.x * s) + 0x80808080u) ^ 0x80808080u;
+  u[1] = ((uint32_t)__float2int_rn(a.y * s) + 0x80808080u) ^ 0x80808080u;
+  u[2] = ((uint32_t)__float2int_rn(a.z * s) + 0x80808080u) ^ 0x80808080u;
+  u[3] = ((uint32_t)__float2int_rn(a.w * s) + 0x80808080u) ^ 0x80808080u;
+  u[4] = ((uint32_t)__float2int_rn(b.x * s) + 0x80808080u) ^ 0x80808080u;
+  u[5] = ((uint32_t)__float2int_rn(b.y * s) + 0x80808080u) ^ 0x80808080u;
+  u[6] = ((uint32_t)__float2int_rn(b.z * s) + 0x80808080u) ^ 0x80808080u;
+  u[7] = ((uint32_t)__float2int_rn(b.w * s) + 0x80808080u) ^ 0x80808080u;
+  const uint32_t base = smem_u32(xu) + c * 128 + 4 * t;
+  int sa[4], sb[4];  // this lane's limb sums over its 4 + 4 elements
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    const uint32_t k = 3u - (uint32_t)n;  // limb n is byte 3-n
+    const uint32_t lo = q4k::gather_byte(u[0], u[1], u[2], u[3], k);
+    const uint32_t hi = q4k::gather_byte(u[4], u[5], u[6], u[7], k);
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(base + n * 32), "r"(lo) : "memory");
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(base + n * 32 + 16), "r"(hi) : "memory");
+    sa[n] = (int)(int8_t)(lo) + (int)(int8_t)(lo >> 8) + (int)(int8_t)(lo >> 16) + (int)(int8_t)(lo >> 24);
+    sb[n] = (int)(int8_t)(hi) + (int)(int8_t)(hi >> 8) + (int)(int8_t)(hi >> 16) + (int)(int8_t)(hi >> 24);
+  }
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {  // sums over the chunk's four lanes (lanes 4c..4c+3)
+    sa[n] += __shfl_xor_sync(0xffffffffu, sa[n], 1);
+    sa[n] += __shfl_xor_sync(0xffffffffu, sa[n], 2);
+    sb[n] += __shfl_xor_sync(0xffffffffu, sb[n], 1);
+    sb[n] += __shfl_xor_sync(0xffffffffu, sb[n], 2);
+  }
+  // lane t writes columns 2t, 2t+1: t < 2 -> limbs 2t, 2t+1 of the first
+  // sub-block; t >= 2 -> limbs 2(t-2), 2(t-2)+1 of the second
+  const int c0 = t < 2 ? (t == 0 ? sa[0] : sa[2]) : (t == 2 ? sb[0] : sb[2]);
+  const int c1 = t < 2 ? (t == 0 ? sa[1] : sa[3]) : (t == 2 ? sb[1] : sb[3]);
+  sts64(smem_u32(xu) + 1024 + 32 * c + 8 * t, (uint64_t)(uint32_t)(-32 * c0) | ((uint64_t)(uint32_t)(-32 * c1) << 32));
+  if (lane == 0) reinterpret_cast<float*>(xu + 1280)[0] = exp2i(-e);
+}
+
+template <int W>
+__device__ void stage_x(uint8_t* xs, const Params& p) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int u = warp; u < p.nku; u += W) stage_unit(xs + u * kUnitX, p.x + 256 * u, lane);
+  __syncthreads();
+}
+
+// Word at a 2-byte-aligned shared address: one load, or (odd) two aligned
+// loads joined by a funnel shift.
+template <bool Odd>
+GI_DEVINL uint32_t ldw(uint32_t a) {
+  if (!Odd) return lds32(a);
+  return __funnelshift_r(lds32(a - 2), lds32(a + 2), 16);
+}
+
+// Signed byte k of w, sign-extended.
+GI_DEVINL int sbyte(uint32_t w, uint32_t k) { return (int)prmt(w, 0u, k | ((k | 8u) * 0x1110u)); }
+
+// One unit: rows g and g+8 of a 16-row tile.  blk: row g's block in the
+// stage (row g+8's is 8 slots on); xu: the unit's staged activations.
+template <bool Odd>
+GI_DEVINL void compute_unit(uint32_t blk, uint32_t xu, int g, int t, float W0, float W1, float& yA, float& yB) {
+  const uint32_t bA = blk, bB = blk + 8 * kRowSlot;
+  // scales of the two rows (16 signed bytes at 192)
+  uint32_t sA[4], sB[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    sA[i] = ldw<Odd>(bA + 192 + 4 * i);
+    sB[i] = ldw<Odd>(bB + 192 + 4 * i);
+  }
+  const uint32_t hsel = t >= 2 ? 1u : 0u;  // this lane's sub-block within a chunk
+  int iA0 = 0, iA1 = 0, iB0 = 0, iB1 = 0;
+  const uint32_t xb_off = (uint32_t)((g & 3) * 32 + (g < 4 ? 0 : 16) + 4 * t);
+#pragma unroll
+  for (int n = 0; n < 2; ++n) {
+    // ql words (j even: L0, j odd: L1) and the qh word at quads 4t and 16+4t
+    const uint32_t L0A = ldw<Odd>(bA + 64 * n + 4 * t), L0A2 = ldw<Odd>(bA + 64 * n + 16 + 4 * t);
+    const uint32_t L1A = ldw<Odd>(bA + 64 * n + 32 + 4 * t), L1A2 = ldw<Odd>(bA + 64 * n + 48 + 4 * t);
+    const uint32_t QA = ldw<Odd>(bA + 128 + 32 * n + 4 * t), QA2 = ldw<Odd>(bA + 128 + 32 * n + 16 + 4 * t);
+    const uint32_t L0B = ldw<Odd>(bB + 64 * n + 4 * t), L0B2 = ldw<Odd>(bB + 64 * n + 16 + 4 * t);
+    const uint32_t L1B = ldw<Odd>(bB + 64 * n + 32 + 4 * t), L1B2 = ldw<Odd>(bB + 64 * n + 48 + 4 * t);
+    const uint32_t QB = ldw<Odd>(bB + 128 + 32 * n + 4 * t), QB2 = ldw<Odd>(bB + 128 + 32 * n + 16 + 4 * t);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // q = 4 bits of ql | 2 bits of qh << 4 (quant.go:270-282)
+      auto q6 = [j](uint32_t L0, uint32_t L1, uint32_t Q) {
+        const uint32_t L = (j & 1) ? L1 : L0;
+        const uint32_t lo = (j >> 1) ? (L >> 4) & 0x0F0F0F0Fu : L & 0x0F0F0F0Fu;
+        return lo | (((Q >> (2 * j)) << 4) & 0x30303030u);
+      };
+      const uint32_t a0 = q6(L0A, L1A, QA), a1 = q6(L0B, L1B, QB);
+      const uint32_t a2 = q6(L0A2, L1A2, QA2), a3 = q6(L0B2, L1B2, QB2);
+      const int c = 4 * n + j;
+      const uint32_t xw = lds32(xu + c * 128 + xb_off);
+      const uint64_t cs = lds64(xu + 1024 + 32 * c + 8 * t);
+      int d[4] = {(int)(uint32_t)cs, (int)(uint32_t)(cs >> 32), (int)(uint32_t)cs, (int)(uint32_t)(cs >> 32)};
+      imma_16832(d, a0, a1, a2, a3, g < 4 ? xw : 0u, g < 4 ? 0u : xw);
+      // sub-block 8n + 2j + hsel: byte (2j + hsel) & 3 of scale word 2n + (2j + hsel) / 4
+      const uint32_t sbk = 2u * (uint32_t)j + hsel;
+      const int scA = sbyte(sA[2 * n + (sbk >> 2)], sbk & 3u), scB = sbyte(sB[2 * n + (sbk >> 2)], sbk & 3u);
+      iA0 += d[0] * scA;
+      iA1 += d[1] * scA;
+      iB0 += d[2] * scB;
+      iB1 += d[3] * scB;
+    }
+  }
+  const float inv = __uint_as_float(lds32(xu + 1280));
+  const float dA = __half2float(__ushort_as_half((unsigned short)lds16(bA + 208)));
+  const float dB = __half2float(__ushort_as_half((unsigned short)lds16(bB + 208)));
+  yA = fmaf(fmaf((float)iA0, W0, (float)iA1 * W1) * dA, inv, yA);
+  yB = fmaf(fmaf((float)iB0, W0, (float)iB1 * W1) * dB, inv, yB);
+}
+
+template <int W, int S>
+__global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gemv_q6m_kernel(const Params p) {
+  constexpr int kWarps = W, kThreads = W * 32;
+  extern __shared__ __align__(16) uint8_t smem[];
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int c = blockIdx.x;
+  const int T0 = (int)((long long)p.ntiles * c / p.ctas), T1 = (int)((long long)p.ntiles * (c + 1) / p.ctas);
+  const int ntl = T1 - T0, n = ntl * p.nku;
+  const uint32_t ring = smem_u32(smem) + warp * S * kUnitBytes;
+  uint8_t* xs = smem + p.x_off;
+  const uint32_t xs_s = smem_u32(xs);
+  float* slots = reinterpret_cast<float*>(smem + p.slot_off);  // [ntl][kWarps][16]
+  const uint64_t pol = l2_evict_first_policy();
+  for (int i = threadIdx.x; i < ntl * kWarps * 16; i += kThreads) slots[i] = 0.f;
+
+  // Request cursor: lane L copies row L/2 of the unit, chunks L%2, L%2 + 2,
+  // ..., L%2 + 12 of the 14 that cover the row's block.
+  const int crow = lane >> 1, cpar = lane & 1;
+  int ltile = warp / p.nku, lku = warp - ltile * p.nku;
+  int next = warp;
+  const uint8_t* src = nullptr;
+  auto seek = [&]() {
+    src = p.w + (long long)min((T0 + ltile) * 16 + crow, p.rows - 1) * p.rowb + ((210 * lku) & ~15);
+  };
+  if (next < n) seek();
+  const uint32_t dst = ring + crow * kRowSlot + 16 * cpar;
+  auto request = [&](int stage) {  // always commits one group (possibly empty)
+    if (next < n) {
+      const uint32_t o = (uint32_t)stage * kUnitBytes;
+#pragma unroll
+      for (int i = 0; i < 7; ++i) cp_async16_hint(dst + o + 32 * i, src + 16 * cpar + 32 * i, pol);
+      next += kWarps;
+      lku += kWarps;
+      if (lku < p.nku) {
+        src += (210 * lku & ~15) - (210 * (lku - kWarps) & ~15);
+      } else {
+        do {
+          lku -= p.nku;
+          ++ltile;
+        } while (lku >= p.nku);
+        if (next < n) seek();
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int s = 0; s < S; ++s) request(s);
+  griddep_wait();
+  stage_x<W>(xs, p);  // ends with a CTA barrier (also orders the slot zeroing)
+
+  // limb weights of this lane's two columns: limbs 2(t&1), 2(t&1)+1
+  const float W0 = (t & 1) ? 256.f : 16777216.f, W1 = (t & 1) ? 1.f : 65536.f;
+  int ctile = warp / p.nku, cku = warp - ctile * p.nku;
+  uint32_t cx = xs_s + cku * kUnitX;
+  float yA = 0.f, yB = 0.f;
+  int stage = 0;
+  for (int i = warp; i < n; i += kWarps) {
+    cp_async_wait<S - 1>();
+    __syncwarp();
+    const uint32_t blk = ring + stage * kUnitBytes + g * kRowSlot + ((2 * cku) & 15);
+    if (cku & 1)
+      compute_unit<true>(blk, cx, g, t, W0, W1, yA, yB);
+    else
+      compute_unit<false>(blk, cx, g, t, W0, W1, yA, yB);
+    __syncwarp();
+    request(stage);
+    stage = stage + 1 == S ? 0 : stage + 1;
+    const int tile = ctile;
+    cku += kWarps;
+    if (cku < p.nku) {
+      cx += kWarps * kUnitX;
+    } else {
+      do {
+        cku -= p.nku;
+        ++ctile;
+      } while (cku >= p.nku);
+      cx = xs_s + cku * kUnitX;
+    }
+    if (ctile != tile || i + kWarps >= n) {  // this warp is done with `tile`
+      float vA = yA + __shfl_xor_sync(0xffffffffu, yA, 1);
+      float vB = yB + __shfl_xor_sync(0xffffffffu, yB, 1);
+      vA += __shfl_xor_sync(0xffffffffu, vA, 2);
+      vB += __shfl_xor_sync(0xffffffffu, vB, 2);
+      yA = 0.f;
+      yB = 0.f;
+      if (t == 0) {
+        float* sl = slots + (tile * kWarps + warp) * 16;
+        sl[g] = vA;
+        sl[g + 8] = vB;
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  for (int tl = warp; tl < ntl; tl += kWarps) {
+    if (lane < 16) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) sum += slots[(tl * kWarps + w) * 16 + lane];
+      const int row = (T0 + tl) * 16 + lane;
+      if (row < p.rows) p.y[row] = sum;
+    }
+  }
+}
+
+struct Layout {
+  int warps, ctas, stages, x_off, slot_off, smem;
+};
+
+Layout layout(int64_t rows, int64_t cols, const GemvLaunch& L) {
+  Layout o;
+  const int nku = (int)(cols / 256), ntiles = (int)((rows + 15) / 16);
+  o.ctas = ntiles < L.sm_count ? ntiles : L.sm_count;
+  const int max_tiles = (ntiles + o.ctas - 1) / o.ctas;
+  bool large = o.ctas < L.sm_count || (long long)ntiles * nku >= 64LL * o.ctas;
+  const int xbytes = nku * kUnitX;
+  if (large && xbytes + max_tiles * 16 * 64 + 16 * 2 * kUnitBytes > kSmemMax) large = false;
+  o.warps = large ? 16 : 8;
+  const int fixed = xbytes + max_tiles * o.warps * 64;
+  o.stages = 3;
+  while (o.stages > 2 && fixed + o.warps * o.stages * kUnitBytes > kCoresidentSmem) --o.stages;
+  o.x_off = o.warps * o.stages * kUnitBytes;
+  o.slot_off = o.x_off + xbytes;
+  o.smem = o.slot_off + max_tiles * o.warps * 64;
+  return o;
+}
+
+int launch(float* y, const float* x, const uint8_t* w, int64_t rows, int64_t cols, const GemvLaunch& L,
+           cudaStream_t stream) {
+  if (cols % 2048 != 0 || (reinterpret_cast<uintptr_t>(w) & 15) != 0) return -4;
+  const Layout o = layout(rows, cols, L);
+  if (o.smem > kSmemMax) return -4;
+  Params p;
+  p.w = w;
+  p.y = y;
+  p.x = x;
+  p.rowb = (cols / 256) * 210;
+  p.rows = (int)rows;
+  p.nku = (int)(cols / 256);
+  p.ntiles = (int)((rows + 15) / 16);
+  p.ctas = o.ctas;
+  p.x_off = o.x_off;
+  p.slot_off = o.slot_off;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(o.ctas);
+  cfg.blockDim = dim3(o.warps * 32);
+  cfg.dynamicSmemBytes = o.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = L.pdl ? 1 : 0;
+  cudaError_t e;
+  switch ((o.warps == 16 ? 10 : 0) + o.stages) {
+    case 2: e = cudaLaunchKernelEx(&cfg, gemv_q6m_kernel<8, 2>, p); break;
+    case 3: e = cudaLaunchKernelEx(&cfg, gemv_q6m_kernel<8, 3>, p); break;
+    case 12: e = cudaLaunchKernelEx(&cfg, gemv_q6m_kernel<16, 2>, p); break;
+    case 13: e = cudaLaunchKernelEx(&cfg, gemv_q6m_kernel<16, 3>, p); break;
+    default: return -4;
+  }
+  return e == cudaSuccess ? 0 : -5;
+}
+
+template <int W, int S>
+cudaError_t prepare_one() {
+  cudaError_t e = cudaFuncSetAttribute(gemv_q6m_kernel<W, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  return e == cudaSuccess ? set_max_shared_carveout(gemv_q6m_kernel<W, S>) : e;
+}
+
+int prepare() {
+  cudaError_t e = prepare_one<8, 2>();
+  if (e == cudaSuccess) e = prepare_one<8, 3>();
+  if (e == cudaSuccess) e = prepare_one<16, 2>();
+  if (e == cudaSuccess) e = prepare_one<16, 3>();
+  return e == cudaSuccess ? 0 : -5;
+}
+}  // namespace q6m
+
 int gemv_prepare_device() {
   if (q4k::prepare() != 0) return -5;
   if (set_max_shared_carveout(q80::gemv_q80_kernel) != cudaSuccess) return -5;
@@ -1199,6 +1547,17 @@ int gemv_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
       return launch_rowwarp(q80::gemv_q80_kernel, rows, L, stream, y, x, wb, wb + w_bytes,
                             (long long)rb, (int)rows, (int)(cols / 32));
     case kTypeQ6_K:
+      if (L.q6k_mma && cols % 2048 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
+        static int prepared_device = -1;  // kernel attributes, set on first use per device
+        int dev = -1;
+        if (cudaGetDevice(&dev) != cudaSuccess) return -5;
+        if (dev != prepared_device) {
+          if (q6m::prepare() != 0) return -5;
+          prepared_device = dev;
+        }
+        const int r = q6m::launch(y, x, wb, rows, cols, L, stream);
+        if (r != -4) return r;  // -4: the activation staging does not fit; the ring kernel takes it
+      }
       if (cols % 2048 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) return q6k::launch_ring(y, x, wb, rows, cols, L, stream);
       return launch_rowwarp(q6k::gemv_q6k_kernel, rows, L, stream, y, x, wb, wb + w_bytes,
                             (long long)rb, (int)rows, (int)(cols / 256));

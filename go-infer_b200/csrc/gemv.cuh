@@ -37,6 +37,8 @@ struct GemvLaunch {
   int sm_count = 148;
   bool pdl = false;  // programmatic dependent launch (weights must not be
                      // written by the preceding kernel)
+  bool q6k_mma = false;  // Q6_K rows of whole 2048-column groups on the int8
+                         // tensor cores (gemv.cu, namespace q6m)
 };
 
 // Per-device one-time set-up (kernel attributes); call with the device current.

@@ -48,7 +48,7 @@ EXPORTS = (
     "gi_cuda_gemm_buf", "gi_cuda_gemm_fused_gate_up_buf", "gi_cuda_add_residual", "gi_cuda_swiglu",
     "gi_cuda_gemv_q8_0", "gi_cuda_gemv_q4_k", "gi_cuda_gemv_q6_k",
     "gi_cuda_gemm_q8_0", "gi_cuda_gemm_q4_k", "gi_cuda_gemm_q6_k", "gi_cuda_gemv_dev",
-    "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl",
+    "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl", "gi_cuda_set_q6k_mma",
     "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize", "gi_quantize_seeded",
     "gi_cuda_alloc_buffers", "gi_cuda_forward_transformer", "gi_cuda_model_create", "gi_cuda_model_destroy",
     "gi_cuda_model_reset", "gi_cuda_model_set_persistent", "gi_cuda_model_generate", "gi_cuda_tp_prepare", "gi_cuda_tp_connect", "gi_cuda_tp_close",
@@ -128,6 +128,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "gi_cuda_buffer_device_ptr": ([vp], vp),
         "gi_cuda_buffer_bytes": ([vp], sz),
         "gi_cuda_set_pdl": ([i32], i32),
+        "gi_cuda_set_q6k_mma": ([i32], i32),
         "gi_cuda_last_error": ([], ctypes.c_char_p),
         "gi_quant_row_bytes": ([i32, ctypes.c_int64], ctypes.c_int64),
         "gi_quantize": ([i32, f32p, ctypes.c_int64, ctypes.c_int64, vp, i32], i32),
@@ -348,6 +349,11 @@ def gemv_multi_dev(quant_type: int, ys: list[int], x_ptr: int, ws: list[int], w_
 
 def set_pdl(enable: bool) -> None:
     load_library().gi_cuda_set_pdl(1 if enable else 0)
+
+
+def set_q6k_mma(enable: bool) -> None:
+    """Q6_K GEMVs (rows of whole 2048-column groups) on the int8 tensor cores."""
+    load_library().gi_cuda_set_q6k_mma(1 if enable else 0)
 
 
 def row_bytes(quant_type: int, cols: int) -> int:

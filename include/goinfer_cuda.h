@@ -283,6 +283,12 @@ size_t gi_cuda_buffer_bytes(gi_cuda_buffer_t buf);
  * the kernel just before. */
 int gi_cuda_set_pdl(int enable);
 
+/* Q6_K GEMVs of rows of whole 2048-column groups on the int8 tensor cores
+ * (1) or on the CUDA cores (0, default) -- no reference counterpart: a
+ * choice between two kernels of this library.  Same results within the
+ * GEMV tolerance; the tensor-core kernel has not been measured yet. */
+int gi_cuda_set_q6k_mma(int enable);
+
 /* Text of the last failure on the calling thread ("" if none). */
 const char* gi_cuda_last_error(void);
 

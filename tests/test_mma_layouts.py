@@ -193,3 +193,135 @@ def test_q4k_stage_swizzle_and_ldmatrix_fragments():
             xhi = L[:, 64 * c + 32:64 * c + 64]
             assert np.array_equal(Dl[:, 0:4], lo @ xlo.T)
             assert np.array_equal((Df - Dl)[:, 4:8], 16 * ((A >> 4) @ xhi.T))
+
+
+# ---- Q6_K on the int8 tensor cores (gemv.cu, namespace q6m) ----------------
+
+def q6m_ldw(slot, a):
+    """ldw<Odd>: the word at byte a of a row slot (a even); a % 4 == 2 reads
+    the aligned words at a - 2 and a + 2 and joins them (funnel shift 16)."""
+    def word(o):
+        assert o % 4 == 0 and 0 <= o and o + 4 <= slot.size
+        return int.from_bytes(bytes(slot[o:o + 4].astype(np.uint8)), "little")
+    if a % 4 == 0:
+        return word(a)
+    assert a % 4 == 2
+    return ((word(a - 2) >> 16) | (word(a + 2) << 16)) & 0xFFFFFFFF
+
+
+def q6m_stage_x(L):
+    """stage_unit: [chunk][limb][32 bytes, element order] and, per chunk and
+    lane t, the pair (-32 x limb sum) of columns 2t, 2t+1."""
+    xs = np.zeros((8, 4, 32), np.int64)
+    cs = np.zeros((8, 4, 2), np.int64)
+    for c in range(8):
+        e0 = 128 * (c >> 2) + 32 * (c & 3)
+        xs[c] = L[:, e0:e0 + 32]
+        sa = L[:, e0:e0 + 16].sum(axis=1)
+        sb = L[:, e0 + 16:e0 + 32].sum(axis=1)
+        for t in range(4):
+            src = sa if t < 2 else sb
+            n0 = 2 * (t & 1)
+            cs[c, t] = (-32 * src[n0], -32 * src[n0 + 1])
+    return xs, cs
+
+
+def test_q6k_mma_fragments_give_exact_sub_block_dots():
+    """The Q6_K tensor-core kernel's unit as its cp.async requests stage it
+    (the 14 aligned chunks that cover each row's block, the block at byte
+    (2b) % 16 of a 224-byte slot), its A fragments built from (funnel-shifted)
+    ql / qh words, B from the staged limbs, the accumulator started at -32 x
+    the limb sums and the per-lane int8 scales: the lanes' integer sums give
+    sum_sub-blocks sc * sum (q - 32) * X exactly, with q as the oracle's
+    DequantizeQ6_K decodes it (quant.go:256-291), for both block parities."""
+    import oracle as O
+    rng = np.random.default_rng(6)
+    x = rng.normal(0, 1, 256).astype(np.float32)
+    e = exponent(x)
+    L = limbs_of(x, e)
+    X = sum(L[n] * 256 ** (3 - n) for n in range(4))
+    xs, cs = q6m_stage_x(L)
+    for b in range(16):  # column block: the parity and the offset in the slot
+        s = (2 * b) % 16
+        blocks = rng.integers(0, 256, (16, 210), dtype=np.int64)
+        blocks[:, 208:210] = (0x00, 0x3C)  # d = 1.0: the oracle then gives sc * (q - 32)
+        slots = rng.integers(0, 256, (16, 224), dtype=np.int64)  # bytes around the block: garbage
+        slots[:, s:s + 210] = blocks
+        # the oracle's decode of each row: integer sc * (q - 32)
+        want_w = np.stack([O.dequantize(O.GGML_Q6_K, blocks[r].astype(np.uint8), 256) for r in range(16)])
+        assert np.array_equal(want_w, np.rint(want_w))
+        want = want_w.astype(np.int64) @ X
+        got = np.zeros(16, np.int64)
+        # per lane: its words, fragments and accumulators
+        lanes = {}
+        for lane in range(32):
+            g, t = lane >> 2, lane & 3
+            rows = (g, g + 8)
+            w = {}
+            for r in rows:
+                sl = slots[r]
+                for n in range(2):
+                    for name, off in (("L0", 64 * n), ("L1", 64 * n + 32), ("Q", 128 + 32 * n)):
+                        w[r, n, name, 0] = q6m_ldw(sl, s + off + 4 * t)
+                        w[r, n, name, 1] = q6m_ldw(sl, s + off + 16 + 4 * t)
+                w[r, "sc"] = [q6m_ldw(sl, s + 192 + 4 * i) for i in range(4)]
+            lanes[lane] = w
+        acc = {lane: [0, 0, 0, 0] for lane in range(32)}
+        for n in range(2):
+            for j in range(4):
+                c = 4 * n + j
+                A = np.zeros((16, 32), np.int64)
+                B = np.zeros((32, 8), np.int64)
+                for lane in range(32):
+                    g, t = lane >> 2, lane & 3
+                    w = lanes[lane]
+                    for reg, (r, half) in enumerate(((g, 0), (g + 8, 0), (g, 1), (g + 8, 1))):
+                        Lw = w[r, n, "L1" if j & 1 else "L0", half]
+                        Qw = w[r, n, "Q", half]
+                        lo = (Lw >> 4) & 0x0F0F0F0F if j >> 1 else Lw & 0x0F0F0F0F
+                        a = lo | (((Qw >> (2 * j)) << 4) & 0x30303030)
+                        k0 = 4 * t + 16 * half
+                        A[r, k0:k0 + 4] = [(a >> (8 * i)) & 0xFF for i in range(4)]
+                    xw = xs[c, g & 3, (0 if g < 4 else 16) + 4 * t:(0 if g < 4 else 16) + 4 * t + 4]
+                    if g < 4:
+                        B[4 * t:4 * t + 4, g] = xw      # b0
+                    else:
+                        B[16 + 4 * t:20 + 4 * t, g] = xw  # b1
+                assert A.max() < 64 and A.min() >= 0
+                C = np.zeros((16, 8), np.int64)
+                for lane in range(32):
+                    g, t = lane >> 2, lane & 3
+                    C[g, 2 * t:2 * t + 2] = cs[c, t]
+                    C[g + 8, 2 * t:2 * t + 2] = cs[c, t]
+                D = A @ B + C
+                assert np.abs(D).max() < 2 ** 31
+                for lane in range(32):
+                    g, t = lane >> 2, lane & 3
+                    sbk = 2 * j + (1 if t >= 2 else 0)
+                    for idx, r in ((0, g), (2, g + 8)):
+                        word = lanes[lane][r, "sc"][2 * n + (sbk >> 2)]
+                        byte = (word >> (8 * (sbk & 3))) & 0xFF
+                        sc = byte - 256 if byte >= 128 else byte
+                        acc[lane][idx] += int(D[r, 2 * t]) * sc
+                        acc[lane][idx + 1] += int(D[r, 2 * t + 1]) * sc
+        for lane in range(32):
+            g, t = lane >> 2, lane & 3
+            W0, W1 = (256, 1) if t & 1 else (2 ** 24, 2 ** 16)
+            assert max(abs(v) for v in acc[lane]) < 2 ** 31
+            got[g] += acc[lane][0] * W0 + acc[lane][1] * W1
+            got[g + 8] += acc[lane][2] * W0 + acc[lane][3] * W1
+        assert np.array_equal(got, want), b
+
+
+def test_q6k_mma_request_covers_each_block():
+    """The cursor's source offsets: row start + ((210 b) & ~15) + 16 i for the
+    14 chunks covers block b and ends inside the row when the row holds whole
+    2048-column groups (the last block ends exactly at the row's end)."""
+    for nsb in (8, 16, 32, 112):
+        rowb = 210 * nsb
+        assert rowb % 16 == 0
+        for b in range(nsb):
+            start = (210 * b) & ~15
+            assert start <= 210 * b and start + 224 >= 210 * b + 210
+            assert start + 224 <= rowb
+            assert (210 * b) - start == (2 * b) % 16
