@@ -32,6 +32,7 @@ def main():
     ap.add_argument("--gen", type=int, default=16)
     ap.add_argument("--out", required=True)
     ap.add_argument("--device-synth", action="store_true", help="draw the weights on the GPU")
+    ap.add_argument("--persistent", action="store_true", help="every layer of a step in one persistent launch")
     a = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -41,6 +42,8 @@ def main():
     cfg = CONFIGS[a.config]
     tp.connect(rank, world, cfg.dim)
     dev, model = tp.build(cfg, a.seed, rank, world, device_synth=a.device_synth)
+    if a.persistent:
+        model.set_persistent(True)
     prompt = np.random.default_rng(a.seed + 1).integers(0, cfg.vocab, a.prompt)
     ids, ms = tp.greedy(model, prompt, a.gen)
     all_ids = [None] * world
