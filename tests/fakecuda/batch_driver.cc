@@ -240,6 +240,8 @@ int main() {
     CHECK(gi_cuda_add_residual(a.data(), a.data(), 0) == -4);
     CHECK(gi_cuda_swiglu(nullptr, a.data(), 8) == -4);
     CHECK(gi_cuda_add_residual(a.data(), a.data(), 8) == 0 && a[0] == 2.f && a[7] == 2.f);
+    CHECK(gi_cuda_model_set_persistent(nullptr, 1) == -4);
+    CHECK(gi_cuda_set_q6k_mma(1) == 0 && gi_cuda_set_q6k_mma(0) == 0);
   }
 
   // ---- H: the no-alloc prefill against gi_cuda_gemm_dev, device pointers ----
