@@ -89,3 +89,49 @@ def test_cursor_matches_direct_addressing(rows, nku, W, ctas):
 def test_cursor_swiglu_interleave():
     assert replay([96, 96], 4, 8, 3, swiglu=True) > 0
     assert replay([100, 100], 16, 16, 5, swiglu=True) > 0
+
+
+def q6m_replay(rows, nku, W, ctas):
+    """The Q6_K tensor-core kernel's request cursor (gemv.cu, q6m): lane L
+    copies row L/2 of a unit from src = row start + ((210 lku) & ~15); within
+    a tile src moves by the difference of those rounded offsets, and a new
+    tile re-seeks (clamping rows past the end).  Every unit's source must be
+    the direct one, 16-byte aligned, and its 224 bytes must end inside the
+    matrix."""
+    ntiles = (rows + 15) // 16
+    rowb = 210 * nku
+    checked = 0
+    for c in range(ctas):
+        T0, T1 = ntiles * c // ctas, ntiles * (c + 1) // ctas
+        n = (T1 - T0) * nku
+        for warp in range(W):
+            for crow in range(16):
+                ltile, lku, nxt = warp // nku, warp % nku, warp
+                src = None
+
+                def seek():
+                    return min((T0 + ltile) * 16 + crow, rows - 1) * rowb + ((210 * lku) & ~15)
+                if nxt < n:
+                    src = seek()
+                while nxt < n:
+                    want = min((T0 + ltile) * 16 + crow, rows - 1) * rowb + ((210 * lku) & ~15)
+                    assert src == want
+                    assert src % 16 == 0 and src + 224 <= rows * rowb
+                    checked += 1
+                    nxt += W
+                    lku += W
+                    if lku < nku:
+                        src += ((210 * lku) & ~15) - ((210 * (lku - W)) & ~15)
+                    else:
+                        while lku >= nku:
+                            lku -= nku
+                            ltile += 1
+                        if nxt < n:
+                            src = seek()
+    return checked
+
+
+@pytest.mark.parametrize("rows,nku,W,ctas", [(16, 8, 16, 1), (17, 8, 16, 2), (300, 16, 16, 19), (2000, 32, 16, 125),
+                                             (4100, 8, 8, 148), (40, 16, 8, 3)])
+def test_q6m_request_cursor(rows, nku, W, ctas):
+    assert q6m_replay(rows, nku, W, ctas) > 0
