@@ -40,6 +40,9 @@ decode   (the metric's second half) greedy decode tokens/s of the Llama-
          one persistent launch (gi_cuda_model_set_persistent), and whether
          their ids equal the per-layer launches'.  --q6k-mma adds the Q6_K
          lm_head shapes on the int8 tensor-core kernel (gemv_other, "_mma").
+--e2e-batch  runs the e2e step's three calls inside gi_cuda_begin_batch /
+         gi_cuda_end_batch (go-infer's metal.BeginBatch/EndBatch: one wait
+         per step), after checking that it reproduces the call-by-call step.
 """
 from __future__ import annotations
 
@@ -508,10 +511,25 @@ def run_ours(args):
     hx_g, hx_d = px_g.numpy(), px_d.numpy()
     hy_g, hy_u, hy_d = py_g.numpy(), py_u.numpy(), py_d.numpy()
 
-    def e2e_step():
+    def e2e_calls():
         G.MatMulBuf(G.TYPE_Q4_K, hy_g, hx_g, bufs["gate"], *GATE)
         G.MatMulBuf(G.TYPE_Q4_K, hy_u, hx_g, bufs["up"], *GATE)
         G.MatMulBuf(G.TYPE_Q4_K, hy_d, hx_d, bufs["down"], *DOWN)
+
+    def e2e_batched():  # metal.BeginBatch / EndBatch around the step: one wait per step
+        G.BeginBatch()
+        e2e_calls()
+        G.EndBatch()
+
+    e2e_step = e2e_batched if args.e2e_batch else e2e_calls
+    if args.e2e_batch:  # the batched step must give the call-by-call outputs, bit for bit
+        e2e_calls()
+        want = [a.copy() for a in (hy_g, hy_u, hy_d)]
+        for a in (hy_g, hy_u, hy_d):
+            a.fill(np.nan)
+        e2e_batched()
+        if not all(np.array_equal(a.view(np.uint32), b.view(np.uint32)) for a, b in zip((hy_g, hy_u, hy_d), want)):
+            raise RuntimeError("batched e2e step differs from the call-by-call step")
 
     for _ in range(max(3, args.warmup)):
         e2e_step()
@@ -554,7 +572,9 @@ def run_ours(args):
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": 4 * (GATE[1] + DOWN[1]),
                     "d2h_bytes_per_step": 4 * (2 * GATE[0] + DOWN[0]),
-                    "api": "gi_cuda_gemv_buf (host y/x, pinned: x copied in, y stored by the kernel)", "steps": e2e_steps},
+                    "api": ("gi_cuda_gemv_buf x3 inside gi_cuda_begin_batch/end_batch (host y/x, pinned)" if args.e2e_batch
+                            else "gi_cuda_gemv_buf (host y/x, pinned: x copied in, y stored by the kernel)"),
+                    "steps": e2e_steps},
             "gpu_launches": 2 * args.steps,
             "step_distribution": dist,
             "cpu_baseline": cpu,
@@ -577,6 +597,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / prefill section")
+    ap.add_argument("--e2e-batch", action="store_true",
+                    help="e2e step inside BeginBatch/EndBatch (one wait per step), checked against call-by-call")
     ap.add_argument("--q6k-mma", action="store_true",
                     help="also time the Q6_K lm_head shapes on the int8 tensor-core kernel (set_q6k_mma)")
     ap.add_argument("--persistent", action="store_true",
