@@ -1548,12 +1548,12 @@ int gemv_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
                             (long long)rb, (int)rows, (int)(cols / 32));
     case kTypeQ6_K:
       if (L.q6k_mma && cols % 2048 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
-        static int prepared_device = -1;  // kernel attributes, set on first use per device
+        static bool prepared[64] = {};  // kernel attributes, set on first use per device
         int dev = -1;
-        if (cudaGetDevice(&dev) != cudaSuccess) return -5;
-        if (dev != prepared_device) {
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -5;
+        if (!prepared[dev]) {
           if (q6m::prepare() != 0) return -5;
-          prepared_device = dev;
+          prepared[dev] = true;
         }
         const int r = q6m::launch(y, x, wb, rows, cols, L, stream);
         if (r != -4) return r;  // -4: the activation staging does not fit; the ring kernel takes it
