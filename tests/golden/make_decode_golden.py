@@ -23,11 +23,24 @@ import oracle as O  # noqa: E402
 import synth  # noqa: E402
 
 
+def draw_order(cfg) -> list:
+    """The model's tensor names in the order synth_model draws them (token
+    table, each layer's seven matrices and two norms, output norm, head)."""
+    names = ["token_embd.weight"]
+    for l in range(cfg.n_layers):
+        names += [synth.layer_tensor(l, role) for role in synth.LAYER_MATS]
+        names += [f"blk.{l}.attn_norm.weight", f"blk.{l}.ffn_norm.weight"]
+    return names + ["output_norm.weight", "output.weight"]
+
+
 def model_digest(host) -> str:
+    """SHA-256 over every 4099th byte of each tensor, tensors in draw order.
+    Names are not hashed, so renaming tensors keeps the digest; changed
+    weight bytes, types or shapes change it."""
     h = hashlib.sha256()
-    for name in sorted(host.tensors):
-        _qt, arr = host.tensors[name]
-        h.update(name.encode())
+    for name in draw_order(host.cfg):
+        qt, arr = host.tensors[name]
+        h.update(np.int64(qt).tobytes())
         h.update(np.ascontiguousarray(arr).view(np.uint8)[:: 4099].tobytes())
     return h.hexdigest()
 
