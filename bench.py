@@ -162,18 +162,27 @@ def profiled_traffic():
     return None
 
 
-def cpu_port_gemv_gbs(budget_s, row_frac=1.0):
-    """go-infer's CPU path (oracle restatement), all host threads."""
+def cpu_matrices(row_frac=1.0):
+    """The step's three Q4_K matrices (their first row_frac of the rows) for
+    the CPU legs, quantised by oracle/quantize_np.py, the byte-identical
+    numpy restatement of the library's Q4_K quantiser: no CPU leg loads the
+    product library."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import goinfer_cuda as G
-    import oracle as O
-    O.build() if not os.path.exists(O.LIB_PATH) else None
-    threads = os.cpu_count() or 1
+    import quantize_np
     mats = []
     for seed, (rows, cols) in ((3, GATE), (4, GATE), (5, DOWN)):
         r = max(16, int(rows * row_frac))
-        raw = G.quantize(G.TYPE_Q4_K, seeded(seed, (r, cols), 0.02))
-        mats.append((raw, r, cols))
+        mats.append((quantize_np.quantize_q4_k(seeded(seed, (rows, cols), 0.02)[:r]), r, cols))
+    return mats
+
+
+def cpu_port_gemv_gbs(budget_s, row_frac=1.0):
+    """go-infer's CPU path (oracle restatement), all host threads."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.build() if not os.path.exists(O.LIB_PATH) else None
+    threads = os.cpu_count() or 1
+    mats = cpu_matrices(row_frac)
     xg, xd = seeded(101, GATE[1], 1.0), seeded(102, DOWN[1], 1.0)
     done_bytes, t0, steps = 0, time.perf_counter(), 0
     while True:
@@ -189,6 +198,14 @@ def cpu_port_gemv_gbs(budget_s, row_frac=1.0):
     return done_bytes / el / 1e9, threads, sample
 
 
+def step_config(world):
+    """The line's config, the same in both arms."""
+    return {"workload": WORKLOAD, "parallelism": f"replicas x{world}" if world > 1 else "single",
+            "l2": (f"inputs larger than L2: GPU arm {NCOPIES} rotating weight copies "
+                   f"({NCOPIES * STEP_BYTES / 1e6:.0f} MB > 126 MB L2); CPU arm {STEP_BYTES / 1e6:.0f} MB per step"),
+            "graph": "GPU arm: K steps in one CUDA graph, programmatic dependent launch; CPU arm: one call per matrix"}
+
+
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
@@ -197,15 +214,10 @@ def run_reference(args):
     probe, _, _ = cpu_port_gemv_gbs(0.0, 1.0)
     t_step = STEP_BYTES / (probe * 1e9)
     frac = min(1.0, 120.0 / max(1e-9, t_step * (args.steps + args.warmup)))
-    cpu_port_gemv_gbs(0.0, frac)  # warm-up sample
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import goinfer_cuda as G
     import oracle as O
     threads = os.cpu_count() or 1
-    mats = []
-    for seed, (rows, cols) in ((3, GATE), (4, GATE), (5, DOWN)):
-        r = max(16, int(rows * frac))
-        mats.append((G.quantize(G.TYPE_Q4_K, seeded(seed, (r, cols), 0.02)), r, cols))
+    mats = cpu_matrices(frac)
     xg, xd = seeded(101, GATE[1], 1.0), seeded(102, DOWN[1], 1.0)
     for _ in range(args.warmup):
         for (raw, r, cols), x in zip(mats, (xg, xg, xd)):
@@ -225,9 +237,10 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
-        "config": {"workload": WORKLOAD, "rows_sampled": frac},
+        "config": step_config(world),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": sample, "nproc": os.cpu_count(), "cpu_model": cpu_model()},
+                         "sample": sample, "rows_sampled": round(frac, 4), "nproc": os.cpu_count(),
+                         "cpu_model": cpu_model()},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -478,6 +491,7 @@ def run_ours(args):
     g_timed = capture(args.steps)
     for _ in range(2):
         g_warm.replay()
+    g_timed.replay()  # uploads the timed graph: its first replay is not timed
     torch.cuda.synchronize()
 
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -561,9 +575,7 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic (seeded N(0,0.02) weights -> Q4_K, N(0,1) activations)",
-            "config": {"workload": WORKLOAD, "parallelism": f"replicas x{world}" if world > 1 else "single",
-                       "l2": f"{NCOPIES} rotating weight copies ({NCOPIES * STEP_BYTES / 1e6:.0f} MB > 126 MB L2)",
-                       "graph": "K steps in one CUDA graph, programmatic dependent launch"},
+            "config": step_config(world),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": profiled_traffic(),
                          "peak_source": peak_kind, "kernel": "gemv_q4k_kernel",

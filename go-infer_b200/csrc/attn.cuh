@@ -30,10 +30,14 @@ inline size_t attn_smem_bytes(int kv_mul, int hd) {
 // exp of kernels.go:60.
 // One (kv head g, chunk c) item, by every thread of the calling CTA; sm:
 // attn_smem_bytes(kv_mul, hd) of shared memory.
-GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* __restrict__ q,
-                                 const float* __restrict__ k, const float* __restrict__ v,
+//
+// q, k, v and (in attn_combine_one) part may have been written earlier in the
+// same launch by other CTAs (the persistent decode-layer kernel rewrites them
+// every layer), so they are read with L2-coherent loads (__ldcg), never
+// through the read-only path, whose per-SM lines could be stale.
+GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* q, const float* k, const float* v,
                                  const float2* __restrict__ rope, float* __restrict__ kc, float* __restrict__ vc,
-                                 float* __restrict__ part, int kv_mul, int hd, int kv_dim, int splits, float scale,
+                                 float* part, int kv_mul, int hd, int kv_dim, int splits, float scale,
                                  uint32_t max_pos, int* error, int g, int c, float* sm) {
   const uint32_t pos = st->pos, slot = st->slot;
   if (pos >= max_pos) {  // past the RoPE table: report, touch nothing
@@ -55,7 +59,7 @@ GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* 
   for (int i = threadIdx.x; i < kv_mul * half; i += blockDim.x) {
     const int h = i / half, j = i - h * half;
     const float2 r = cs[j];
-    const float v0 = qg[h * hd + j], v1 = qg[h * hd + j + half];
+    const float v0 = __ldcg(qg + h * hd + j), v1 = __ldcg(qg + h * hd + j + half);
     qs[h * hd + j] = __fsub_rn(__fmul_rn(v0, r.x), __fmul_rn(v1, r.y));
     qs[h * hd + j + half] = __fadd_rn(__fmul_rn(v0, r.y), __fmul_rn(v1, r.x));
   }
@@ -74,7 +78,7 @@ GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* 
     float* vrow = vc + (size_t)slot * kv_dim + (size_t)g * hd;
     for (int j = threadIdx.x; j < half; j += blockDim.x) {
       const float2 r = cs[j];
-      const float v0 = k[g * hd + j], v1 = k[g * hd + j + half];
+      const float v0 = __ldcg(k + g * hd + j), v1 = __ldcg(k + g * hd + j + half);
       const float r0 = __fsub_rn(__fmul_rn(v0, r.x), __fmul_rn(v1, r.y));
       const float r1 = __fadd_rn(__fmul_rn(v0, r.y), __fmul_rn(v1, r.x));
       ks[cur * hd + j] = r0;
@@ -83,7 +87,7 @@ GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* 
       krow[j + half] = r1;
     }
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-      const float val = v[g * hd + d];
+      const float val = __ldcg(v + g * hd + d);
       vs[cur * hd + d] = val;
       vrow[d] = val;
     }
@@ -134,18 +138,17 @@ GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* 
 }
 
 // Output element (head h, dimension d): the splits' partials merged.
-GI_DEVINL void attn_combine_one(const float* __restrict__ part, float* __restrict__ att, int hd, int splits, int h,
-                                int d) {
+GI_DEVINL void attn_combine_one(const float* part, float* __restrict__ att, int hd, int splits, int h, int d) {
   const float* ph = part + (size_t)h * splits * (hd + 2);
   float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, ph[s * (hd + 2)]);
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, __ldcg(ph + s * (hd + 2)));
   float L = 0.f, acc = 0.f;
   for (int s = 0; s < splits; ++s) {
-    const float m = ph[s * (hd + 2)];
+    const float m = __ldcg(ph + s * (hd + 2));
     if (m == -INFINITY) continue;
     const float f = (float)exp((double)(m - M));
-    L = fmaf(ph[s * (hd + 2) + 1], f, L);
-    acc = fmaf(ph[s * (hd + 2) + 2 + d], f, acc);
+    L = fmaf(__ldcg(ph + s * (hd + 2) + 1), f, L);
+    acc = fmaf(__ldcg(ph + s * (hd + 2) + 2 + d), f, acc);
   }
   if (d < hd) att[(size_t)h * hd + d] = L > 0.f ? acc / L : 0.f;
 }

@@ -144,13 +144,13 @@ GI_DEVINL float4 mul3(float4 a, float s, float4 w) {  // (a * s) * w, one roundi
                      __fmul_rn(__fmul_rn(a.z, s), w.z), __fmul_rn(__fmul_rn(a.w, s), w.w));
 }
 
-// Load of the activation vector: through the read-only path, or (C) with a
-// plain coherent load when the vector was written earlier in the same
-// kernel (the persistent decode-layer kernel), where the read-only path may
-// still hold an older copy.
+// Load of the activation vector: through the read-only path, or (C) with an
+// L2-coherent load (__ldcg) when the vector was written earlier in the same
+// kernel by other CTAs (the persistent decode-layer kernel), where the
+// read-only path may still hold an older copy.
 template <bool C>
 GI_DEVINL float4 ld_x4(const float4* p) {
-  if (C) return *p;
+  if (C) return __ldcg(p);
   return __ldg(p);
 }
 
@@ -164,7 +164,7 @@ __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
   const int j = lane >> 2, q = lane & 3;
   const int offA = 64 * (j >> 1) + 32 * (j & 1) + 4 * q, offB = offA + 16;  // stage_unit's a, b
   const int nku = p.nku;
-  const float* __restrict__ x = p.x;
+  const float* x = p.x;
   float scale = 1.f;
   if (F && p.xmode == kXNorm) {
     const float4* x4 = reinterpret_cast<const float4*>(x);

@@ -249,26 +249,103 @@ int quantize_host(int qtype, const float* src, int64_t rows, int64_t cols, uint8
 
 // Seeded N(0, std) weights, quantised row by row without holding the fp32
 // matrix.  Every 256-column block of row r draws from its own splitmix64
-// stream keyed by (seed, r, block) through the Box-Muller transform (in
-// double), so any rows and any 256-aligned column range can be generated on
-// their own (tensor-parallel shards) and the bytes do not depend on the
-// thread count.  F32 writes the float32 values themselves.
+// stream keyed by (seed, r, block), so any rows and any 256-aligned column
+// range can be generated on their own (tensor-parallel shards) and the
+// bytes do not depend on the thread count.  The normal deviates come from
+// the Marsaglia polar method in double precision, with the logarithm
+// written out below: every step is an integer operation or one correctly
+// rounded double add, multiply, divide or square root, so the host
+// (gi_quantize_seeded) and the device (gi_synth_weights) produce the same
+// bytes.  F32 writes the float32 values themselves.
 namespace {
-inline uint64_t splitmix64(uint64_t& s) {
+GI_HD uint64_t splitmix64(uint64_t& s) {
   uint64_t z = (s += 0x9E3779B97F4A7C15ull);
   z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
   z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
   return z ^ (z >> 31);
 }
-void normal_block(uint64_t seed, int64_t row, int64_t blk, float stddev, float* out, int64_t n) {
-  uint64_t s = seed * 0xD1B54A32D192ED03ull ^ (uint64_t)row * 0x8CB92BA72F3D8DD7ull ^
-               (uint64_t)blk * 0xA0761D6478BD642Full;
+
+// Correctly rounded double operations, spelled out so that the device
+// compiler cannot contract them (the host build uses -ffp-contract=off).
+GI_HD double dadd(double a, double b) {
+#ifdef __CUDA_ARCH__
+  return __dadd_rn(a, b);
+#else
+  return a + b;
+#endif
+}
+GI_HD double dmul(double a, double b) {
+#ifdef __CUDA_ARCH__
+  return __dmul_rn(a, b);
+#else
+  return a * b;
+#endif
+}
+GI_HD double ddiv(double a, double b) {
+#ifdef __CUDA_ARCH__
+  return __ddiv_rn(a, b);
+#else
+  return a / b;
+#endif
+}
+GI_HD double dsqrt(double a) {
+#ifdef __CUDA_ARCH__
+  return __dsqrt_rn(a);
+#else
+  return std::sqrt(a);
+#endif
+}
+
+// Natural logarithm of a positive normal double: s = m * 2^k with m in
+// [sqrt(1/2), sqrt(2)), ln m = 2 atanh(t) = 2 (t + t^3/3 + t^5/5 + ...) with
+// t = (m - 1) / (m + 1), |t| < 0.172, summed to t^23 (the next term is
+// below 2^-60 of the total).
+GI_HD double log_pos(double s) {
+  uint64_t bits;
+  std::memcpy(&bits, &s, 8);
+  int k = (int)((bits >> 52) & 0x7FF) - 1023;
+  bits = (bits & 0x000FFFFFFFFFFFFFull) | 0x3FF0000000000000ull;
+  double m;
+  std::memcpy(&m, &bits, 8);
+  if (m > 1.4142135623730951) {
+    m = dmul(m, 0.5);
+    ++k;
+  }
+  const double t = ddiv(dadd(m, -1.0), dadd(m, 1.0));
+  const double r = dmul(t, t);
+  double p = 2.0 / 23.0;
+  p = dadd(dmul(p, r), 2.0 / 21.0);
+  p = dadd(dmul(p, r), 2.0 / 19.0);
+  p = dadd(dmul(p, r), 2.0 / 17.0);
+  p = dadd(dmul(p, r), 2.0 / 15.0);
+  p = dadd(dmul(p, r), 2.0 / 13.0);
+  p = dadd(dmul(p, r), 2.0 / 11.0);
+  p = dadd(dmul(p, r), 2.0 / 9.0);
+  p = dadd(dmul(p, r), 2.0 / 7.0);
+  p = dadd(dmul(p, r), 2.0 / 5.0);
+  p = dadd(dmul(p, r), 2.0 / 3.0);
+  const double lnm = dadd(dmul(2.0, t), dmul(dmul(t, r), p));
+  return dadd(dmul((double)k, 0.6931471805599453), lnm);  // + k ln 2
+}
+
+GI_HD uint64_t block_stream(uint64_t seed, int64_t row, int64_t blk) {
+  return seed * 0xD1B54A32D192ED03ull ^ (uint64_t)row * 0x8CB92BA72F3D8DD7ull ^
+         (uint64_t)blk * 0xA0761D6478BD642Full;
+}
+
+// The first n (<= 256) deviates of N(0, stddev) of one block's stream.
+GI_HD void normal_block(uint64_t seed, int64_t row, int64_t blk, float stddev, float* out, int64_t n) {
+  uint64_t s = block_stream(seed, row, blk);
   for (int64_t i = 0; i < n; i += 2) {
-    const double u1 = ((splitmix64(s) >> 11) + 1) * 0x1.0p-53;  // (0, 1]
-    const double u2 = (splitmix64(s) >> 11) * 0x1.0p-53;        // [0, 1)
-    const double r = std::sqrt(-2.0 * std::log(u1)), a = 6.283185307179586 * u2;
-    out[i] = (float)(r * std::cos(a) * stddev);
-    if (i + 1 < n) out[i + 1] = (float)(r * std::sin(a) * stddev);
+    double u, v, q;
+    do {  // a point uniform in the unit disc (minus the centre)
+      u = dadd(dmul((double)(splitmix64(s) >> 11), 0x1.0p-52), -1.0);  // [-1, 1)
+      v = dadd(dmul((double)(splitmix64(s) >> 11), 0x1.0p-52), -1.0);
+      q = dadd(dmul(u, u), dmul(v, v));
+    } while (q >= 1.0 || q == 0.0);
+    const double f = dmul(dsqrt(ddiv(dmul(-2.0, log_pos(q)), q)), (double)stddev);
+    out[i] = (float)dmul(u, f);
+    if (i + 1 < n) out[i + 1] = (float)dmul(v, f);
   }
 }
 }  // namespace
@@ -313,35 +390,17 @@ int quantize_seeded(int qtype, uint64_t seed, float stddev, int64_t row0, int64_
 }
 
 // ---- device generator of the synthetic benchmark models --------------------
-// The same splitmix64 streams as normal_block (one per (seed, row, 256-column
-// block)), but a float32 Box-Muller transform, and the block quantisers
-// above: one thread per 256-column block.  Deterministic on a given GPU; not
-// bit-identical to the host generator (float vs double transform).
+// gi_quantize_seeded's generator and block quantisers on the device, one
+// thread per 256-column block: the same bytes as the host, in a fraction of
+// a second for a 70B-shaped model.
 namespace {
-__device__ inline uint64_t splitmix64_d(uint64_t& s) {
-  uint64_t z = (s += 0x9E3779B97F4A7C15ull);
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
-}
-
 __global__ void synth_kernel(int qtype, uint64_t seed, float stddev, int64_t row0, int64_t rows, int64_t col0,
                              int64_t nblk, uint8_t* __restrict__ dst, int64_t rb) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * nblk) return;
   const int64_t r = i / nblk, b = i - r * nblk;
   float w[256];
-  uint64_t s = seed * 0xD1B54A32D192ED03ull ^ (uint64_t)(row0 + r) * 0x8CB92BA72F3D8DD7ull ^
-               (uint64_t)(col0 / 256 + b) * 0xA0761D6478BD642Full;
-  for (int k = 0; k < 256; k += 2) {
-    const float u1 = (float)((splitmix64_d(s) >> 40) + 1) * 0x1.0p-24f;  // (0, 1]
-    const float u2 = (float)(splitmix64_d(s) >> 40) * 0x1.0p-24f;        // [0, 1)
-    const float rad = sqrtf(-2.0f * logf(u1));
-    float sn, cs;
-    sincospif(2.0f * u2, &sn, &cs);
-    w[k] = rad * cs * stddev;
-    w[k + 1] = rad * sn * stddev;
-  }
+  normal_block(seed, row0 + r, col0 / 256 + b, stddev, w, 256);
   uint8_t* o = dst + r * rb;
   if (qtype == kTypeQ4_K) {
     q4_k_block(w, o + 144 * b);

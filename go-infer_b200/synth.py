@@ -55,9 +55,10 @@ class LlamaConfig:
 LLAMA2_7B = LlamaConfig(n_layers=32, dim=4096, hidden=11008, n_heads=32, n_kv_heads=32, vocab=32000, max_seq=192)
 
 # Config 5: Llama-3-70B shape (80 layers, d=8192, 64 query / 8 KV heads, FFN
-# 28672, vocab 128256, RoPE base 500000), 512-token prompt + 64 greedy steps.
+# 28672, vocab 128256, RoPE base 500000), every matrix Q4_K (the output head
+# too), 512-token prompt + 64 greedy steps.
 LLAMA3_70B = LlamaConfig(n_layers=80, dim=8192, hidden=28672, n_heads=64, n_kv_heads=8, vocab=128256, max_seq=576,
-                         rope_theta=500000.0)
+                         rope_theta=500000.0, out_type=G.TYPE_Q4_K)
 
 LAYER_MATS = ("wq", "wk", "wv", "wo", "ffn_gate", "ffn_up", "ffn_down")
 

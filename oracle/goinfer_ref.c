@@ -318,6 +318,22 @@ static void* chunk_run_f64(void* arg) {
   return NULL;
 }
 
+/* Sum over k of |w[r][k] * x[k]| in double, over the reference's float32
+ * dequantised rows: the conditioning of each output (a test statistic, not
+ * a reference function). */
+static void* chunk_run_abs(void* arg) {
+  chunk_t* c = (chunk_t*)arg;
+  float* deq = (float*)malloc((size_t)c->cols * sizeof(float));
+  for (int64_t r = c->start; r < c->end; r++) {
+    deq_row(c->type, c->raw + r * c->bpr, c->cols, c->bpr, deq);
+    double s = 0.0;
+    for (int64_t k = 0; k < c->cols; k++) s += fabs((double)deq[k] * (double)c->x[k]);
+    c->y64[r] = s;
+  }
+  free(deq);
+  return NULL;
+}
+
 /* The row chunking of pkg/math/gemv.go:134-167 (identical for every type). */
 static int run_chunks(int type, float* y, double* y64, const float* x, const uint8_t* raw,
                       int64_t rows, int64_t cols, int nthreads, void* (*fn)(void*)) {
@@ -355,6 +371,11 @@ int ref_matmul(int type, float* y, const float* x, const uint8_t* raw, int64_t r
 int ref_matmul_f64(int type, double* y, const float* x, const uint8_t* raw, int64_t rows,
                    int64_t cols, int nthreads) {
   return run_chunks(type, NULL, y, x, raw, rows, cols, nthreads, chunk_run_f64);
+}
+
+int ref_matmul_absdot(int type, double* y, const float* x, const uint8_t* raw, int64_t rows,
+                      int64_t cols, int nthreads) {
+  return run_chunks(type, NULL, y, x, raw, rows, cols, nthreads, chunk_run_abs);
 }
 
 int ref_matmul_batch(int type, float* y, const float* x, const uint8_t* raw, int64_t batch,

@@ -87,6 +87,9 @@ int ref_matmul_f64(int type, double* y, const float* x, const uint8_t* raw,
  * Layout as the Metal batched kernels use it (kernels.metal:678):
  * y[b*rows + r], x[b*cols + k].
  */
+/* Per row, sum of |w*x| in double (the conditioning of each output). */
+int ref_matmul_absdot(int type, double* y, const float* x, const uint8_t* raw, int64_t rows,
+                      int64_t cols, int nthreads);
 int ref_matmul_batch(int type, float* y, const float* x, const uint8_t* raw,
                      int64_t batch, int64_t rows, int64_t cols, int nthreads);
 

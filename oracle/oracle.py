@@ -64,6 +64,8 @@ def lib() -> ctypes.CDLL:
         L.ref_matmul.restype = ctypes.c_int
         L.ref_matmul_f64.argtypes = [ctypes.c_int, f64p, f32p, u8p, i64, i64, ctypes.c_int]
         L.ref_matmul_f64.restype = ctypes.c_int
+        L.ref_matmul_absdot.argtypes = [ctypes.c_int, f64p, f32p, u8p, i64, i64, ctypes.c_int]
+        L.ref_matmul_absdot.restype = ctypes.c_int
         L.ref_matmul_batch.argtypes = [ctypes.c_int, f32p, f32p, u8p, i64, i64, i64, ctypes.c_int]
         L.ref_matmul_batch.restype = ctypes.c_int
         _lib = L
@@ -149,6 +151,20 @@ def matmul_f64(qtype: int, x: np.ndarray, raw: np.ndarray, rows: int, cols: int,
                               _f32(x), _u8(raw), rows, cols, nthreads or os.cpu_count() or 1)
     if rc:
         raise ValueError(f"ref_matmul_f64: unsupported type {qtype}")
+    return y
+
+
+def matmul_absdot(qtype: int, x: np.ndarray, raw: np.ndarray, rows: int, cols: int,
+                  nthreads: int | None = None) -> np.ndarray:
+    """Per row, sum over k of |w[r,k] * x[k]| (double) over the reference's
+    float32 dequantised weights: the conditioning of each output."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    raw = np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1)
+    y = np.empty(rows, dtype=np.float64)
+    rc = lib().ref_matmul_absdot(qtype, y.ctypes.data_as(ctypes.POINTER(ctypes.c_double)),
+                                 _f32(x), _u8(raw), rows, cols, nthreads or os.cpu_count() or 1)
+    if rc:
+        raise ValueError(f"ref_matmul_absdot: unsupported type {qtype}")
     return y
 
 
@@ -286,13 +302,17 @@ class RefModel:
             raise RuntimeError(f"ref_forward failed: {rc}")
         return logits
 
-    def greedy(self, prompt, n_gen: int, start_pos: int = 0):
+    def greedy(self, prompt, n_gen: int, start_pos: int = 0, progress=None):
         """Engine.Generate at temperature 0 with sequential prefill: the ids
-        and, per generated id, the top-2 logit margin."""
+        and, per generated id, the top-2 logit margin.  progress(i, n), if
+        given, is called before forward step i of n."""
         L = lib(); _forward_sigs(L)
         pos = start_pos
         logits = None
+        total = len(prompt) + n_gen - 1
         for t in prompt:
+            if progress:
+                progress(pos - start_pos, total)
             logits = self.forward(int(t), pos)
             pos += 1
         ids, margins = [], []
@@ -302,6 +322,8 @@ class RefModel:
             ids.append(nxt)
             margins.append(float(top[1] - top[0]))
             if i + 1 < n_gen:
+                if progress:
+                    progress(pos - start_pos, total)
                 logits = self.forward(nxt, pos)
                 pos += 1
         return np.array(ids, np.uint32), np.array(margins), logits

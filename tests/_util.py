@@ -26,11 +26,41 @@ def rel_err(y, ref):
     return np.abs(y - ref) / den
 
 
-def assert_parity(y, ref, tol=REL_TOL, what=""):
+def plain_rel_err(y, ref):
+    """Per-element |y - ref| / |ref| with no floor (0 where both are 0)."""
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    d = np.abs(y - ref)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        e = np.where(d == 0, 0.0, d / np.abs(ref))
+    return e
+
+
+def parity_line(y, ref, absdot=None, what=""):
+    """One line reporting both figures: the floored per-element relative
+    error (the bar) and the plain per-element relative error, with, given
+    absdot = sum_k |w[r,k] x[k]| per row, the condition number
+    absdot / |ref| of the row where the plain error is largest -- how much
+    cancellation amplifies the float32 rounding there."""
+    fl = rel_err(y, ref)
+    pl = plain_rel_err(y, ref)
+    if not pl.size:
+        return f"{what}: empty"
+    i = int(np.argmax(pl))
+    line = f"{what}: max rel err {fl.max():.2e} (floored), plain {pl[i]:.2e} at row {i}"
+    if absdot is not None:
+        r = abs(float(np.asarray(ref, np.float64)[i]))
+        kappa = float(absdot[i]) / r if r > 0 else float("inf")
+        line += f" (condition number {kappa:.3g})"
+    return line
+
+
+def assert_parity(y, ref, tol=REL_TOL, what="", absdot=None):
     e = rel_err(y, ref)
     worst = int(np.argmax(e)) if e.size else 0
     assert e.size == 0 or e.max() <= tol, (
         f"{what}: max rel err {e.max():.3e} at {worst} (y={y[worst]!r}, ref={ref[worst]!r})")
+    print(parity_line(y, ref, absdot, what))
     return float(e.max()) if e.size else 0.0
 
 

@@ -101,12 +101,58 @@ def test_config_shapes_match_oracle(what, qt, rows, cols, ws, xs):
     x = seeded_x(xs, cols)
     y = gpu_gemv(qt, raw, x, rows, cols)
     ref = O.matmul(qt, x, raw, rows, cols)
-    worst = assert_parity(y, ref, what=what)
+    assert_parity(y, ref, what=what, absdot=O.matmul_absdot(qt, x, raw, rows, cols))
     # the GPU sits as close to the exact product as the reference itself does
     exact = O.matmul_f64(qt, x, raw, rows, cols)
     scale = np.sqrt(np.mean(exact ** 2))
     assert np.max(np.abs(y - exact)) <= 4 * np.max(np.abs(ref - exact)) + 1e-6 * scale
-    print(f"{what}: max rel err {worst:.2e}")
+
+
+@pytest.mark.parametrize("rows,cols", [(32000, 4096), (1000, 2048), (17, 8192), (3, 2048), (4100, 2048),
+                                       (160, 45056)])
+def test_q6k_tensor_core_kernel_matches_oracle(rows, cols):
+    """The Q6_K GEMV on the int8 tensor cores (gi_cuda_set_q6k_mma; rows of
+    whole 2048-column groups) against DotVecQ6_K (quant.go:256-291, 542-545):
+    the lm_head shape, ragged row counts and a row too long to stage."""
+    raw = G.quantize_seeded(G.TYPE_Q6_K, 600 + rows, 0.02, rows, cols)
+    x = seeded_x(rows + 3, cols)
+    x[::131] *= 40  # activation outliers
+    G.set_q6k_mma(True)
+    try:
+        y = gpu_gemv(G.TYPE_Q6_K, raw, x, rows, cols)
+        again = gpu_gemv(G.TYPE_Q6_K, raw, x, rows, cols)
+    finally:
+        G.set_q6k_mma(False)
+    ref = O.matmul(G.TYPE_Q6_K, x, raw, rows, cols)
+    assert_parity(y, ref, what=f"q6k mma {rows}x{cols}", absdot=O.matmul_absdot(G.TYPE_Q6_K, x, raw, rows, cols))
+    assert np.array_equal(y.view(np.uint32), again.view(np.uint32))
+    exact = O.matmul_f64(G.TYPE_Q6_K, x, raw, rows, cols)
+    scale = np.sqrt(np.mean(exact ** 2))
+    assert np.max(np.abs(y - exact)) <= 4 * np.max(np.abs(ref - exact)) + 1e-6 * scale
+
+
+def test_q6k_tensor_core_kernel_70b_head_rows():
+    """The 128256 x 8192 head shape on the Q6_K tensor-core kernel: every row
+    against the CPU-core kernel's, a row sample against the oracle."""
+    rows, cols = 128256, 8192
+    raw = G.quantize_seeded(G.TYPE_Q6_K, 77, 0.02, rows, cols)
+    x = seeded_x(78, cols)
+    buf = G.CreateBuffer(raw)
+    try:
+        y_mma, y_core = np.zeros(rows, np.float32), np.zeros(rows, np.float32)
+        G.set_q6k_mma(True)
+        try:
+            G.MatMulBuf(G.TYPE_Q6_K, y_mma, x, buf, rows, cols)
+        finally:
+            G.set_q6k_mma(False)
+        G.MatMulBuf(G.TYPE_Q6_K, y_core, x, buf, rows, cols)
+    finally:
+        G.ReleaseBuffer(buf)
+    assert_parity(y_mma, y_core.astype(np.float64), what="q6k mma vs cuda-core kernel")
+    pick = np.sort(np.random.default_rng(79).choice(rows, 512, replace=False))
+    rb = G.row_bytes(G.TYPE_Q6_K, cols)
+    sub = np.concatenate([raw[r * rb:(r + 1) * rb] for r in pick])
+    assert_parity(y_mma[pick], O.matmul(G.TYPE_Q6_K, x, sub, len(pick), cols), what="q6k mma head rows")
 
 
 @pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])

@@ -60,3 +60,18 @@ def test_quantize_rejects_bad_shapes():
     with pytest.raises(G.GoInferCudaError) as e:
         G.quantize(3, np.zeros((2, 256), np.float32))
     assert e.value.code == G.ERR_UNSUPPORTED_TYPE
+
+
+def test_numpy_q4_k_restatement_matches_library_bytewise():
+    """oracle/quantize_np.py (the reference arm's input preparation, which
+    must not load the product library) gives the library's Q4_K bytes."""
+    import quantize_np
+    rng = np.random.default_rng(17)
+    for rows, cols, std in ((64, 4096, 0.02), (300, 512, 3e4), (8, 256, 1e-6), (16, 1024, 1.0)):
+        w = rng.normal(0, std, (rows, cols)).astype(np.float32)
+        w[0, :32] = 0           # one all-zero sub-block
+        w[1, :256] = 5.0        # constant positive block (offset -0)
+        w[2, :256] = -1e-30     # scales underflow the truncating fp16
+        w[3, :256] = 0          # all-zero block
+        w[4, :256] = -2.0       # constant negative block
+        assert np.array_equal(quantize_np.quantize_q4_k(w), G.quantize(G.TYPE_Q4_K, w))

@@ -29,6 +29,7 @@ def main():
     ap.add_argument("--config", default="small")
     ap.add_argument("--seed", type=int, default=21)
     ap.add_argument("--prompt", type=int, default=12)
+    ap.add_argument("--prompt-seed", type=int, default=None, help="numpy seed of the prompt (default seed + 1)")
     ap.add_argument("--gen", type=int, default=16)
     ap.add_argument("--out", required=True)
     ap.add_argument("--device-synth", action="store_true", help="draw the weights on the GPU")
@@ -44,7 +45,8 @@ def main():
     dev, model = tp.build(cfg, a.seed, rank, world, device_synth=a.device_synth)
     if a.persistent:
         model.set_persistent(True)
-    prompt = np.random.default_rng(a.seed + 1).integers(0, cfg.vocab, a.prompt)
+    pseed = a.seed + 1 if a.prompt_seed is None else a.prompt_seed
+    prompt = np.random.default_rng(pseed).integers(0, cfg.vocab, a.prompt)
     ids, ms = tp.greedy(model, prompt, a.gen)
     all_ids = [None] * world
     dist.all_gather_object(all_ids, ids.tolist())
