@@ -25,9 +25,13 @@ matrix from HBM.
 the Go code cannot be built here) on the same workload and prints the same
 line with "impl": "reference".
 
-Multi-GPU: one process per GPU (torchrun); each rank runs its own copy of
-the workload (the GEMV units are independent, no collective on this path):
-weak scaling, value = bytes of all ranks / max rank time.
+Multi-GPU: one process per GPU (torchrun).  At N > 1 the step is config
+2's FFN block split Megatron-style across the ranks (gate/up rows and the
+matching down columns, in whole 256-column Q4_K blocks), the all-reduce of
+the down partials fused into the down GEMV's epilogue over NVLink
+(gi_cuda_ffn_dev): strong scaling, value = the FFN's bytes / max rank time.
+At N=1 ffn_block times the same FFN block on one GPU, the reference point of
+those lines.
 
 decode   (the metric's second half) greedy decode tokens/s of the Llama-
          shaped synthetic models, device-timed (CUDA events around the
@@ -38,8 +42,9 @@ decode   (the metric's second half) greedy decode tokens/s of the Llama-
          3, 512 tokens x 4096 columns) at N=1.  --persistent adds, under
          "persistent", the same generations with every layer of a step in
          one persistent launch (gi_cuda_model_set_persistent), and whether
-         their ids equal the per-layer launches'.  --q6k-mma adds the Q6_K
-         lm_head shapes on the int8 tensor-core kernel (gemv_other, "_mma").
+         their ids equal the per-layer launches'.  gemv_other times the Q6_K
+         lm_head shapes on both Q6_K kernels (the int8 tensor-core default and
+         "_cuda_cores").
 --e2e-batch  runs the e2e step's three calls inside gi_cuda_begin_batch /
          gi_cuda_end_batch (go-infer's metal.BeginBatch/EndBatch: one wait
          per step), after checking that it reproduces the call-by-call step.
@@ -198,9 +203,15 @@ def cpu_port_gemv_gbs(budget_s, row_frac=1.0):
     return done_bytes / el / 1e9, threads, sample
 
 
+TP_WORKLOAD = ("config2 FFN block, Llama-7B shapes, Megatron-split: x += down(SwiGLU(gate(n), up(n))), "
+               "n = RMSNorm(x); gate/up 11008x4096 column-split and down 4096x11008 row-split in whole 256-column "
+               "blocks; two launches per rank, the all-reduce of the down partials fused into its epilogue")
+
+
 def step_config(world):
     """The line's config, the same in both arms."""
-    return {"workload": WORKLOAD, "parallelism": f"replicas x{world}" if world > 1 else "single",
+    return {"workload": WORKLOAD if world == 1 else TP_WORKLOAD,
+            "parallelism": f"tensor parallel x{world}" if world > 1 else "single",
             "l2": (f"inputs larger than L2: GPU arm {NCOPIES} rotating weight copies "
                    f"({NCOPIES * STEP_BYTES / 1e6:.0f} MB > 126 MB L2); CPU arm {STEP_BYTES / 1e6:.0f} MB per step"),
             "graph": "GPU arm: K steps in one CUDA graph, programmatic dependent launch; CPU arm: one call per matrix"}
@@ -293,7 +304,7 @@ def decode_section(args, world, rank, local, pg):
     if world > 1:
         pg.barrier()
         G.tp_close()
-    out["config5"] = {"model": "Llama-3-70B shape (80 x d8192, 64/8 heads, FFN 28672, vocab 128256), Q4_K + Q6_K head",
+    out["config5"] = {"model": "Llama-3-70B shape (80 x d8192, 64/8 heads, FFN 28672, vocab 128256), every matrix Q4_K",
                       "parallelism": f"tensor parallel x{world}" if world > 1 else "single GPU",
                       "prompt": 512, "steps": 64, "tok_s": round(63 / (ms / 1e3), 2),
                       "ms_per_token": round(ms / 63, 4),
@@ -340,14 +351,13 @@ def decode_section(args, world, rank, local, pg):
     # plain decode GEMV, rotating weight copies past the L2, graph + PDL
     peak, _kind = measured_peak()
     other = {}
-    shapes = [("q8_0_config1_4096x4096", G.TYPE_Q8_0, 4096, 4096, False),
-              ("q6_k_lm_head_32000x4096", G.TYPE_Q6_K, 32000, 4096, False),
-              ("q6_k_lm_head_128256x8192", G.TYPE_Q6_K, 128256, 8192, False)]
-    if args.q6k_mma:  # the same Q6_K shapes on the int8 tensor-core kernel
-        shapes += [(n + "_mma", qt, r, c, True) for n, qt, r, c, _m in shapes if qt == G.TYPE_Q6_K]
+    # Q6_K: the int8 tensor-core kernel (the default) and the CUDA-core one
+    shapes = [("q8_0_config1_4096x4096", G.TYPE_Q8_0, 4096, 4096, True),
+              ("q6_k_lm_head_32000x4096", G.TYPE_Q6_K, 32000, 4096, True),
+              ("q6_k_lm_head_128256x8192", G.TYPE_Q6_K, 128256, 8192, True)]
+    shapes += [(n + "_cuda_cores", qt, r, c, False) for n, qt, r, c, _m in shapes if qt == G.TYPE_Q6_K]
     for name, qt, rows, cols, mma in shapes:
-        if args.q6k_mma:
-            G.set_q6k_mma(mma)
+        G.set_q6k_mma(mma)
         wbytes = rows * G.row_bytes(qt, cols)
         ncopy = max(2, int(2 * 126e6 / wbytes) + 1)
         bufs = [G.synth_buffer(qt, 20 + c, 0.02, rows, cols) for c in range(ncopy)]
@@ -373,8 +383,7 @@ def decode_section(args, world, rank, local, pg):
         del graph
         for b in bufs:
             G.ReleaseBuffer(b)
-    if args.q6k_mma:
-        G.set_q6k_mma(False)
+    G.set_q6k_mma(True)
     out["gemv_other"] = other
     # config 3: prefill dequant-GEMM (512 tokens x 4096 columns)
     x = torch.randn(512, 4096, device=dev)
@@ -441,59 +450,27 @@ def step_distribution(capture, steps_per_replay=100, replays=20):
         return {"error": f"{type(exc).__name__}: {exc}"[:200]}
 
 
-def run_ours(args):
+def ffn_shard(world, rank):
+    """(h0, hn): rank's slice of the FFN hidden dimension under the Megatron
+    split, in whole 256-column Q4_K blocks (11008 = 43 blocks, so slices
+    differ by at most one block)."""
+    nsb = GATE[0] // 256
+    b0, b1 = nsb * rank // world, nsb * (rank + 1) // world
+    return 256 * b0, 256 * (b1 - b0)
+
+
+def time_graph(capture, steps, warmup, pg, local, dev):
+    """Device time (ms, max over ranks) of `steps` steps captured in one
+    CUDA graph, after `warmup` untimed steps and one untimed replay of the
+    timed graph itself; barrier and synchronize on both sides; clocks
+    sampled during the timed replay."""
     import torch
-    import goinfer_cuda as G
-
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    pg = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-        pg = dist
-    G.Init(local)
-    dev = torch.device("cuda", local)
-
-    # weights: one seeded layer, replicated into NCOPIES distinct HBM copies
-    raws = {"gate": G.quantize(G.TYPE_Q4_K, seeded(3, GATE, 0.02)),
-            "up": G.quantize(G.TYPE_Q4_K, seeded(4, GATE, 0.02)),
-            "down": G.quantize(G.TYPE_Q4_K, seeded(5, DOWN, 0.02))}
-    copies = {k: [torch.from_numpy(v).to(dev) for _ in range(NCOPIES)] for k, v in raws.items()}
-    xg = torch.from_numpy(seeded(101, GATE[1], 1.0)).to(dev)
-    xd = torch.from_numpy(seeded(102, DOWN[1], 1.0)).to(dev)
-    yg = torch.empty(GATE[0], device=dev)
-    yu = torch.empty(GATE[0], device=dev)
-    yd = torch.empty(DOWN[0], device=dev)
-
-    def step(i, stream):
-        # gate and up share their activation: one launch for both (as the
-        # decode engine runs them), then down.
-        c = i % NCOPIES
-        wg, wu, wd = copies["gate"][c], copies["up"][c], copies["down"][c]
-        G.gemv_multi_dev(G.TYPE_Q4_K, [yg.data_ptr(), yu.data_ptr()], xg.data_ptr(), [wg.data_ptr(), wu.data_ptr()],
-                         [wg.numel(), wu.numel()], [GATE[0], GATE[0]], GATE[1], stream)
-        G.gemv_dev(G.TYPE_Q4_K, yd.data_ptr(), xd.data_ptr(), wd.data_ptr(), wd.numel(), DOWN[0], DOWN[1], stream)
-
-    G.set_pdl(True)
-
-    def capture(nsteps):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            s = torch.cuda.current_stream().cuda_stream
-            for i in range(nsteps):
-                step(i, s)
-        return g
-
-    g_warm = capture(max(args.warmup, 3))
-    g_timed = capture(args.steps)
+    g_warm = capture(max(warmup, 3))
+    g_timed = capture(steps)
     for _ in range(2):
         g_warm.replay()
     g_timed.replay()  # uploads the timed graph: its first replay is not timed
     torch.cuda.synchronize()
-
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if pg:
         pg.barrier()
@@ -509,41 +486,149 @@ def run_ours(args):
     t = torch.tensor([ms], device=dev)
     if pg:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = STEP_BYTES * args.steps * world / (ms_max / 1e3) / 1e9
+    del g_timed, g_warm
+    return float(t.item()), ms, clocks.summary()
+
+
+def run_ours(args):
+    import torch
+    import goinfer_cuda as G
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    G.Init(local)
+    dev = torch.device("cuda", local)
+    G.set_pdl(True)
+    stream_of = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+
+    # ---- config 2's FFN block, Megatron-split over the ranks (any N) --------
+    # x += down(SwiGLU(gate(n), up(n))), n = RMSNorm(x): gate/up rows
+    # [h0, h0 + hn) and the same columns of down on this rank; the down
+    # GEMV sums the ranks' partials in its epilogue (gi_cuda_ffn_dev).
+    import tp
+    if world > 1:
+        tp.connect(rank, world, DOWN[0])
+    h0, hn = ffn_shard(world, rank)
+    fw = {"gate": G.quantize(G.TYPE_Q4_K, seeded(3, GATE, 0.02)[h0:h0 + hn]),
+          "up": G.quantize(G.TYPE_Q4_K, seeded(4, GATE, 0.02)[h0:h0 + hn]),
+          "down": G.quantize(G.TYPE_Q4_K, np.ascontiguousarray(seeded(5, DOWN, 0.02)[:, h0:h0 + hn]))}
+    rank_bytes = sum(v.nbytes for v in fw.values())
+    ncopy = max(NCOPIES, -(-300_000_000 // rank_bytes))  # > 2x the 126 MB L2 on every rank
+    fcopies = {k: [torch.from_numpy(v).to(dev) for _ in range(ncopy)] for k, v in fw.items()}
+    norm = torch.ones(DOWN[0], device=dev)
+    x_ffn = torch.from_numpy(seeded(101, GATE[1], 1.0)).to(dev)
+    h = torch.empty(hn, device=dev)
+
+    def ffn_step(i, stream):
+        c = i % ncopy
+        wg, wu, wd = fcopies["gate"][c], fcopies["up"][c], fcopies["down"][c]
+        G.ffn_dev(x_ffn.data_ptr(), norm.data_ptr(), wg.data_ptr(), wu.data_ptr(), wd.data_ptr(), wg.numel(),
+                  wu.numel(), wd.numel(), h.data_ptr(), DOWN[0], hn, 1e-5, stream)
+
+    def capture_ffn(nsteps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            s = stream_of()
+            for i in range(nsteps):
+                ffn_step(i, s)
+        return g
+
+    # ---- config 2 as BASELINE states it (N=1): gate and up (one launch,
+    # shared activation), then down, all on N(0, 1) activations -------------
+    if world == 1:
+        raws = {"gate": G.quantize(G.TYPE_Q4_K, seeded(3, GATE, 0.02)),
+                "up": G.quantize(G.TYPE_Q4_K, seeded(4, GATE, 0.02)),
+                "down": G.quantize(G.TYPE_Q4_K, seeded(5, DOWN, 0.02))}
+        copies = {k: [torch.from_numpy(v).to(dev) for _ in range(NCOPIES)] for k, v in raws.items()}
+        xg = torch.from_numpy(seeded(101, GATE[1], 1.0)).to(dev)
+        xd = torch.from_numpy(seeded(102, DOWN[1], 1.0)).to(dev)
+        yg = torch.empty(GATE[0], device=dev)
+        yu = torch.empty(GATE[0], device=dev)
+        yd = torch.empty(DOWN[0], device=dev)
+
+        def gemv_step(i, stream):
+            c = i % NCOPIES
+            wg, wu, wd = copies["gate"][c], copies["up"][c], copies["down"][c]
+            G.gemv_multi_dev(G.TYPE_Q4_K, [yg.data_ptr(), yu.data_ptr()], xg.data_ptr(),
+                             [wg.data_ptr(), wu.data_ptr()], [wg.numel(), wu.numel()], [GATE[0], GATE[0]], GATE[1],
+                             stream)
+            G.gemv_dev(G.TYPE_Q4_K, yd.data_ptr(), xd.data_ptr(), wd.data_ptr(), wd.numel(), DOWN[0], DOWN[1],
+                       stream)
+
+        def capture(nsteps):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                s = stream_of()
+                for i in range(nsteps):
+                    gemv_step(i, s)
+            return g
+    else:
+        capture = capture_ffn
+
+    ms_max, ms, clocks = time_graph(capture, args.steps, args.warmup, pg, local, dev)
+    value = STEP_BYTES * args.steps / (ms_max / 1e3) / 1e9  # the whole step's bytes, over all ranks
+    launch_bytes = (STEP_BYTES / 2) if world == 1 else rank_bytes / 2
     launch_ms = ms / (2 * args.steps)  # this rank's average Q4_K GEMV launch
-    achieved = (STEP_BYTES / 2) / (launch_ms / 1e3) / 1e9
+    achieved = launch_bytes / (launch_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
     dist = step_distribution(capture)
+    ffn_block = None
+    if world == 1:  # the FFN block at N=1: the reference point of the N>1 lines
+        f_ms, _f, _c = time_graph(capture_ffn, args.steps, args.warmup, None, local, dev)
+        ffn_block = {"gbs": round(STEP_BYTES * args.steps / (f_ms / 1e3) / 1e9, 2),
+                     "us_per_step": round(f_ms * 1e3 / args.steps, 3),
+                     "what": "gi_cuda_ffn_dev: RMSNorm + gate/up + SwiGLU (one launch), down + residual (second)"}
 
-    # e2e through the reference-facing C ABI: host x/y, resident weights
-    bufs = {k: G.CreateBuffer(v) for k, v in raws.items()}
-    px_g = torch.from_numpy(seeded(101, GATE[1], 1.0)).pin_memory()
-    px_d = torch.from_numpy(seeded(102, DOWN[1], 1.0)).pin_memory()
-    py_g, py_u = torch.empty(GATE[0]).pin_memory(), torch.empty(GATE[0]).pin_memory()
-    py_d = torch.empty(DOWN[0]).pin_memory()
-    hx_g, hx_d = px_g.numpy(), px_d.numpy()
-    hy_g, hy_u, hy_d = py_g.numpy(), py_u.numpy(), py_d.numpy()
+    # ---- e2e through the reference-facing C ABI: host x (and y), resident weights
+    if world == 1:
+        bufs = {k: G.CreateBuffer(v) for k, v in raws.items()}
+        px_g = torch.from_numpy(seeded(101, GATE[1], 1.0)).pin_memory()
+        px_d = torch.from_numpy(seeded(102, DOWN[1], 1.0)).pin_memory()
+        py_g, py_u = torch.empty(GATE[0]).pin_memory(), torch.empty(GATE[0]).pin_memory()
+        py_d = torch.empty(DOWN[0]).pin_memory()
+        hx_g, hx_d = px_g.numpy(), px_d.numpy()
+        hy_g, hy_u, hy_d = py_g.numpy(), py_u.numpy(), py_d.numpy()
 
-    def e2e_calls():
-        G.MatMulBuf(G.TYPE_Q4_K, hy_g, hx_g, bufs["gate"], *GATE)
-        G.MatMulBuf(G.TYPE_Q4_K, hy_u, hx_g, bufs["up"], *GATE)
-        G.MatMulBuf(G.TYPE_Q4_K, hy_d, hx_d, bufs["down"], *DOWN)
+        def e2e_calls():
+            G.MatMulBuf(G.TYPE_Q4_K, hy_g, hx_g, bufs["gate"], *GATE)
+            G.MatMulBuf(G.TYPE_Q4_K, hy_u, hx_g, bufs["up"], *GATE)
+            G.MatMulBuf(G.TYPE_Q4_K, hy_d, hx_d, bufs["down"], *DOWN)
 
-    def e2e_batched():  # metal.BeginBatch / EndBatch around the step: one wait per step
-        G.BeginBatch()
-        e2e_calls()
-        G.EndBatch()
+        def e2e_batched():  # metal.BeginBatch / EndBatch around the step: one wait per step
+            G.BeginBatch()
+            e2e_calls()
+            G.EndBatch()
 
-    e2e_step = e2e_batched if args.e2e_batch else e2e_calls
-    if args.e2e_batch:  # the batched step must give the call-by-call outputs, bit for bit
-        e2e_calls()
-        want = [a.copy() for a in (hy_g, hy_u, hy_d)]
-        for a in (hy_g, hy_u, hy_d):
-            a.fill(np.nan)
-        e2e_batched()
-        if not all(np.array_equal(a.view(np.uint32), b.view(np.uint32)) for a, b in zip((hy_g, hy_u, hy_d), want)):
-            raise RuntimeError("batched e2e step differs from the call-by-call step")
+        e2e_step = e2e_batched if args.e2e_batch else e2e_calls
+        if args.e2e_batch:  # the batched step must give the call-by-call outputs, bit for bit
+            e2e_calls()
+            want = [a.copy() for a in (hy_g, hy_u, hy_d)]
+            for a in (hy_g, hy_u, hy_d):
+                a.fill(np.nan)
+            e2e_batched()
+            if not all(np.array_equal(a.view(np.uint32), b.view(np.uint32))
+                       for a, b in zip((hy_g, hy_u, hy_d), want)):
+                raise RuntimeError("batched e2e step differs from the call-by-call step")
+        h2d, d2h = 4 * (GATE[1] + DOWN[1]), 4 * (2 * GATE[0] + DOWN[0])
+        api = ("gi_cuda_gemv_buf x3 inside gi_cuda_begin_batch/end_batch (host y/x, pinned)" if args.e2e_batch
+               else "gi_cuda_gemv_buf (host y/x, pinned: x copied in, y stored by the kernel)")
+    else:
+        bufs = {k: G.CreateBuffer(v) for k, v in fw.items()}
+        bufs["norm"] = G.CreateBuffer(np.ones(DOWN[0], np.float32))
+        hx = torch.from_numpy(seeded(101, GATE[1], 1.0)).pin_memory().numpy()
+
+        def e2e_step():
+            G.FFNBuf(hx, bufs["norm"], bufs["gate"], bufs["up"], bufs["down"], DOWN[0], hn, 1e-5)
+
+        h2d = d2h = 4 * DOWN[0]
+        api = "gi_cuda_ffn_buf (host x, pinned: copied in and back; the down partials all-reduced on the GPUs)"
 
     for _ in range(max(3, args.warmup)):
         e2e_step()
@@ -557,9 +642,13 @@ def run_ours(args):
     te = torch.tensor([e2e_s], device=dev)
     if pg:
         pg.all_reduce(te, op=pg.ReduceOp.MAX)
-    e2e_gbs = STEP_BYTES * e2e_steps * world / float(te.item()) / 1e9
+    e2e_gbs = STEP_BYTES * e2e_steps / float(te.item()) / 1e9
     for b in bufs.values():
         G.ReleaseBuffer(b)
+    del fcopies
+    if world > 1:
+        pg.barrier()
+        G.tp_close()
 
     decode = None if args.no_decode else decode_section(args, world, rank, local, pg)
 
@@ -573,29 +662,29 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "fp32",
             "data": "synthetic (seeded N(0,0.02) weights -> Q4_K, N(0,1) activations)",
             "config": step_config(world),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": profiled_traffic(),
+                         "frac": round(achieved / peak, 4), "traffic": profiled_traffic() if world == 1 else None,
                          "peak_source": peak_kind, "kernel": "gemv_q4k_kernel",
-                         "bytes_per_launch": STEP_BYTES // 2},
+                         "bytes_per_launch": int(launch_bytes)},
             "frac_of_8TBs": round(value / world / 8000.0, 4),
-            "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": 4 * (GATE[1] + DOWN[1]),
-                    "d2h_bytes_per_step": 4 * (2 * GATE[0] + DOWN[0]),
-                    "api": ("gi_cuda_gemv_buf x3 inside gi_cuda_begin_batch/end_batch (host y/x, pinned)" if args.e2e_batch
-                            else "gi_cuda_gemv_buf (host y/x, pinned: x copied in, y stored by the kernel)"),
-                    "steps": e2e_steps},
+            "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "api": api, "steps": e2e_steps},
             "gpu_launches": 2 * args.steps,
             "step_distribution": dist,
+            "ffn_block": ffn_block,
             "cpu_baseline": cpu,
-            "clocks": clocks.summary(),
+            "clocks": clocks,
             "decode": decode,
         }
+        if world > 1:
+            line["tp_shard"] = {"hidden_rows_per_rank": [ffn_shard(world, r)[1] for r in range(world)],
+                                "weight_bytes_per_rank": int(rank_bytes), "rotating_copies": ncopy}
         print(json.dumps(line), flush=True)
     if pg:
-        del g_timed, g_warm
         pg.barrier()
         pg.destroy_process_group()
 
@@ -611,8 +700,6 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / prefill section")
     ap.add_argument("--e2e-batch", action="store_true",
                     help="e2e step inside BeginBatch/EndBatch (one wait per step), checked against call-by-call")
-    ap.add_argument("--q6k-mma", action="store_true",
-                    help="also time the Q6_K lm_head shapes on the int8 tensor-core kernel (set_q6k_mma)")
     ap.add_argument("--persistent", action="store_true",
                     help="also time configs 4 and 5 with the persistent layers kernel (Model.set_persistent)")
     args = ap.parse_args()

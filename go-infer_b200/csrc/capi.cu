@@ -57,7 +57,7 @@ struct Ctx {
   size_t pinned_cap = 0;
   bool batch = false;
   bool pdl = false;
-  bool q6k_mma = false;
+  bool q6k_mma = true;  // gi_cuda_set_q6k_mma
   // Outputs of the open batch: still in device memory, copied back to their
   // host buffers when the batch ends; later calls of the batch read them there.
   gi::PendingOutputs pending;
@@ -1079,6 +1079,82 @@ int gi_cuda_gemv_multi_dev(int quant_type, int nmat, float* const* y, const floa
   if (rc) return fail(rc, rc == -2 ? "unsupported quant type" : rc == -4 ? "unsupported shape" : "launch failed",
                       rc == -5 ? cudaGetLastError() : cudaSuccess);
   return 0;
+}
+
+namespace {
+// The feed-forward half of a layer on this rank's shard: gate and up with
+// the RMSNorm prologue and SwiGLU epilogue into h, then down adding into x
+// (under tensor parallelism the ranks' partials, summed in its epilogue).
+int ffn_launch(float* x, const float* norm, const void* gate, const void* up, const void* down, size_t gate_bytes,
+               size_t up_bytes, size_t down_bytes, float* h, uint32_t dim, uint32_t hidden, float eps,
+               cudaStream_t s, bool pdl) {
+  const gi::GemvLaunch L = launch_cfg(pdl);
+  float* ys[2] = {h, h};  // the SwiGLU epilogue writes y[0]
+  const void* wgu[2] = {gate, up};
+  const size_t bgu[2] = {gate_bytes, up_bytes};
+  const int64_t rgu[2] = {hidden, hidden};
+  gi::GemvFuse f;
+  f.xmode = gi::kXNorm;
+  f.x2 = norm;
+  f.eps = eps;
+  f.ymode = gi::kYSwiGLU;
+  int rc = gi::gemv_q4k_fused(2, ys, x, wgu, bgu, rgu, dim, f, L, s);
+  if (rc) return rc;
+  gi::TpDev tp;
+  gi::GemvFuse fd;
+  fd.ymode = gi::kYAdd;
+  if (g_tp.connected && g_tp.world > 1) {
+    if ((int)dim > g_tp.max_dim) return -4;
+    tp = g_tp.dev;
+    tp.error = g.scratch.error;
+    fd.ymode = gi::kYPush;
+    fd.tp = &tp;
+  }
+  float* yd[1] = {x};
+  const void* wd[1] = {down};
+  const size_t bd[1] = {down_bytes};
+  const int64_t rd[1] = {dim};
+  return gi::gemv_q4k_fused(1, yd, h, wd, bd, rd, hidden, fd, L, s);
+}
+
+int ffn_fail(int rc) {
+  return fail(rc, rc == -4 ? "unsupported shape, alignment or buffer size" : "launch failed",
+              rc == -5 ? cudaGetLastError() : cudaSuccess);
+}
+}  // namespace
+
+int gi_cuda_ffn_dev(float* x, const float* norm, const void* gate, const void* up, const void* down,
+                    size_t gate_bytes, size_t up_bytes, size_t down_bytes, float* h, uint32_t dim, uint32_t hidden,
+                    float eps, void* stream) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!x || !norm || !gate || !up || !down || !h) return fail(-4, "null device pointer");
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+  const int rc = ffn_launch(x, norm, gate, up, down, gate_bytes, up_bytes, down_bytes, h, dim, hidden, eps, s, g.pdl);
+  return rc ? ffn_fail(rc) : 0;
+}
+
+int gi_cuda_ffn_buf(float* x, gi_cuda_buffer_t norm, gi_cuda_buffer_t gate, gi_cuda_buffer_t up,
+                    gi_cuda_buffer_t down, uint32_t dim, uint32_t hidden, float eps) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  if (int rc = ensure_ready()) return rc;
+  if (!x) return fail(-4, "null x");
+  if (!norm || !gate || !up || !down) return fail(-1, "null buffer");
+  if (g.batch) return fail(-4, "gi_cuda_ffn_buf: not inside gi_cuda_begin_batch / gi_cuda_end_batch");
+  const Buffer* bn = static_cast<const Buffer*>(norm);
+  if (bn->bytes < sizeof(float) * dim) return fail(-4, "norm buffer smaller than dim floats");
+  void* xd;
+  const size_t xbytes = (sizeof(float) * dim + 255) & ~(size_t)255;
+  if (int rc = arena_alloc(xbytes + sizeof(float) * hidden, &xd)) return rc;
+  float* hd = reinterpret_cast<float*>(static_cast<uint8_t*>(xd) + xbytes);
+  GI_CUDA_TRY(cudaMemcpyAsync(xd, x, sizeof(float) * dim, cudaMemcpyHostToDevice, g.stream), "copy x to device");
+  const Buffer *bg = static_cast<const Buffer*>(gate), *bu = static_cast<const Buffer*>(up),
+               *bd = static_cast<const Buffer*>(down);
+  const int rc = ffn_launch(static_cast<float*>(xd), static_cast<const float*>(bn->dptr), bg->dptr, bu->dptr, bd->dptr,
+                            bg->bytes, bu->bytes, bd->bytes, hd, dim, hidden, eps, g.stream, false);
+  if (rc) return ffn_fail(rc);
+  GI_CUDA_TRY(cudaMemcpyAsync(x, xd, sizeof(float) * dim, cudaMemcpyDeviceToHost, g.stream), "copy x to host");
+  return complete_locked();
 }
 
 int gi_cuda_set_pdl(int enable) {

@@ -37,8 +37,9 @@ struct GemvLaunch {
   int sm_count = 148;
   bool pdl = false;  // programmatic dependent launch (weights must not be
                      // written by the preceding kernel)
-  bool q6k_mma = false;  // Q6_K rows of whole 2048-column groups on the int8
-                         // tensor cores (gemv.cu, namespace q6m)
+  bool q6k_mma = true;  // Q6_K rows of whole 2048-column groups on the int8
+                        // tensor cores (gemv.cu, namespace q6m); false: the
+                        // CUDA-core kernel
 };
 
 // Per-device one-time set-up (kernel attributes); call with the device current.

@@ -48,7 +48,7 @@ EXPORTS = (
     "gi_cuda_gemm_buf", "gi_cuda_gemm_fused_gate_up_buf", "gi_cuda_add_residual", "gi_cuda_swiglu",
     "gi_cuda_gemv_q8_0", "gi_cuda_gemv_q4_k", "gi_cuda_gemv_q6_k",
     "gi_cuda_gemm_q8_0", "gi_cuda_gemm_q4_k", "gi_cuda_gemm_q6_k", "gi_cuda_gemv_dev",
-    "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl", "gi_cuda_set_q6k_mma",
+    "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_ffn_dev", "gi_cuda_ffn_buf", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl", "gi_cuda_set_q6k_mma",
     "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize", "gi_quantize_seeded",
     "gi_cuda_alloc_buffers", "gi_cuda_forward_transformer", "gi_cuda_model_create", "gi_cuda_model_destroy",
     "gi_cuda_model_reset", "gi_cuda_model_set_persistent", "gi_cuda_model_generate", "gi_cuda_tp_prepare", "gi_cuda_tp_connect", "gi_cuda_tp_close",
@@ -127,6 +127,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "gi_cuda_gemv_multi_dev": ([i32, i32, vp, vp, vp, vp, vp, u32, vp], i32),
         "gi_cuda_buffer_device_ptr": ([vp], vp),
         "gi_cuda_buffer_bytes": ([vp], sz),
+        "gi_cuda_ffn_dev": ([vp, vp, vp, vp, vp, sz, sz, sz, vp, u32, u32, ctypes.c_float, vp], i32),
+        "gi_cuda_ffn_buf": ([f32p, vp, vp, vp, vp, u32, u32, ctypes.c_float], i32),
         "gi_cuda_set_pdl": ([i32], i32),
         "gi_cuda_set_q6k_mma": ([i32], i32),
         "gi_cuda_last_error": ([], ctypes.c_char_p),
@@ -345,6 +347,23 @@ def gemv_multi_dev(quant_type: int, ys: list[int], x_ptr: int, ws: list[int], w_
     _err("gi_cuda_gemv_multi_dev", load_library().gi_cuda_gemv_multi_dev(
         quant_type, n, arr_p(*ys), x_ptr, arr_p(*ws), (ctypes.c_size_t * n)(*w_bytes),
         (ctypes.c_uint32 * n)(*rows), cols, stream or None))
+
+
+def ffn_dev(x_ptr: int, norm_ptr: int, gate_ptr: int, up_ptr: int, down_ptr: int, gate_bytes: int, up_bytes: int,
+            down_bytes: int, h_ptr: int, dim: int, hidden: int, eps: float, stream: int = 0) -> None:
+    """x += down(SwiGLU(gate(n), up(n))), n = RMSNorm(x) * norm, on this rank's
+    shard (forward.go:275-287; the down partials summed across the ranks after
+    tp_connect).  Device pointers; h: `hidden` floats of scratch."""
+    _err("gi_cuda_ffn_dev", load_library().gi_cuda_ffn_dev(x_ptr, norm_ptr, gate_ptr, up_ptr, down_ptr, gate_bytes,
+                                                            up_bytes, down_bytes, h_ptr, dim, hidden, eps,
+                                                            stream or None))
+
+
+def FFNBuf(x: np.ndarray, norm: Buffer, gate: Buffer, up: Buffer, down: Buffer, dim: int, hidden: int,
+           eps: float) -> None:
+    """ffn_dev with x in host memory (updated in place) and buffer weights."""
+    _err("gi_cuda_ffn_buf", load_library().gi_cuda_ffn_buf(_f32(x), _h(norm), _h(gate), _h(up), _h(down), dim,
+                                                            hidden, eps))
 
 
 def set_pdl(enable: bool) -> None:

@@ -111,18 +111,15 @@ def test_config_shapes_match_oracle(what, qt, rows, cols, ws, xs):
 @pytest.mark.parametrize("rows,cols", [(32000, 4096), (1000, 2048), (17, 8192), (3, 2048), (4100, 2048),
                                        (160, 45056)])
 def test_q6k_tensor_core_kernel_matches_oracle(rows, cols):
-    """The Q6_K GEMV on the int8 tensor cores (gi_cuda_set_q6k_mma; rows of
-    whole 2048-column groups) against DotVecQ6_K (quant.go:256-291, 542-545):
+    """The Q6_K GEMV on the int8 tensor cores (the default for rows of whole
+    2048-column groups; gi_cuda_set_q6k_mma) against DotVecQ6_K (quant.go:256-291, 542-545):
     the lm_head shape, ragged row counts and a row too long to stage."""
     raw = G.quantize_seeded(G.TYPE_Q6_K, 600 + rows, 0.02, rows, cols)
     x = seeded_x(rows + 3, cols)
     x[::131] *= 40  # activation outliers
-    G.set_q6k_mma(True)
-    try:
-        y = gpu_gemv(G.TYPE_Q6_K, raw, x, rows, cols)
-        again = gpu_gemv(G.TYPE_Q6_K, raw, x, rows, cols)
-    finally:
-        G.set_q6k_mma(False)
+    G.set_q6k_mma(True)  # the default
+    y = gpu_gemv(G.TYPE_Q6_K, raw, x, rows, cols)
+    again = gpu_gemv(G.TYPE_Q6_K, raw, x, rows, cols)
     ref = O.matmul(G.TYPE_Q6_K, x, raw, rows, cols)
     assert_parity(y, ref, what=f"q6k mma {rows}x{cols}", absdot=O.matmul_absdot(G.TYPE_Q6_K, x, raw, rows, cols))
     assert np.array_equal(y.view(np.uint32), again.view(np.uint32))
@@ -140,12 +137,12 @@ def test_q6k_tensor_core_kernel_70b_head_rows():
     buf = G.CreateBuffer(raw)
     try:
         y_mma, y_core = np.zeros(rows, np.float32), np.zeros(rows, np.float32)
-        G.set_q6k_mma(True)
+        G.MatMulBuf(G.TYPE_Q6_K, y_mma, x, buf, rows, cols)
+        G.set_q6k_mma(False)  # the CUDA-core kernel
         try:
-            G.MatMulBuf(G.TYPE_Q6_K, y_mma, x, buf, rows, cols)
+            G.MatMulBuf(G.TYPE_Q6_K, y_core, x, buf, rows, cols)
         finally:
-            G.set_q6k_mma(False)
-        G.MatMulBuf(G.TYPE_Q6_K, y_core, x, buf, rows, cols)
+            G.set_q6k_mma(True)
     finally:
         G.ReleaseBuffer(buf)
     assert_parity(y_mma, y_core.astype(np.float64), what="q6k mma vs cuda-core kernel")
@@ -367,3 +364,42 @@ def test_fused_gate_up_swiglu_matches_oracle(batch):
     finally:
         G.ReleaseBuffer(gb)
         G.ReleaseBuffer(ub)
+
+
+def ffn_oracle(x, norm, graw, uraw, draw, dim, hidden, eps):
+    """Engine.Forward's FFN half (forward.go:275-287) through the oracle."""
+    n = O.rmsnorm(x, norm, eps)
+    hb = O.swiglu(O.matmul(G.TYPE_Q4_K, n, graw, hidden, dim), O.matmul(G.TYPE_Q4_K, n, uraw, hidden, dim))
+    return (x + O.matmul(G.TYPE_Q4_K, hb, draw, dim, hidden)).astype(np.float32)
+
+
+@pytest.mark.parametrize("dim,hidden", [(4096, 11008), (512, 1280)])
+def test_ffn_block_matches_oracle(dim, hidden):
+    """gi_cuda_ffn_buf / gi_cuda_ffn_dev on one GPU: RMSNorm, gate/up, SwiGLU,
+    down and the residual add in two launches, against the oracle's steps."""
+    import torch
+    graw = G.quantize(G.TYPE_Q4_K, seeded_weights(110, hidden, dim))
+    uraw = G.quantize(G.TYPE_Q4_K, seeded_weights(111, hidden, dim))
+    draw = G.quantize(G.TYPE_Q4_K, seeded_weights(112, dim, hidden))
+    norm = (1.0 + 0.1 * seeded_x(113, dim)).astype(np.float32)
+    x0 = seeded_x(114, dim)
+    want = ffn_oracle(x0, norm, graw, uraw, draw, dim, hidden, 1e-5)
+    bufs = [G.CreateBuffer(a) for a in (norm, graw, uraw, draw)]
+    try:
+        x = x0.copy()
+        G.FFNBuf(x, *bufs, dim, hidden, 1e-5)
+        assert_parity(x, want, what=f"ffn {dim}x{hidden}")
+        dev = [torch.from_numpy(a).cuda() for a in (norm, graw, uraw, draw)]
+        xd = torch.from_numpy(x0).cuda()
+        hd = torch.empty(hidden, device="cuda")
+        G.ffn_dev(xd.data_ptr(), dev[0].data_ptr(), dev[1].data_ptr(), dev[2].data_ptr(), dev[3].data_ptr(),
+                  graw.size, uraw.size, draw.size, hd.data_ptr(), dim, hidden, 1e-5,
+                  torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert np.array_equal(xd.cpu().numpy().view(np.uint32), x.view(np.uint32))
+        with pytest.raises(G.GoInferCudaError) as e:
+            G.FFNBuf(x, bufs[0], bufs[1], bufs[2], bufs[3], dim, hidden + 100, 1e-5)
+        assert e.value.code == G.ERR_SHAPE
+    finally:
+        for b in bufs:
+            G.ReleaseBuffer(b)

@@ -67,3 +67,25 @@ def test_tp_config5_matches_oracle_golden(world, tmp_path):
         i = int(np.argmax(res["ids"] != gold["ids"]))
         pytest.fail(f"tp{world} config-5 ids differ first at step {i}: {res['ids'][i]} vs oracle {gold['ids'][i]} "
                     f"(oracle top-2 margin {gold['margins'][i]:.3e})")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_ffn_block_matches_oracle(world, tmp_path):
+    """gi_cuda_ffn_buf split over `world` GPUs (unequal hidden slices), three
+    blocks in a row: every rank ends with the same x, which matches the
+    oracle's FFN half of Engine.Forward on the whole matrices."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import goinfer_cuda as G
+    from _util import assert_parity
+    from tp_worker import FFN_SHAPE, ffn_weights
+    res = run_split(world, tmp_path, 29700 + world, ["--ffn", "--seed", "31"])
+    assert bool(res["same_on_all_ranks"])
+    dim, hidden = FFN_SHAPE
+    gate, up, down, norm, x = ffn_weights(31)
+    raws = [G.quantize(G.TYPE_Q4_K, m) for m in (gate, up, down)]
+    for k in range(3):
+        n = O.rmsnorm(x, norm, 1e-5)
+        hb = O.swiglu(O.matmul(G.TYPE_Q4_K, n, raws[0], hidden, dim), O.matmul(G.TYPE_Q4_K, n, raws[1], hidden, dim))
+        x = (x + O.matmul(G.TYPE_Q4_K, hb, raws[2], dim, hidden)).astype(np.float32)
+        assert_parity(res["xs"][k], x, what=f"tp{world} ffn block {k}")
