@@ -64,15 +64,38 @@ def test_c_program_links_and_calls_the_library(tmp_path):
     assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
 
 
-def test_integration_binding_names_declared_functions():
-    """Every C function and type INTEGRATION.md's cgo code uses is declared
-    in the header."""
+GO_BINDING = os.path.join(ROOT, "bindings", "go", "pkg", "cuda")
+
+
+def go_sources():
+    """The committed cgo binding (cuda_linux.go) and its stubs (cuda_fallback.go)."""
+    return {f: open(os.path.join(GO_BINDING, f)).read() for f in ("cuda_linux.go", "cuda_fallback.go")}
+
+
+def test_go_binding_names_declared_functions():
+    """Every C function and type the cgo binding uses is declared in the header."""
     text = open(HEADER).read()
-    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    used = set(re.findall(r"\bC\.(gi_\w+)", doc))
+    src = go_sources()["cuda_linux.go"]
+    used = set(re.findall(r"\bC\.(gi_\w+)", src))
     assert used
     for name in used:
         assert re.search(r"\b" + name + r"\b", text), name
+
+
+def test_go_fallback_covers_the_binding():
+    """cuda_fallback.go defines every exported package-level function of
+    cuda_linux.go with the same parameters (metal_fallback.go's role)."""
+    def funcs(src):
+        return {m.group(1): re.sub(r"\s+", " ", m.group(2)) for m in
+                re.finditer(r"^func ([A-Z]\w*)\(([^)]*)\)", src, flags=re.M)}
+    srcs = go_sources()
+    linux, stub = funcs(srcs["cuda_linux.go"]), funcs(srcs["cuda_fallback.go"])
+    missing = {n for n in linux if n not in stub and n not in ("AllocBuffers", "ForwardTransformer", "NewModel")}
+    assert not missing, missing
+    for n, params in stub.items():
+        assert linux.get(n) == params, (n, params, linux.get(n))
+    assert "//go:build linux && cgo && cuda" in srcs["cuda_linux.go"]
+    assert "//go:build !linux || !cgo || !cuda" in srcs["cuda_fallback.go"]
 
 
 def _split_args(text, start):
@@ -96,24 +119,24 @@ def _split_args(text, start):
     return [a for a in (x.strip() for x in args) if a]
 
 
-def test_integration_binding_argument_counts():
-    """Each C.gi_*(...) call in INTEGRATION.md's Go code passes as many
-    arguments as include/goinfer_cuda.h declares."""
+def test_go_binding_argument_counts():
+    """Each C.gi_*(...) call in the cgo binding passes as many arguments as
+    include/goinfer_cuda.h declares."""
     header = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
     decl = {}
     for m in re.finditer(r"\b(gi_\w+)\s*\(", header):
         params = _split_args(header, m.end() - 1)
         decl[m.group(1)] = 0 if params == ["void"] else len(params)
-    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    src = go_sources()["cuda_linux.go"]
     checked = 0
-    for m in re.finditer(r"\bC\.(gi_\w+)\(", doc):
+    for m in re.finditer(r"\bC\.(gi_\w+)\(", src):
         name = m.group(1)
         if name not in decl:
             continue  # a type conversion such as C.gi_cuda_buffer_t(x)
-        n = len(_split_args(doc, m.end() - 1))
-        assert n == decl[name], f"{name}: {n} arguments in INTEGRATION.md, {decl[name]} declared"
+        n = len(_split_args(src, m.end() - 1))
+        assert n == decl[name], f"{name}: {n} arguments in cuda_linux.go, {decl[name]} declared"
         checked += 1
-    assert checked >= 10
+    assert checked >= 20
 
 
 def test_row_bytes_follow_gemv_go():
