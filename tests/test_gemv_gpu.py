@@ -403,3 +403,49 @@ def test_ffn_block_matches_oracle(dim, hidden):
     finally:
         for b in bufs:
             G.ReleaseBuffer(b)
+
+
+@pytest.mark.parametrize("batch", [3, 16])
+def test_batch_mode_chained_prefill_ffn(batch):
+    """go-infer's prefill FFN inside one BeginBatch/EndBatch (forward.go:
+    607-640): gate and up into host slices, SwiGLU on them, down reading
+    the SwiGLU slice, the residual add reading the down slice -- every
+    later call reads an earlier call's output through the host slice,
+    which inside a batch still lives on the device (Metal's shared-memory
+    contract).  The outputs equal the same calls made one by one, bit for
+    bit, and the oracle's chain within the bar."""
+    dim, hidden = 512, 1280
+    graw = G.quantize(G.TYPE_Q4_K, seeded_weights(120, hidden, dim))
+    uraw = G.quantize(G.TYPE_Q4_K, seeded_weights(121, hidden, dim))
+    draw = G.quantize(G.TYPE_Q4_K, seeded_weights(122, dim, hidden))
+    bufs = [G.CreateBuffer(r) for r in (graw, uraw, draw)]
+    xs = np.random.default_rng(123).normal(size=(batch, dim)).astype(np.float32).reshape(-1)
+    xn = np.random.default_rng(124).normal(size=(batch, dim)).astype(np.float32).reshape(-1)
+
+    def chain(batched):
+        x, g, u, d = xs.copy(), np.full(batch * hidden, np.nan, np.float32), \
+            np.full(batch * hidden, np.nan, np.float32), np.full(batch * dim, np.nan, np.float32)
+        if batched:
+            G.BeginBatch()
+        G.MatMulBatchBuf(G.TYPE_Q4_K, g, xn, bufs[0], batch, hidden, dim)
+        G.MatMulBatchBuf(G.TYPE_Q4_K, u, xn, bufs[1], batch, hidden, dim)
+        G.SwiGLU(g, u, batch * hidden)
+        G.MatMulBatchBuf(G.TYPE_Q4_K, d, g, bufs[2], batch, dim, hidden)
+        G.AddResidual(x, d, batch * dim)
+        if batched:
+            G.EndBatch()
+        return x, g, d
+
+    try:
+        plain = chain(False)
+        batched = chain(True)
+    finally:
+        for b in bufs:
+            G.ReleaseBuffer(b)
+    for a, b in zip(plain, batched):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    for t in range(batch):
+        n = xn[t * dim:(t + 1) * dim]
+        h = O.swiglu(O.matmul(G.TYPE_Q4_K, n, graw, hidden, dim), O.matmul(G.TYPE_Q4_K, n, uraw, hidden, dim))
+        want = (xs[t * dim:(t + 1) * dim] + O.matmul(G.TYPE_Q4_K, h, draw, dim, hidden)).astype(np.float32)
+        assert_parity(batched[0][t * dim:(t + 1) * dim], want, what=f"batched chain token {t}")
