@@ -12,6 +12,7 @@ generated token.
     python go-infer_b200/run.py decode --gguf model.gguf --prompt 16 --steps 32
     python go-infer_b200/run.py export --model llama2-7b --layers 2 --out small.gguf
     python go-infer_b200/run.py prefill --type q4_k --rows 4096 --cols 4096 --batch 512 --reps 3
+    python go-infer_b200/run.py gemv --type q6_k --rows 32000 --cols 4096 --reps 20
 """
 from __future__ import annotations
 
@@ -96,6 +97,43 @@ def prefill(args) -> None:
         G.ReleaseBuffer(wb)
 
 
+def gemv(args) -> None:
+    """Decode GEMVs y = W x of one shape, rotating over enough weight copies
+    that every launch streams its matrix from HBM (> 2 x the 126 MB L2)."""
+    import torch
+    qt = TYPES[args.type]
+    nbytes = args.rows * G.row_bytes(qt, args.cols)
+    ncopy = max(1, -(-252_000_000 // nbytes))
+    bufs = [G.synth_buffer(qt, args.seed + c, 0.02, args.rows, args.cols) for c in range(ncopy)]
+    x = torch.randn(args.cols, device="cuda")
+    y = torch.empty(args.rows, device="cuda")
+    st = torch.cuda.Stream()
+    G.set_q6k_mma(not args.cuda_cores)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def run(i):
+        b = bufs[i % ncopy]
+        G.gemv_dev(qt, y.data_ptr(), x.data_ptr(), b.device_ptr, b.nbytes, args.rows, args.cols, st.cuda_stream)
+
+    try:
+        for i in range(3):
+            run(i)
+        st.synchronize()
+        with torch.cuda.stream(st):
+            e0.record()
+            for i in range(args.reps):
+                run(i)
+            e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.reps
+        print(f"gemv {args.type} {args.rows}x{args.cols}: {us:.2f} us per launch "
+              f"({(nbytes + 4 * (args.rows + args.cols)) / us / 1e3:.1f} GB/s, {ncopy} weight copies)")
+    finally:
+        G.set_q6k_mma(True)
+        for b in bufs:
+            G.ReleaseBuffer(b)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -119,6 +157,13 @@ def main() -> None:
     p.add_argument("--batch", type=int, default=512)
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--seed", type=int, default=8)
+    v = sub.add_parser("gemv")
+    v.add_argument("--type", choices=sorted(TYPES), default="q4_k")
+    v.add_argument("--rows", type=int, default=11008)
+    v.add_argument("--cols", type=int, default=4096)
+    v.add_argument("--reps", type=int, default=20)
+    v.add_argument("--seed", type=int, default=20)
+    v.add_argument("--cuda-cores", action="store_true", help="Q6_K on the CUDA-core kernel")
     args = ap.parse_args()
     if args.cmd == "export":  # host only
         export(args)
@@ -126,7 +171,7 @@ def main() -> None:
     G.Init(0)
     if not G.IsAvailable():
         raise SystemExit("libgoinfer_cuda: no CUDA device")
-    (decode if args.cmd == "decode" else prefill)(args)
+    {"decode": decode, "prefill": prefill, "gemv": gemv}[args.cmd](args)
 
 
 if __name__ == "__main__":
