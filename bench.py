@@ -390,7 +390,7 @@ def decode_section(args, world, rank, local, pg):
     st = torch.cuda.Stream()
     pre = {}
     for name, qt, rows, seed in (("q4k_4096", G.TYPE_Q4_K, 4096, 8), ("q4k_11008", G.TYPE_Q4_K, 11008, 9),
-                                 ("q6k_32000", G.TYPE_Q6_K, 32000, 10)):
+                                 ("q6k_32000", G.TYPE_Q6_K, 32000, 10), ("q8_0_4096", G.TYPE_Q8_0, 4096, 1)):
         wb = G.synth_buffer(qt, seed, 0.02, rows, 4096)
         y = torch.empty(512, rows, device=dev)
         run = lambda: G.gemm_dev(qt, y.data_ptr(), x.data_ptr(), wb.device_ptr, wb.nbytes, 512, rows, 4096,

@@ -10,8 +10,8 @@
 
 namespace gi {
 
-// Batches at least this large take the tensor-core path (Q4_K, Q6_K);
-// smaller ones, and Q8_0, run one decode GEMV per token.
+// Batches at least this large take the tensor-core path (Q4_K, Q6_K, Q8_0);
+// smaller ones run one decode GEMV per token.
 constexpr int64_t kGemmTcMinBatch = 16;
 
 // Device workspace of the tensor-core path: the activations staged as fp16
@@ -38,7 +38,7 @@ int gemm_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
 bool gemm_tc_supported(int qtype, int64_t batch, int64_t rows, int64_t cols);
 size_t gemm_tc_workspace(int64_t batch, int64_t cols);
 int gemm_tc_prepare_device();
-// x 16-byte aligned; Q4_K weights 16-byte aligned, Q6_K 2-byte aligned.
+// x 16-byte aligned; Q4_K weights 16-byte aligned, Q6_K and Q8_0 2-byte aligned.
 int gemm_tc_launch(int qtype, float* y, const float* x, const void* w, int64_t batch, int64_t rows,
                    int64_t cols, const GemmWorkspace& ws, int* error, cudaStream_t stream);
 

@@ -15,6 +15,11 @@
 //    the integer mins against the sub-block sums.  A Q6_K weight is
 //    d*sc*(q6-32) (quant.go:256-291); sc*q can need 12 bits, so its A
 //    operand is the pair fp16(sc*q) + (sc*q - fp16(sc*q)), both exact.
+//    A Q8_0 weight is d*q (quant.go:196-212, 32-element blocks): d*q needs
+//    19 bits, so its A operand is an exact hi/lo pair too, with each block's
+//    d folded in and scaled by a power of two per super-block of 256
+//    columns (largest d of the 8 blocks -> [64, 128)) that the epilogue
+//    divides out.
 //  * Activations.  Each token row is scaled by a power of two (its largest
 //    magnitude lands below 2^10) and split into fp16 hi + lo, 22 bits of
 //    mantissa.  The staging kernel writes both halves once per call.
@@ -76,6 +81,16 @@ struct Cfg<kTypeQ6_K> {
   static constexpr int kACol = 256;
   static constexpr int kAStageCols = 64;  // hi part, then lo part
   static constexpr int kPrefetch = 2;
+};
+template <>
+struct Cfg<kTypeQ8_0> {  // the Q6_K pipeline: hi and lo weight parts, no min term
+  static constexpr int kStages = 4;
+  static constexpr bool kMins = false;
+  static constexpr int kStageBytes = 2 * kTileBytes;  // B hi, B lo
+  static constexpr int kD2Col = 0;
+  static constexpr int kACol = 256;
+  static constexpr int kAStageCols = 64;  // hi part, then lo part
+  static constexpr int kPrefetch = 3;
 };
 constexpr int kTmemCols = 512;
 
@@ -387,6 +402,87 @@ GI_DEVINL void q6k_decode(const Q6kRaw& r, int chunk, uint32_t (&hi)[32], uint32
   }
 }
 
+// Q8_0 chunk c (64 elements) of a row = blocks 2c and 2c+1: fp16 d at bytes
+// 0 and 34, int8 quants at 2..33 and 36..67 (quant.go:37-41).  Word u of
+// the operand fills unit u in the Q4_K K order, elements 4u.. of block 2c
+// in its low half and 4u.. of block 2c+1 in its high half.  Blocks are
+// 2-byte aligned: the 68 bytes are read as aligned words (the last two
+// bytes by a 16-bit load when misaligned, so no read passes the chunk)
+// and realigned with a funnel shift.  The first chunk of each 256-column
+// super-block also carries the super-block's eight d, from which the
+// decode and the epilogue derive the same power of two.
+struct Q80Raw {
+  uint32_t w[18];
+  uint32_t shift;  // 0 or 16
+  uint32_t dd[4];  // chunk & 3 == 0: the super-block's 8 fp16 d
+};
+
+GI_DEVINL void q80_load_d(uint32_t (&dd)[4], const uint8_t* wrow, int sb) {
+  const uint8_t* p = wrow + (size_t)sb * 272;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) dd[k] = ldg_nc16(p + 68 * k) | (ldg_nc16(p + 68 * k + 34) << 16);
+}
+
+// 2^E with (largest |d| of the 8) * 2^E in [64, 128) (1 for an all-zero
+// super-block): fp16 d * 2^E times an int8 quant is then an fp16 hi part
+// below 2^14 plus an exact fp16 residual.
+GI_DEVINL float q80_sb_scale(const uint32_t (&dd)[4]) {
+  uint32_t m = 0;  // fp16 magnitudes order as unsigned integers
+#pragma unroll
+  for (int k = 0; k < 4; ++k) m = max(m, max(dd[k] & 0x7FFFu, (dd[k] >> 16) & 0x7FFFu));
+  const float f = __half2float(__ushort_as_half((unsigned short)m));
+  if (!(f > 0.f) || f > 65504.f) return 1.f;
+  return exp2i(6 - ilogbf(f));
+}
+
+GI_DEVINL void q80_load(Q80Raw& r, const uint8_t* wrow, int chunk, bool valid) {
+  if (!valid) {
+#pragma unroll
+    for (int i = 0; i < 18; ++i) r.w[i] = 0;
+    r.dd[0] = r.dd[1] = r.dd[2] = r.dd[3] = 0;
+    r.shift = 0;
+    return;
+  }
+  const uint8_t* blk = wrow + (size_t)chunk * 68;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
+  r.shift = (uint32_t)(a & 3) * 8;
+  const uint8_t* base = reinterpret_cast<const uint8_t*>(a & ~(uintptr_t)3);
+#pragma unroll
+  for (int i = 0; i < 17; ++i) r.w[i] = ldg_nc32(base + 4 * i);
+  r.w[17] = r.shift ? ldg_nc16(blk + 66) : 0u;
+  if ((chunk & 3) == 0) q80_load_d(r.dd, wrow, chunk >> 2);
+}
+
+// hi = fp16(q * d), lo = q * d - hi (exact) for the quant pairs of units u.
+GI_DEVINL void q80_decode(const Q80Raw& r, float scale, uint32_t (&hi)[32], uint32_t (&lo)[32]) {
+  uint32_t W[17];
+#pragma unroll
+  for (int k = 0; k < 17; ++k) W[k] = __funnelshift_r(r.w[k], r.w[k + 1], r.shift);
+  const uint32_t s0 = h2_splat(__half2float(__ushort_as_half((unsigned short)(W[0] & 0xFFFFu))) * scale);
+  const uint32_t s1 = h2_splat(__half2float(__ushort_as_half((unsigned short)(W[8] >> 16))) * scale);
+  const uint32_t k1152 = 0x64806480u, sign = 0x80008000u, mag = 0x64646464u;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    // quants as unsigned bytes (q + 128), two to an fp16 pair as 1024 + q + 128
+    const uint32_t qa = __funnelshift_r(W[u], W[u + 1], 16) ^ 0x80808080u;  // block 2c, 4u..4u+3
+    const uint32_t qb = W[9 + u] ^ 0x80808080u;                             // block 2c+1, 4u..4u+3
+    const uint32_t v0 = hsub2_u32(prmt(qa, mag, 0x4240u), k1152);  // (4u, 4u+2)
+    const uint32_t v1 = hsub2_u32(prmt(qa, mag, 0x4341u), k1152);  // (4u+1, 4u+3)
+    const uint32_t v2 = hsub2_u32(prmt(qb, mag, 0x4240u), k1152);
+    const uint32_t v3 = hsub2_u32(prmt(qb, mag, 0x4341u), k1152);
+    const uint32_t h0 = hmul2_u32(v0, s0), h1 = hmul2_u32(v1, s0);
+    const uint32_t h2 = hmul2_u32(v2, s1), h3 = hmul2_u32(v3, s1);
+    hi[4 * u + 0] = h0;
+    hi[4 * u + 1] = h1;
+    hi[4 * u + 2] = h2;
+    hi[4 * u + 3] = h3;
+    lo[4 * u + 0] = hfma2_u32(v0, s0, h0 ^ sign);
+    lo[4 * u + 1] = hfma2_u32(v1, s0, h1 ^ sign);
+    lo[4 * u + 2] = hfma2_u32(v2, s1, h2 ^ sign);
+    lo[4 * u + 3] = hfma2_u32(v3, s1, h3 ^ sign);
+  }
+}
+
 // ---- the prefill kernel -----------------------------------------------------------
 
 struct Params {
@@ -543,13 +639,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint8_t* wrow = P.w + (size_t)(valid ? row0 + r : 0) * P.rowb;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + C::kACol;
     constexpr int R = C::kPrefetch;
-    using Raw = typename std::conditional<QT == kTypeQ4_K, Q4kRaw, Q6kRaw>::type;
+    using Raw = typename std::conditional<QT == kTypeQ4_K, Q4kRaw,
+                                          typename std::conditional<QT == kTypeQ6_K, Q6kRaw, Q80Raw>::type>::type;
+    float q80_scale = 1.f;  // Q8_0: the current super-block's power of two
     Raw ring[R];
 #pragma unroll
     for (int j = 0; j < R; ++j) {
       if (j < nchunk) {
         if constexpr (QT == kTypeQ4_K) q4k_load(ring[j], wrow, j, valid);
-        else q6k_load(ring[j], wrow, j, valid);
+        else if constexpr (QT == kTypeQ6_K) q6k_load(ring[j], wrow, j, valid);
+        else q80_load(ring[j], wrow, j, valid);
       }
     }
     bool ok = true;
@@ -574,7 +673,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             } else {
               uint32_t hi[32], lo[32];
-              q6k_decode(ring[j], i, hi, lo);
+              if constexpr (QT == kTypeQ6_K) {
+                q6k_decode(ring[j], i, hi, lo);
+              } else {
+                if ((i & 3) == 0) q80_scale = q80_sb_scale(ring[j].dd);
+                q80_decode(ring[j], q80_scale, hi, lo);
+              }
               tmem_st32(col, hi);
               tmem_st32(col + 32, lo);
             }
@@ -584,7 +688,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(prod_full(s));
             if (i + R < nchunk) {
               if constexpr (QT == kTypeQ4_K) q4k_load(ring[j], wrow, i + R, valid);
-              else q6k_load(ring[j], wrow, i + R, valid);
+              else if constexpr (QT == kTypeQ6_K) q6k_load(ring[j], wrow, i + R, valid);
+              else q80_load(ring[j], wrow, i + R, valid);
             }
           }
         }
@@ -603,11 +708,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     float acc[kTileTok];
 #pragma unroll
     for (int t = 0; t < kTileTok; ++t) acc[t] = 0.f;
-    // d (and dmin) of the row's super-block as an fp16 pair.
+    // d (and dmin) of the row's super-block as an fp16 pair; Q8_0: the
+    // float bits of 2^-E, the super-block's power of two divided out.
     auto load_scale = [&](int sb) -> uint32_t {
       if (!valid) return 0u;
-      if constexpr (QT == kTypeQ4_K) return ldg_nc32(wrow + (size_t)sb * 144);
-      else return ldg_nc16(wrow + (size_t)sb * 210 + 208);
+      if constexpr (QT == kTypeQ4_K) {
+        return ldg_nc32(wrow + (size_t)sb * 144);
+      } else if constexpr (QT == kTypeQ6_K) {
+        return ldg_nc16(wrow + (size_t)sb * 210 + 208);
+      } else {
+        uint32_t dd[4];
+        q80_load_d(dd, wrow, sb);
+        return __float_as_uint(1.f / q80_sb_scale(dd));
+      }
     };
     uint32_t dd = load_scale(0);
     bool ok = true;
@@ -632,7 +745,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(d2_empty);
       }
-      const float d = h_lo(dd);
+      float d;
+      if constexpr (QT == kTypeQ8_0) d = __uint_as_float(dd);
+      else d = h_lo(dd);
       const uint32_t col = lane_base + b * 128;
 #pragma unroll
       for (int cc = 0; cc < kTileTok / 16; ++cc) {
@@ -714,7 +829,7 @@ __global__ void __launch_bounds__(256) stage_tokens_kernel(const float* __restri
     const int chunk = g >> 3, u = g & 7;
     const int sb = chunk >> 2, c = chunk & 3;
     int lo_base, hi_off;
-    if (QT == kTypeQ4_K) {
+    if (QT != kTypeQ6_K) {  // Q4_K and Q8_0: chunk c = elements 64c .. 64c + 63
       lo_base = sb * 256 + 64 * c;
       hi_off = 32;
     } else {
@@ -808,7 +923,8 @@ int launch_typed(float* y, const float* x, const void* w, int64_t batch, int64_t
 
 bool gemm_tc_supported(int qtype, int64_t batch, int64_t rows, int64_t cols) {
   (void)rows;
-  return (qtype == kTypeQ4_K || qtype == kTypeQ6_K) && batch >= kGemmTcMinBatch && cols % 256 == 0 &&
+  return (qtype == kTypeQ4_K || qtype == kTypeQ6_K || qtype == kTypeQ8_0) && batch >= kGemmTcMinBatch &&
+         cols % 256 == 0 &&
          batch <= 65535 * (int64_t)tc::kTileTok && cols <= (int64_t)1 << 24;
 }
 
@@ -820,6 +936,9 @@ int gemm_tc_prepare_device() {
     return -5;
   if (cudaFuncSetAttribute(tc::prefill_kernel<kTypeQ6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            tc::smem_bytes<kTypeQ6_K>()) != cudaSuccess)
+    return -5;
+  if (cudaFuncSetAttribute(tc::prefill_kernel<kTypeQ8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::smem_bytes<kTypeQ8_0>()) != cudaSuccess)
     return -5;
   return 0;
 }
@@ -833,6 +952,7 @@ int gemm_tc_launch(int qtype, float* y, const float* x, const void* w, int64_t b
     return tc::launch_typed<kTypeQ4_K>(y, x, w, batch, rows, cols, ws, error, stream);
   }
   if (reinterpret_cast<uintptr_t>(w) % 2) return -4;
+  if (qtype == kTypeQ8_0) return tc::launch_typed<kTypeQ8_0>(y, x, w, batch, rows, cols, ws, error, stream);
   return tc::launch_typed<kTypeQ6_K>(y, x, w, batch, rows, cols, ws, error, stream);
 }
 

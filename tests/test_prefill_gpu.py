@@ -1,5 +1,5 @@
-"""GPU parity of the tensor-core prefill dequant-GEMM (Q4_K, Q6_K; batches of
-at least 16 tokens) against the CPU oracle, through the C ABI.
+"""GPU parity of the tensor-core prefill dequant-GEMM (Q4_K, Q6_K, Q8_0;
+batches of at least 16 tokens) against the CPU oracle, through the C ABI.
 
 The oracle is the restatement of go-infer's per-token prefill semantics
 (MatMulBatch declining, pkg/engine/forward.go:482-495: one GEMVEngine.MatMul
@@ -68,7 +68,7 @@ def check_against_oracle(qt, raw, x, y, rows, cols, what):
     assert gpu_dev <= 4 * ref_dev + 1e-6 * scale, f"{what}: |gpu-exact| {gpu_dev:.3e} vs |ref-exact| {ref_dev:.3e}"
 
 
-@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K])
+@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
 @pytest.mark.parametrize("batch,rows,cols", [
     (16, 128, 256),     # one tile, one super-block
     (17, 130, 512),     # ragged tokens and rows
@@ -83,7 +83,7 @@ def test_tc_shapes_match_oracle(qt, batch, rows, cols):
     check_against_oracle(qt, raw, x, y, rows, cols, f"tc {qt} {batch}x{rows}x{cols}")
 
 
-@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K])
+@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
 def test_tc_threshold_agrees_with_per_token_path(qt):
     """batch 15 runs per token, batch 16 on the tensor cores: same answers."""
     rows, cols = 96, 768
@@ -112,11 +112,23 @@ def random_q6k_blocks(rng, rows, nsb):
     return raw.reshape(-1)
 
 
-@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K])
+def random_q80_blocks(rng, rows, nsb):
+    """Random int8 quants; fp16 scales spread over six decades, so blocks of
+    one 256-column group carry very different d (the kernel folds d into the
+    weight operand under one power of two per group)."""
+    raw = rng.integers(0, 256, size=(rows, nsb * 8, 34), dtype=np.uint8)
+    d = (10.0 ** rng.uniform(-7, -1, size=(rows, nsb * 8))).astype(np.float16)
+    d[:, ::5] = 0  # some all-zero blocks
+    raw[:, :, 0:2] = d.view(np.uint8).reshape(rows, nsb * 8, 2)
+    return raw.reshape(-1)
+
+
+@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
 def test_tc_random_raw_blocks(qt):
     rng = np.random.default_rng(44)
     batch, rows, cols = 48, 160, 1536
-    raw = (random_q4k_blocks if qt == G.TYPE_Q4_K else random_q6k_blocks)(rng, rows, cols // 256)
+    make = {G.TYPE_Q4_K: random_q4k_blocks, G.TYPE_Q6_K: random_q6k_blocks, G.TYPE_Q8_0: random_q80_blocks}[qt]
+    raw = make(rng, rows, cols // 256)
     x = rng.normal(size=(batch, cols)).astype(np.float32)
     y = gpu_gemm(qt, raw, x, batch, rows, cols)
     check_against_oracle(qt, raw, x, y, rows, cols, f"raw blocks {qt}")
@@ -146,7 +158,7 @@ def test_tc_q6k_extreme_products():
     check_against_oracle(G.TYPE_Q6_K, raw, x, y, rows, cols, "q6k extreme products")
 
 
-@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K])
+@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
 def test_tc_activation_scaling_extremes(qt):
     """Per-token power-of-two scaling: tiny, huge and mixed-magnitude rows."""
     rows, cols, batch = 128, 1024, 24
@@ -166,7 +178,8 @@ def test_tc_activation_scaling_extremes(qt):
 
 
 @pytest.mark.parametrize("qt,rows,seed", [
-    (G.TYPE_Q4_K, 4096, 8), (G.TYPE_Q4_K, 11008, 9), (G.TYPE_Q6_K, 32000, 10)])
+    (G.TYPE_Q4_K, 4096, 8), (G.TYPE_Q4_K, 11008, 9), (G.TYPE_Q6_K, 32000, 10),
+    (G.TYPE_Q8_0, 4096, 1)])  # config 1's Q8_0 matrix as a 512-token prefill
 def test_tc_config3_shapes(qt, rows, seed):
     """Config 3: X 512 x 4096 ~ N(0,1) (seed 7), W ~ N(0, 0.02) quantised."""
     batch, cols = 512, 4096
