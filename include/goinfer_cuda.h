@@ -140,9 +140,9 @@ int gi_cuda_gemm_dev(int quant_type, float* y, const float* x, const void* w, si
  * The prefill workspace is a fixed 16 MiB device array inside the library
  * instead of memory grown at call time, so a call never allocates or
  * synchronises the device.  Limit: the staged activations of the call must
- * fit: 4 bytes (Q6_K) or 4.125 bytes (Q4_K) per column per token, tokens
- * rounded up to a multiple of 128; 512 tokens x 4096 columns fit.  Larger
- * calls return GI_ERR_SHAPE (batches under 16 and Q8_0 need no scratch).  The first call on a device looks up the array's
+ * fit: about 4.1 bytes per column per token, tokens rounded up to a
+ * multiple of 128; 512 tokens x 4096 columns fit.  Larger calls return
+ * GI_ERR_SHAPE (batches under 16 need no scratch).  The first call on a device looks up the array's
  * address (make it before any stream capture); the array is shared by all
  * calls on the device, so calls that overlap in time race on it. */
 int gi_cuda_gemm_dev_noalloc(int quant_type, float* y, const float* x, const void* w, size_t w_bytes,
