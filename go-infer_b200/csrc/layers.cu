@@ -55,17 +55,28 @@ GI_DEVINL uint32_t ld_acquire_gpu(const unsigned* p) {
   return v;
 }
 
-// Grid-wide barrier: the counter at `bar` (zero at launch) reaches `target`
-// = (barrier number) x (CTAs).  All writes of the CTA before it are visible
-// to every CTA after it (fence, release add, acquire poll, fence).  False
-// when it gave up: after 2 s, or soon after another wait set the error word
-// (read every 256 polls: mapped host memory, a PCIe round trip).
-GI_DEVINL bool grid_sync(unsigned* bar, unsigned target, int* error, int* flag) {
+// Grid-wide barrier in two halves: the counter at `bar` (zero at launch)
+// reaches `target` = (barrier number) x (CTAs).  All writes of the CTA
+// before grid_arrive are visible to every CTA after its grid_wait (fence,
+// add; acquire poll, fence).  The halves are split so that a CTA can
+// request its next projection's weights in between: a fence issued after
+// those cp.async requests waits for them (measured: the barrier released
+// 4-5 us after the last CTA arrived, against ~1 us when nothing was in
+// flight).  grid_wait is false when it gave up: after 2 s, or soon after
+// another wait set the error word (read every 256 polls: mapped host
+// memory, a PCIe round trip).
+GI_DEVINL void grid_arrive(unsigned* bar) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(bar, 1u);
+  }
+}
+
+GI_DEVINL bool grid_wait(unsigned* bar, unsigned target, int* error, int* flag) {
   __syncthreads();
   if (threadIdx.x == 0) {
     int ok = 1;
-    __threadfence();
-    atomicAdd(bar, 1u);
     if (ld_acquire_gpu(bar) < target) {
       const uint64_t t0 = now_ns();
       for (uint32_t i = 1;; ++i) {
@@ -83,7 +94,10 @@ GI_DEVINL bool grid_sync(unsigned* bar, unsigned target, int* error, int* flag) 
         }
       }
     }
-    __threadfence();
+    // No trailing fence: the acquire load above orders this thread after
+    // every arriving CTA's release (fence + add), and the CTA barrier below
+    // orders the other threads after it; a fence here would also wait for
+    // the weight requests issued since grid_arrive.
     *flag = ok;
   }
   __syncthreads();
@@ -321,9 +335,14 @@ __global__ void __launch_bounds__(kLThreads, 1) layers_kernel(const LayersCfg a,
   const int c = blockIdx.x;
   const unsigned nct = gridDim.x;
   unsigned nbar = 0;
-  auto sync = [&]() {
+  auto arrive = [&]() {
     ++nbar;
-    return grid_sync(a.bar, nbar * nct, a.error, flag);
+    grid_arrive(a.bar);
+  };
+  auto wait = [&]() { return grid_wait(a.bar, nbar * nct, a.error, flag); };
+  auto sync = [&]() {
+    arrive();
+    return wait();
   };
   GemvPhase<kLW, S> G;
   G.init();
@@ -340,11 +359,12 @@ __global__ void __launch_bounds__(kLThreads, 1) layers_kernel(const LayersCfg a,
   const int items = a.n_kv_heads * a.splits, nph = 4 * a.n_layers;
   for (int k = 0; k < nph; ++k) {
     G.run(*p, smem);
+    arrive();
     if (k + 1 < nph) {
       load_params(p, d.ph + k + 1);
-      G.begin(*p, smem, c);  // the next projection's first units, before the barrier
+      G.begin(*p, smem, c);  // the next projection's first units, while the barrier completes
     }
-    if (!sync()) break;
+    if (!wait()) break;
     if ((k & 3) == 0) {
       const int l = k >> 2;
       float* kc = a.kcache + (size_t)l * a.layer_kv;
