@@ -424,19 +424,23 @@ def cpu_model() -> str:
     return platform.processor() or "unknown"
 
 
-def step_distribution(capture, steps_per_replay=100, replays=20):
+def step_distribution(capture, steps_per_replay=100, replays=20, pg=None, dev=None):
     """Spread of the step time, outside the timed region: `replays` replays
     of a graph of `steps_per_replay` steps, each timed with CUDA events on
-    the launching stream (this rank).  An optional statistic: a failure is
-    reported in the line, never raised."""
+    the launching stream (this rank).  With several ranks each replay's
+    start event follows a one-element all-reduce, as in time_graph.  An
+    optional statistic: a failure is reported in the line, never raised."""
     import torch
     try:
         g = capture(steps_per_replay)
         g.replay()
         torch.cuda.synchronize()
+        rendezvous = torch.zeros(1, device=dev) if pg else None
         per_step = []
         for _ in range(replays):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if pg:
+                pg.all_reduce(rendezvous)
             a.record()
             g.replay()
             b.record()
@@ -588,7 +592,7 @@ def run_ours(args):
     launch_ms = ms / (2 * args.steps)  # this rank's average Q4_K GEMV launch
     achieved = launch_bytes / (launch_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
-    dist = step_distribution(capture)
+    dist = step_distribution(capture, pg=pg, dev=dev)
     ffn_block = None
     if world == 1:  # the FFN block at N=1: the reference point of the N>1 lines
         f_ms, _f, _c = time_graph(capture_ffn, args.steps, args.warmup, None, local, dev)
