@@ -18,7 +18,7 @@ a changed generator).  The weights come from gi_quantize_seeded, whose bytes
 gi_synth_weights reproduces on the GPU, so the GPU tests draw the same model
 on the device.  Run from the repository root:
     python tests/golden/make_decode_golden.py 7b    (a few minutes on 8 cores)
-    python tests/golden/make_decode_golden.py 70b   (about 1.5 hours on 8
+    python tests/golden/make_decode_golden.py 70b   (about 2.3 hours on 8
                                                       cores, 40 GB of memory)"""
 import hashlib
 import os
