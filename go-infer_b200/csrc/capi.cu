@@ -1169,6 +1169,12 @@ int gi_cuda_set_q6k_mma(int enable) {
   return 0;
 }
 
+int gi_cuda_set_prefill_pair(int enable) {
+  std::lock_guard<std::mutex> lk(g.mu);
+  gi::gemm_tc_set_pair(enable != 0);
+  return 0;
+}
+
 const char* gi_cuda_last_error(void) { return t_err.c_str(); }
 
 int64_t gi_quant_row_bytes(int quant_type, int64_t cols) { return gi::row_bytes(quant_type, cols); }

@@ -38,6 +38,7 @@ int gemm_launch(int qtype, float* y, const float* x, const void* w, size_t w_byt
 bool gemm_tc_supported(int qtype, int64_t batch, int64_t rows, int64_t cols);
 size_t gemm_tc_workspace(int64_t batch, int64_t cols);
 int gemm_tc_prepare_device();
+void gemm_tc_set_pair(bool on);  // CTA pairs (default) or single CTAs
 // x 16-byte aligned; Q4_K weights 16-byte aligned, Q6_K and Q8_0 2-byte aligned.
 int gemm_tc_launch(int qtype, float* y, const float* x, const void* w, int64_t batch, int64_t rows,
                    int64_t cols, const GemmWorkspace& ws, int* error, cudaStream_t stream);

@@ -41,6 +41,20 @@
 //   warps 6-9   epilogue: TMEM -> registers, d/dmin scaling, y stores
 // Every wait is bounded in time; on expiry the kernel sets *error, drains its
 // own copies and MMAs, frees tensor memory and returns.
+//
+// CTA pairs (opt-in, gi_cuda_set_prefill_pair): two CTAs of a cluster own
+// consecutive 128-row weight tiles of the same token tile, and rank 0
+// issues 256-row cta_group::2 MMAs over both.  Each CTA still decodes its
+// own rows into its own tensor memory and reads back its own accumulators,
+// but copies only its 64-token half of every activation tile: the
+// activation traffic from L2 (every 128-row weight tile re-reads the whole
+// activation) halves.  No copy reads another CTA's shared memory; the
+// tensor core reads both halves.  Measured on B200 the pairs are slower:
+// the MMA issuer of a single CTA waits little on its activation copies
+// (~3 us per launch), while a pair's decoded-weight hand-off (multicast
+// commit to the other CTA, its decode, a remote arrive back) outlasts the
+// 4-stage pipeline (~33 us of waiting per launch), so single CTAs are the
+// default.
 #include <type_traits>
 
 #include "common.cuh"
@@ -94,9 +108,17 @@ struct Cfg<kTypeQ8_0> {  // the Q6_K pipeline: hi and lo weight parts, no min te
 };
 constexpr int kTmemCols = 512;
 
-template <int QT>
+// Bytes of one pipeline stage in shared memory.  A CTA of a pair holds only
+// its 64-token half of the activation tiles and of the sub-block sums (the
+// mins tile keeps all 128 rows of its own weight tile).
+template <int QT, bool P2>
+constexpr int stage_bytes() {
+  return P2 ? Cfg<QT>::kStageBytes / 2 + (Cfg<QT>::kMins ? kSmallBytes / 2 : 0) : Cfg<QT>::kStageBytes;
+}
+
+template <int QT, bool P2 = false>
 constexpr int smem_bytes() {
-  return Cfg<QT>::kStages * Cfg<QT>::kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
+  return Cfg<QT>::kStages * stage_bytes<QT, P2>() + 1024 /* alignment */ + 256 /* barriers */;
 }
 
 // ---- tcgen05 / TMA / timer primitives ---------------------------------------
@@ -107,22 +129,39 @@ GI_DEVINL uint64_t globaltimer_ns() {
   return t;
 }
 
-// Wait for the phase of `parity` on an mbarrier, giving up after kWaitNs.
+// mbarrier test with acquire at cluster scope: for barriers that the other
+// CTA of a pair arrives on.
+GI_DEVINL bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; "
+      "selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase of `parity` on an mbarrier, giving up after kWaitNs
+// (CL: acquire at cluster scope).
+template <bool CL = false>
 GI_DEVINL bool wait_phase(uint32_t bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto test = [&]() { return CL ? mbar_try_wait_cl(bar, parity) : mbar_try_wait(bar, parity); };
+  if (test()) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+      if (test()) return true;
     if (globaltimer_ns() - t0 > kWaitNs) return false;
   }
 }
 
 // The same for a whole warp: lane 0 polls, every lane gets the outcome, and
 // the warp leaves converged (the tcgen05 .sync.aligned forms require it).
+template <bool CL = false>
 GI_DEVINL bool warp_wait_phase(uint32_t bar, uint32_t parity) {
   int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = wait_phase(bar, parity);
+  if ((threadIdx.x & 31) == 0) ok = wait_phase<CL>(bar, parity);
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
@@ -181,6 +220,62 @@ GI_DEVINL void mma_commit(uint32_t bar) {
                : "memory");
 }
 
+// ---- CTA-pair (cta_group::2) forms ------------------------------------------
+// The pair is a cluster of two CTAs; rank 0 issues the MMAs for both.  A
+// 256-row MMA reads rows 0-127 of A from rank 0's tensor memory and rows
+// 128-255 from rank 1's, tokens 0-63 of B from rank 0's shared memory and
+// 64-127 from rank 1's (the same offsets in both), and writes each CTA's
+// rows of D into its own tensor memory.
+
+GI_DEVINL uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of shared-memory offset `addr` in CTA `rank`.
+GI_DEVINL uint32_t peer_addr(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier of either CTA of the pair (release at cluster scope).
+GI_DEVINL void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Both CTAs of the cluster, every thread: release then acquire.
+GI_DEVINL void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+GI_DEVINL void mma_f16_2(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+GI_DEVINL void mma_f16_ts_2(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on `bar` (the same offset) in both CTAs of the pair when every
+// pair MMA this thread issued so far has finished.
+GI_DEVINL void mma_commit_2(uint32_t bar) {
+  const uint16_t both = 3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(both)
+      : "memory");
+}
+
 // 32 lanes x 16 columns of fp32 from tensor memory, waited for in place
 // (the wait names the registers, so no use can be scheduled before it).
 GI_DEVINL void tmem_ld16(uint32_t taddr, float (&v)[16]) {
@@ -212,8 +307,10 @@ GI_DEVINL uint64_t desc_plain(uint32_t addr, uint32_t lbo, uint32_t sbo) {
          ((uint64_t)1 << 46);
 }
 
-// Instruction descriptor: fp32 D, fp16 A and B, both K-major, M=128, N=128.
+// Instruction descriptor: fp32 D, fp16 A and B, both K-major, M=128, N=128;
+// for a CTA pair M=256 (128 rows in each CTA).
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kTileTok >> 3) << 17) | ((uint32_t)(kTileRows >> 4) << 24);
+constexpr uint32_t kIdesc2 = (1u << 4) | ((uint32_t)(kTileTok >> 3) << 17) | ((uint32_t)(2 * kTileRows >> 4) << 24);
 
 GI_DEVINL void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
@@ -496,15 +593,26 @@ struct Params {
   int* error;
 };
 
-template <int QT>
+// P2: the kernel runs as CTA pairs (clusters of two along the weight-row
+// tiles: the grid is (row tiles, token tiles), blockIdx.x = 2p, 2p + 1; a
+// pair's two CTAs are ranks 0 and 1 of the cluster's x dimension, the
+// dimension 2-SM MMA pairs are formed along).  Rank 0 issues 256-row MMAs over both
+// CTAs' operands; each CTA decodes its own 128 weight rows into its own
+// tensor memory, copies its own 64-token half of the activation tiles, and
+// reads its own rows of D.  Arrivals meant for rank 0's barriers (decode,
+// epilogue, and rank 1's copy completions, relayed by rank 1's warp 1) are
+// remote mbarrier arrives; the MMA commits arrive on both CTAs' barriers.
+template <int QT, bool P2>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const Params P) {
   using C = Cfg<QT>;
   constexpr int S = C::kStages;
+  constexpr int kSB = stage_bytes<QT, P2>();
+  constexpr int kBH = P2 ? kTileBytes / 2 : kTileBytes;  // this CTA's activation hi (and lo) tile
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023) & ~1023u;
-  const uint32_t bars = sbase + S * C::kStageBytes;
+  const uint32_t bars = sbase + S * kSB;
   // barriers: tma_full[S], prod_full[S], empty[S], acc_full[2], acc_empty[2], d2_empty, done
   auto tma_full = [&](int s) { return bars + 8 * s; };
   auto prod_full = [&](int s) { return bars + 8 * (S + s); };
@@ -517,38 +625,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(smem_raw + (tmem_slot - raw));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t tok0 = blockIdx.x * kTileTok;
-  const uint32_t row0 = blockIdx.y * kTileRows;
+  const uint32_t tt = P2 ? blockIdx.y : blockIdx.x;  // token tile
+  const uint32_t tok0 = tt * kTileTok;
+  const uint32_t row0 = (P2 ? blockIdx.x : blockIdx.y) * kTileRows;
   const int nchunk = (int)P.nsb * 4;
+  const uint32_t rank = P2 ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
+  // Arrive on rank 0's copy of one of this CTA's barrier offsets.
+  auto arrive_leader = [&](uint32_t bar) {
+    if (P2) mbar_arrive_cluster(peer_addr(bar, 0));
+    else mbar_arrive(bar);
+  };
 
   // Stage s: [activation hi tile][activation lo tile][mins (Q4_K)][sub-block sums (Q4_K)].
-  auto stage_bh = [&](int s) { return sbase + s * C::kStageBytes; };
-  auto stage_bl = [&](int s) { return stage_bh(s) + kTileBytes; };
-  auto stage_a2 = [&](int s) { return stage_bh(s) + 2 * kTileBytes; };
+  auto stage_bh = [&](int s) { return sbase + s * kSB; };
+  auto stage_bl = [&](int s) { return stage_bh(s) + kBH; };
+  auto stage_a2 = [&](int s) { return stage_bh(s) + 2 * kBH; };
   auto stage_b2 = [&](int s) { return stage_a2(s) + kSmallBytes; };
 
   if (threadIdx.x == 0) {
+    const uint32_t pair = P2 ? 2u : 1u;
     for (int s = 0; s < S; ++s) {
-      mbar_init(tma_full(s), 1);
-      mbar_init(prod_full(s), 4);
+      mbar_init(tma_full(s), (P2 && leader) ? 2u : 1u);  // rank 0: its own copy + rank 1's relay
+      mbar_init(prod_full(s), 4 * pair);
       mbar_init(empty(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), 4);
+      mbar_init(acc_empty(b), 4 * pair);
     }
-    mbar_init(d2_empty, 4);
+    mbar_init(d2_empty, 4 * pair);
     mbar_init(done_bar, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (P2) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
+                   "r"(kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
+                   "r"(kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (P2) cluster_sync();  // both CTAs' barriers initialised before any remote arrive
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot_ptr);
 
@@ -556,34 +681,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- bulk copies of the staged activation tiles ----
     if (lane == 0) {
       int issued = 0;
+      // A pair's workspace holds each chunk as [rank 0's half | rank 1's half].
+      constexpr int kSums = P2 ? kSmallBytes / 2 : kSmallBytes;
       for (int i = 0; i < nchunk; ++i) {
         const int s = i % S;
-        if (!wait_phase(empty(s), ((i / S) & 1) ^ 1)) {
+        if (!wait_phase<P2>(empty(s), ((i / S) & 1) ^ 1)) {
           atomicExch(P.error, 1);
           break;
         }
         const bool mins = C::kMins && (i & 3) == 3;
-        mbar_arrive_expect_tx(tma_full(s), 2 * kTileBytes + (mins ? kSmallBytes : 0));
+        mbar_arrive_expect_tx(tma_full(s), 2 * kBH + (mins ? kSums : 0));
         // The hi and lo tiles are adjacent in the stage and in the workspace.
-        bulk_load(stage_bh(s), P.xs + ((size_t)blockIdx.x * nchunk + i) * (2 * kTileBytes), 2 * kTileBytes,
+        bulk_load(stage_bh(s), P.xs + (((size_t)tt * nchunk + i) * (P2 ? 2 : 1) + rank) * (2 * kBH), 2 * kBH,
                   tma_full(s));
         if (mins)
-          bulk_load(stage_b2(s), P.sxs + ((size_t)blockIdx.x * P.nsb + (i >> 2)) * kSmallBytes, kSmallBytes,
-                    tma_full(s));
+          bulk_load(stage_b2(s), P.sxs + (((size_t)tt * P.nsb + (i >> 2)) * (P2 ? 2 : 1) + rank) * kSums,
+                    kSums, tma_full(s));
         issued = i + 1;
       }
-      // Drain: the last S issued copies must have landed before the CTA exits.
-      for (int i = issued - S < 0 ? 0 : issued - S; i < issued; ++i)
-        if (!wait_phase(tma_full(i % S), (i / S) & 1)) atomicExch(P.error, 1);
+      // Drain: the last S issued copies must have landed before the CTA exits
+      // (in a pair, rank 1's relay has observed every one of its copies).
+      if (!P2 || leader)
+        for (int i = issued - S < 0 ? 0 : issued - S; i < issued; ++i)
+          if (!wait_phase<P2>(tma_full(i % S), (i / S) & 1)) atomicExch(P.error, 1);
+    }
+    __syncwarp();
+  } else if (warp == 1 && !leader) {
+    // ---- rank 1 of a pair: relay each of its copies' completion to rank 0,
+    // then wait for rank 0's MMAs to finish with this CTA's tensor memory ----
+    if (lane == 0) {
+      for (int i = 0; i < nchunk; ++i) {
+        const int s = i % S;
+        if (!wait_phase<P2>(tma_full(s), (i / S) & 1)) {
+          atomicExch(P.error, 1);
+          break;
+        }
+        arrive_leader(tma_full(s));
+      }
+      if (!wait_phase<P2>(done_bar, 0)) atomicExch(P.error, 1);
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---- MMA issuer ----
+    // ---- MMA issuer (rank 0 of a pair issues for both CTAs) ----
+    auto mma_a = [&](uint32_t d, uint32_t a, uint64_t b, uint32_t acc) {
+      if constexpr (P2) mma_f16_ts_2(d, a, b, kIdesc2, acc);
+      else mma_f16_ts(d, a, b, kIdesc, acc);
+    };
+    auto commit = [&](uint32_t bar) {
+      if constexpr (P2) mma_commit_2(bar);
+      else mma_commit(bar);
+    };
     if (lane == 0) {
       bool ok = true;
       for (int sb = 0; sb < (int)P.nsb && ok; ++sb) {
         const int b = sb & 1;
-        if (!wait_phase(acc_empty(b), ((sb >> 1) & 1) ^ 1)) {
+        if (!wait_phase<P2>(acc_empty(b), ((sb >> 1) & 1) ^ 1)) {
           ok = false;
           break;
         }
@@ -592,7 +744,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 4; ++c) {
           const int i = sb * 4 + c, s = i % S;
           const uint32_t par = (i / S) & 1;
-          if (!wait_phase(tma_full(s), par) || !wait_phase(prod_full(s), par)) {
+          if (!wait_phase<P2>(tma_full(s), par) || !wait_phase<P2>(prod_full(s), par)) {
             ok = false;
             break;
           }
@@ -603,31 +755,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 4; ++k) {
             // K step of 16 fp16: 8 tensor-memory columns of A, 32 bytes (2
             // units of the descriptor's start address) of B.
-            mma_f16_ts(d1, a + 8 * k, bh + 2 * k, kIdesc, (c | k) != 0);
-            mma_f16_ts(d1, a + 8 * k, bl + 2 * k, kIdesc, 1);
-            if constexpr (!C::kMins) mma_f16_ts(d1, a + 32 + 8 * k, bh + 2 * k, kIdesc, 1);
+            mma_a(d1, a + 8 * k, bh + 2 * k, (c | k) != 0);
+            mma_a(d1, a + 8 * k, bl + 2 * k, 1);
+            if constexpr (!C::kMins) mma_a(d1, a + 32 + 8 * k, bh + 2 * k, 1);
           }
           if constexpr (C::kMins) {
             if (c == 3) {
               // The single D2 accumulator: the epilogue must have read the
               // previous super-block's.
-              if (sb > 0 && !wait_phase(d2_empty, (sb - 1) & 1)) {
+              if (sb > 0 && !wait_phase<P2>(d2_empty, (sb - 1) & 1)) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              mma_f16(tmem + C::kD2Col, desc_plain(stage_a2(s), 2048, 128), desc_plain(stage_b2(s), 2048, 128),
-                      kIdesc, 0);
+              // A pair's sums tile is 64 tokens: its K halves 1024 bytes apart.
+              const uint64_t a2 = desc_plain(stage_a2(s), 2048, 128);
+              const uint64_t b2 = desc_plain(stage_b2(s), P2 ? 1024 : 2048, 128);
+              if constexpr (P2) mma_f16_2(tmem + C::kD2Col, a2, b2, kIdesc2, 0);
+              else mma_f16(tmem + C::kD2Col, a2, b2, kIdesc, 0);
             }
           }
-          mma_commit(empty(s));
+          commit(empty(s));
         }
-        if (ok) mma_commit(acc_full(b));
+        if (ok) commit(acc_full(b));
       }
       if (!ok) atomicExch(P.error, 1);
       // Every MMA issued must finish before tensor memory is released.
-      mma_commit(done_bar);
-      if (!wait_phase(done_bar, 0)) atomicExch(P.error, 1);
+      commit(done_bar);
+      if (!wait_phase<P2>(done_bar, 0)) atomicExch(P.error, 1);
     }
     __syncwarp();
   } else if (warp < 6) {
@@ -658,7 +813,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int i = base + j;
         if (i < nchunk && ok) {
           const int s = i % S;
-          if (!warp_wait_phase(empty(s), ((i / S) & 1) ^ 1)) {
+          if (!warp_wait_phase<P2>(empty(s), ((i / S) & 1) ^ 1)) {
             ok = false;
           } else {
             tc_fence_after();
@@ -685,7 +840,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(prod_full(s));
+            if (lane == 0) arrive_leader(prod_full(s));
             if (i + R < nchunk) {
               if constexpr (QT == kTypeQ4_K) q4k_load(ring[j], wrow, i + R, valid);
               else if constexpr (QT == kTypeQ6_K) q6k_load(ring[j], wrow, i + R, valid);
@@ -727,7 +882,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int sb = 0; sb < (int)P.nsb; ++sb) {
       const int b = sb & 1;
       const uint32_t dd_next = sb + 1 < (int)P.nsb ? load_scale(sb + 1) : 0u;
-      if (!warp_wait_phase(acc_full(b), (sb >> 1) & 1)) {
+      if (!warp_wait_phase<P2>(acc_full(b), (sb >> 1) & 1)) {
         ok = false;
         break;
       }
@@ -743,7 +898,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(d2_empty);
+        if (lane == 0) arrive_leader(d2_empty);
       }
       float d;
       if constexpr (QT == kTypeQ8_0) d = __uint_as_float(dd);
@@ -758,7 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty(b));
+      if (lane == 0) arrive_leader(acc_empty(b));
       dd = dd_next;
     }
     if (!ok) {
@@ -774,11 +929,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (P2) cluster_sync();  // no remote arrive or MMA can still reach either CTA
+  else __syncthreads();
   tc_fence_after();
-  if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
-                 : "memory");
+  if (warp == 1) {
+    if constexpr (P2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                   : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                   : "memory");
+  }
 }
 
 // ---- activation staging ----------------------------------------------------------
@@ -794,7 +955,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // sums of each super-block: 4 KB at sxs + (tt * nsb + sb) * 4 KB, 8 x 16-byte
 // core matrices per 8 tokens, hi sums in K half 0 and lo sums in K half 1.
 // Tokens past the batch (the last tile's padding) are written as zeros.
-template <int QT>
+// P2 (CTA pairs): each 128-token tile is stored as two 64-token halves, the
+// half a pair's rank copies: chunk i of tile tt at xs + ((tt * nchunk + i) *
+// 2 + h) * 16 KB = [hi 8 KB | lo 8 KB] of tokens 64h .. 64h + 63, and the
+// sums as 2 KB halves (K half 1 at 1024 bytes).
+template <int QT, bool P2>
 __global__ void __launch_bounds__(256) stage_tokens_kernel(const float* __restrict__ x, int cols, uint32_t tokens,
                                                            uint8_t* __restrict__ xs, uint8_t* __restrict__ sxs,
                                                            float* __restrict__ tok_scale) {
@@ -824,7 +989,8 @@ __global__ void __launch_bounds__(256) stage_tokens_kernel(const float* __restri
   const float s = live ? exp2i(e) : 0.f;
   if (threadIdx.x == 0 && live) tok_scale[tok] = exp2i(-e);
 
-  const uint32_t row_off = (uint32_t)((t >> 3) * 1024 + (t & 7) * 128);
+  const int th = P2 ? (t >> 6) : 0, tl = P2 ? (t & 63) : t;  // half and row within it
+  const uint32_t row_off = (uint32_t)((tl >> 3) * 1024 + (tl & 7) * 128);
   for (int g = threadIdx.x; g < cols / 8; g += blockDim.x) {
     const int chunk = g >> 3, u = g & 7;
     const int sb = chunk >> 2, c = chunk & 3;
@@ -851,9 +1017,11 @@ __global__ void __launch_bounds__(256) stage_tokens_kernel(const float* __restri
       ph[k] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
       pl[k] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
     }
-    uint8_t* dst = xs + ((size_t)tt * nchunk + chunk) * (2 * kTileBytes) + row_off + ((u ^ (t & 7)) << 4);
+    constexpr int kHalf = P2 ? kTileBytes / 2 : kTileBytes;  // one token block's hi tile
+    uint8_t* dst = xs + (((size_t)tt * nchunk + chunk) * (P2 ? 2 : 1) + th) * (2 * kHalf) + row_off +
+                   ((u ^ (t & 7)) << 4);
     *reinterpret_cast<uint4*>(dst) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-    *reinterpret_cast<uint4*>(dst + kTileBytes) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+    *reinterpret_cast<uint4*>(dst + kHalf) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
   }
   if (QT == kTypeQ4_K) {
     const float* xr = reinterpret_cast<const float*>(xr4);
@@ -870,10 +1038,11 @@ __global__ void __launch_bounds__(256) stage_tokens_kernel(const float* __restri
       const double vs = acc * (double)s;
       const __half hh = __double2half(vs);
       const __half hl = __double2half(vs - (double)__half2float(hh));
-      __half* dst = reinterpret_cast<__half*>(sxs + ((size_t)tt * nsb + sb) * kSmallBytes + (t >> 3) * 128 +
-                                              (t & 7) * 16);
+      constexpr int kSums = P2 ? kSmallBytes / 2 : kSmallBytes;
+      __half* dst = reinterpret_cast<__half*>(sxs + (((size_t)tt * nsb + sb) * (P2 ? 2 : 1) + th) * kSums +
+                                              (tl >> 3) * 128 + (tl & 7) * 16);
       dst[j] = hh;
-      dst[1024 + j] = hl;  // K half 1, 2048 bytes on
+      dst[kSums / 4 + j] = hl;  // K half 1, kSums / 2 bytes on
     }
   }
 }
@@ -895,13 +1064,17 @@ WsLayout ws_layout(int64_t batch, int64_t cols) {
   return L;
 }
 
-template <int QT>
+// CTA pairs (cluster of two, 256-row MMAs) for every launch, or single CTAs
+// (the default).
+bool g_pair = false;
+
+template <int QT, bool P2>
 int launch_typed(float* y, const float* x, const void* w, int64_t batch, int64_t rows, int64_t cols,
                  const GemmWorkspace& ws, int* error, cudaStream_t stream) {
   const WsLayout L = ws_layout(batch, cols);
   uint8_t* base = static_cast<uint8_t*>(ws.ptr);
   const int64_t ntt = (batch + kTileTok - 1) / kTileTok;
-  stage_tokens_kernel<QT><<<(unsigned)(ntt * kTileTok), 256, 0, stream>>>(
+  stage_tokens_kernel<QT, P2><<<(unsigned)(ntt * kTileTok), 256, 0, stream>>>(
       x, (int)cols, (uint32_t)batch, base + L.xs, base + L.sxs, reinterpret_cast<float*>(base + L.scale));
   Params P;
   P.w = static_cast<const uint8_t*>(w);
@@ -914,9 +1087,44 @@ int launch_typed(float* y, const float* x, const void* w, int64_t batch, int64_t
   P.y = y;
   P.tok_scale = reinterpret_cast<const float*>(base + L.scale);
   P.error = error;
-  const dim3 grid((unsigned)ntt, (unsigned)((rows + kTileRows - 1) / kTileRows));
-  prefill_kernel<QT><<<grid, kThreads, smem_bytes<QT>(), stream>>>(P);
-  return cudaPeekAtLastError() == cudaSuccess ? 0 : -5;
+  unsigned row_tiles = (unsigned)((rows + kTileRows - 1) / kTileRows);
+  if (!P2) {
+    prefill_kernel<QT, false><<<dim3((unsigned)ntt, row_tiles), kThreads, smem_bytes<QT>(), stream>>>(P);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -5;
+  }
+  // Pairs of row tiles; an odd last tile gets a partner whose rows are all
+  // past the matrix (decoded as zeros, never stored).
+  row_tiles += row_tiles & 1u;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(row_tiles, (unsigned)ntt);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem_bytes<QT, true>();
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prefill_kernel<QT, true>, P) == cudaSuccess ? 0 : -5;
+}
+
+template <int QT>
+int launch_typed(float* y, const float* x, const void* w, int64_t batch, int64_t rows, int64_t cols,
+                 const GemmWorkspace& ws, int* error, cudaStream_t stream) {
+  return g_pair ? launch_typed<QT, true>(y, x, w, batch, rows, cols, ws, error, stream)
+                : launch_typed<QT, false>(y, x, w, batch, rows, cols, ws, error, stream);
+}
+
+template <int QT>
+cudaError_t prepare_typed() {
+  cudaError_t e = cudaFuncSetAttribute(prefill_kernel<QT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       smem_bytes<QT>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(prefill_kernel<QT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_bytes<QT, true>());
+  return e;
 }
 
 }  // namespace tc
@@ -931,17 +1139,13 @@ bool gemm_tc_supported(int qtype, int64_t batch, int64_t rows, int64_t cols) {
 size_t gemm_tc_workspace(int64_t batch, int64_t cols) { return tc::ws_layout(batch, cols).total; }
 
 int gemm_tc_prepare_device() {
-  if (cudaFuncSetAttribute(tc::prefill_kernel<kTypeQ4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::smem_bytes<kTypeQ4_K>()) != cudaSuccess)
-    return -5;
-  if (cudaFuncSetAttribute(tc::prefill_kernel<kTypeQ6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::smem_bytes<kTypeQ6_K>()) != cudaSuccess)
-    return -5;
-  if (cudaFuncSetAttribute(tc::prefill_kernel<kTypeQ8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::smem_bytes<kTypeQ8_0>()) != cudaSuccess)
+  if (tc::prepare_typed<kTypeQ4_K>() != cudaSuccess || tc::prepare_typed<kTypeQ6_K>() != cudaSuccess ||
+      tc::prepare_typed<kTypeQ8_0>() != cudaSuccess)
     return -5;
   return 0;
 }
+
+void gemm_tc_set_pair(bool on) { tc::g_pair = on; }
 
 int gemm_tc_launch(int qtype, float* y, const float* x, const void* w, int64_t batch, int64_t rows, int64_t cols,
                    const GemmWorkspace& ws, int* error, cudaStream_t stream) {

@@ -48,7 +48,7 @@ EXPORTS = (
     "gi_cuda_gemm_buf", "gi_cuda_gemm_fused_gate_up_buf", "gi_cuda_add_residual", "gi_cuda_swiglu",
     "gi_cuda_gemv_q8_0", "gi_cuda_gemv_q4_k", "gi_cuda_gemv_q6_k",
     "gi_cuda_gemm_q8_0", "gi_cuda_gemm_q4_k", "gi_cuda_gemm_q6_k", "gi_cuda_gemv_dev",
-    "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_ffn_dev", "gi_cuda_ffn_buf", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl", "gi_cuda_set_q6k_mma",
+    "gi_cuda_gemm_dev", "gi_cuda_gemm_dev_noalloc", "gi_cuda_gemv_multi_dev", "gi_cuda_ffn_dev", "gi_cuda_ffn_buf", "gi_cuda_buffer_device_ptr", "gi_cuda_buffer_bytes", "gi_cuda_set_pdl", "gi_cuda_set_q6k_mma", "gi_cuda_set_prefill_pair",
     "gi_cuda_last_error", "gi_quant_row_bytes", "gi_quantize", "gi_quantize_seeded",
     "gi_cuda_alloc_buffers", "gi_cuda_forward_transformer", "gi_cuda_model_create", "gi_cuda_model_destroy",
     "gi_cuda_model_reset", "gi_cuda_model_set_persistent", "gi_cuda_model_generate", "gi_cuda_tp_prepare", "gi_cuda_tp_connect", "gi_cuda_tp_close",
@@ -131,6 +131,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "gi_cuda_ffn_buf": ([f32p, vp, vp, vp, vp, u32, u32, ctypes.c_float], i32),
         "gi_cuda_set_pdl": ([i32], i32),
         "gi_cuda_set_q6k_mma": ([i32], i32),
+        "gi_cuda_set_prefill_pair": ([i32], i32),
         "gi_cuda_last_error": ([], ctypes.c_char_p),
         "gi_quant_row_bytes": ([i32, ctypes.c_int64], ctypes.c_int64),
         "gi_quantize": ([i32, f32p, ctypes.c_int64, ctypes.c_int64, vp, i32], i32),
@@ -368,6 +369,11 @@ def FFNBuf(x: np.ndarray, norm: Buffer, gate: Buffer, up: Buffer, down: Buffer, 
 
 def set_pdl(enable: bool) -> None:
     load_library().gi_cuda_set_pdl(1 if enable else 0)
+
+
+def set_prefill_pair(enable: bool) -> None:
+    """Batched GEMMs on CTA pairs (256-row cta_group::2 tcgen05 MMAs) or on single CTAs (the default)."""
+    load_library().gi_cuda_set_prefill_pair(1 if enable else 0)
 
 
 def set_q6k_mma(enable: bool) -> None:

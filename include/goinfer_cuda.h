@@ -308,6 +308,15 @@ int gi_cuda_set_pdl(int enable);
  * and 128256 x 8192 heads about 30 % faster. */
 int gi_cuda_set_q6k_mma(int enable);
 
+/* Batched (prefill) GEMMs on single CTAs (0, default) or on CTA pairs (1:
+ * clusters of two CTAs, 256-row cta_group::2 tcgen05 MMAs, each CTA loading
+ * half of the activation tile) -- no reference counterpart: a choice between
+ * two launch shapes of this library's tensor-core GEMM, with bit-identical
+ * results.  On B200 the pairs are slower at the config-3 shapes (the
+ * cross-CTA hand-off of the decoded weight tiles outlasts the 4-stage
+ * pipeline), so single CTAs stay the default. */
+int gi_cuda_set_prefill_pair(int enable);
+
 /* Text of the last failure on the calling thread ("" if none). */
 const char* gi_cuda_last_error(void);
 

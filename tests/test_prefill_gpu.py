@@ -29,6 +29,15 @@ def cuda():
     yield
 
 
+@pytest.fixture(params=[True, False], ids=["pair", "single"], autouse=True)
+def launch_shape(request):
+    """Every test on both launch shapes of the tensor-core GEMM: single CTAs
+    (the default) and CTA pairs (clusters of two, 256-row cta_group::2 MMAs)."""
+    G.set_prefill_pair(request.param)
+    yield request.param
+    G.set_prefill_pair(False)
+
+
 def gpu_gemm(qt, raw, x, batch, rows, cols):
     buf = G.CreateBuffer(raw)
     try:
@@ -81,6 +90,23 @@ def test_tc_shapes_match_oracle(qt, batch, rows, cols):
     x = np.random.default_rng(2000 + batch).normal(size=(batch, cols)).astype(np.float32)
     y = gpu_gemm(qt, raw, x, batch, rows, cols)
     check_against_oracle(qt, raw, x, y, rows, cols, f"tc {qt} {batch}x{rows}x{cols}")
+
+
+@pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
+def test_tc_pair_agrees_with_single(qt, launch_shape):
+    """The two launch shapes sum the same products in the same K order: the
+    results agree to float32 rounding (an odd row-tile count included)."""
+    if not launch_shape:
+        pytest.skip("compares the two shapes once")
+    batch, rows, cols = 200, 3 * 128 + 5, 1536
+    raw = G.quantize(qt, seeded_weights(41, rows, cols))
+    x = np.random.default_rng(42).normal(size=(batch, cols)).astype(np.float32)
+    y_pair = gpu_gemm(qt, raw, x, batch, rows, cols)
+    G.set_prefill_pair(False)
+    y_single = gpu_gemm(qt, raw, x, batch, rows, cols)
+    diff = np.abs(y_pair - y_single).max() / (np.abs(y_single).max() + 1e-30)
+    print(f"pair vs single: max |diff| / max |y| = {diff:.3e}, identical: {np.array_equal(y_pair, y_single)}")
+    assert diff <= 1e-6
 
 
 @pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
