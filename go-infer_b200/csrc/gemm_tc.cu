@@ -681,6 +681,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- bulk copies of the staged activation tiles ----
     if (lane == 0) {
       int issued = 0;
+      // The staged activations come from the staging kernel just before
+      // this one (programmatic dependent launch: the weight decode already
+      // runs while it finishes).
+      griddep_wait();
       // A pair's workspace holds each chunk as [rank 0's half | rank 1's half].
       constexpr int kSums = P2 ? kSmallBytes / 2 : kSmallBytes;
       for (int i = 0; i < nchunk; ++i) {
@@ -916,6 +920,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) arrive_leader(acc_empty(b));
       dd = dd_next;
     }
+    griddep_wait();  // tok_scale is the staging kernel's
     if (!ok) {
       atomicExch(P.error, 1);
     } else if (valid) {
@@ -964,6 +969,7 @@ __global__ void __launch_bounds__(256) stage_tokens_kernel(const float* __restri
                                                            uint8_t* __restrict__ xs, uint8_t* __restrict__ sxs,
                                                            float* __restrict__ tok_scale) {
   __shared__ float red[8];
+  griddep_launch_dependents();  // the GEMM may start: it waits for this grid before reading what it writes
   const uint32_t tok = blockIdx.x;
   const bool live = tok < tokens;
   const int tt = (int)(tok >> 7), t = (int)(tok & 127);
@@ -1089,8 +1095,19 @@ int launch_typed(float* y, const float* x, const void* w, int64_t batch, int64_t
   P.error = error;
   unsigned row_tiles = (unsigned)((rows + kTileRows - 1) / kTileRows);
   if (!P2) {
-    prefill_kernel<QT, false><<<dim3((unsigned)ntt, row_tiles), kThreads, smem_bytes<QT>(), stream>>>(P);
-    return cudaPeekAtLastError() == cudaSuccess ? 0 : -5;
+    // Programmatic dependent launch: the weight decode of the first stages
+    // overlaps the staging kernel; the copies and the scale reads wait for it.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ntt, row_tiles);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_bytes<QT>();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, prefill_kernel<QT, false>, P) == cudaSuccess ? 0 : -5;
   }
   // Pairs of row tiles; an odd last tile gets a partner whose rows are all
   // past the matrix (decoded as zeros, never stored).
