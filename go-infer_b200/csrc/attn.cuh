@@ -137,18 +137,40 @@ GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* 
   }
 }
 
-// Output element (head h, dimension d): the splits' partials merged.
+// Output element (head h, dimension d): the splits' partials merged, in
+// split order.  The loads of 8 splits are issued before their arithmetic
+// (the partials sit in L2: one round trip per 8 splits instead of one per
+// split); the operations and their order are those of a plain split loop.
 GI_DEVINL void attn_combine_one(const float* part, float* __restrict__ att, int hd, int splits, int h, int d) {
+  constexpr int U = 8;
   const float* ph = part + (size_t)h * splits * (hd + 2);
+  const int stride = hd + 2, dd = d < hd ? d : 0;  // a thread past the head's dimensions stores nothing
   float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, __ldcg(ph + s * (hd + 2)));
+  for (int s0 = 0; s0 < splits; s0 += U) {
+    float m[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) m[u] = s0 + u < splits ? __ldcg(ph + (size_t)(s0 + u) * stride) : -INFINITY;
+#pragma unroll
+    for (int u = 0; u < U; ++u) M = fmaxf(M, m[u]);
+  }
   float L = 0.f, acc = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    const float m = __ldcg(ph + s * (hd + 2));
-    if (m == -INFINITY) continue;
-    const float f = (float)exp((double)(m - M));
-    L = fmaf(__ldcg(ph + s * (hd + 2) + 1), f, L);
-    acc = fmaf(__ldcg(ph + s * (hd + 2) + 2 + d), f, acc);
+  for (int s0 = 0; s0 < splits; s0 += U) {
+    float m[U], l[U], o[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const bool in = s0 + u < splits;
+      const float* ps = ph + (size_t)(in ? s0 + u : 0) * stride;
+      m[u] = in ? __ldcg(ps) : -INFINITY;
+      l[u] = __ldcg(ps + 1);
+      o[u] = __ldcg(ps + 2 + dd);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (m[u] == -INFINITY) continue;
+      const float f = (float)exp((double)(m[u] - M));
+      L = fmaf(l[u], f, L);
+      acc = fmaf(o[u], f, acc);
+    }
   }
   if (d < hd) att[(size_t)h * hd + d] = L > 0.f ? acc / L : 0.f;
 }

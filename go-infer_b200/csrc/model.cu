@@ -253,13 +253,36 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   griddep_launch_dependents();
   float v = -INFINITY;
   int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float l = logits[i];
-    if (idx == 0x7fffffff || l > v) {  // strictly greater: the first maximum stays
+  auto consider = [&](float l, int i) {  // i increases along each thread's walk
+    if (idx == 0x7fffffff || l > v) {    // strictly greater: the first maximum stays
       v = l;
       idx = i;
     }
+  };
+  // 16-byte loads, 8 in flight per thread (the logits sit in L2, written by
+  // the head GEMV just before), then the scalar tail.
+  constexpr int U = 8;
+  const int n4 = n >> 2;
+  const float4* l4 = reinterpret_cast<const float4*>(logits);
+  for (int base = threadIdx.x; base < n4; base += U * blockDim.x) {
+    float4 q[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = base + u * blockDim.x;
+      q[u] = j < n4 ? l4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = base + u * blockDim.x;
+      if (j < n4) {
+        consider(q[u].x, 4 * j);
+        consider(q[u].y, 4 * j + 1);
+        consider(q[u].z, 4 * j + 2);
+        consider(q[u].w, 4 * j + 3);
+      }
+    }
   }
+  for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) consider(logits[i], i);
   // combine (value, index): larger value wins, equal values keep the lower index
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
