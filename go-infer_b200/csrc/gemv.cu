@@ -229,12 +229,7 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
       const int row = (T0 + tl) * 16 + lane;
       if (lane < 16 && row < p.rows[0]) {
         float sum = 0.f;
-        bool ok = true;
-        for (int r = 0; r < world && ok; ++r) {
-          float v = 0.f;
-          ok = tp_wait_ll(rv + (size_t)r * p.tp.max_dim + row, seq, p.tp.error, &v);
-          sum = r == 0 ? v : __fadd_rn(sum, v);
-        }
+        const bool ok = tp_sum_ll(rv + row, p.tp.max_dim, world, seq, p.tp.error, &sum);
         if (ok)
           p.y[0][row] = __fadd_rn(p.y[0][row], sum);
         else
