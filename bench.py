@@ -39,9 +39,10 @@ decode   (the metric's second half) greedy decode tokens/s of the Llama-
          512-token prompt, 64 steps) tensor-parallel over the N ranks, and at
          N=1 config 4 (Llama-2-7B shape, 128-token prompt, 64 steps) with a
          bounded CPU-oracle sample of the same decode step; prefill (config
-         3, 512 tokens x 4096 columns) at N=1.  --persistent adds, under
-         "persistent", the same generations with every layer of a step in
-         one persistent launch (gi_cuda_model_set_persistent), and whether
+         3, 512 tokens x 4096 columns) at N=1.  "persistent" holds the same
+         generations with every layer of a step in one persistent launch
+         (gi_cuda_model_set_persistent) -- for config 5 always at N > 1, and
+         with --persistent also at N=1 and for config 4 -- and whether
          their ids equal the per-layer launches'.  gemv_other times the Q6_K
          lm_head shapes on both Q6_K kernels (the int8 tensor-core default and
          "_cuda_cores").
@@ -298,7 +299,9 @@ def decode_section(args, world, rank, local, pg):
     ids, _l, ms = model.generate(prompt5, 64)
     ms = max_over_ranks(ms)
     w_bytes = sum(b.nbytes for b in dm.bufs.values()) - dm.bufs["token_embd.weight"].nbytes
-    pers5 = persistent_run(model, prompt5, ids) if args.persistent else None
+    # Under tensor parallelism the persistent kernel is always timed too (on
+    # B200 it was ahead of the per-layer launches at TP2 and 22 % ahead at TP4).
+    pers5 = persistent_run(model, prompt5, ids) if (args.persistent or world > 1) else None
     model.close()
     dm.close()
     if world > 1:
