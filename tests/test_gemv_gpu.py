@@ -315,7 +315,8 @@ def test_prefill_batch_matches_per_token_oracle():
 @pytest.mark.parametrize("qt", [G.TYPE_Q4_K, G.TYPE_Q6_K, G.TYPE_Q8_0])
 def test_pinned_host_output_written_directly(qt):
     """A page-locked, device-mapped y is written by the kernel itself (no
-    device-to-host copy); the result is bit-identical to the copied one."""
+    device-to-host copy); the results are bit-identical to the copied ones
+    (batch 1, per-token batch 3, tensor-core batch 16)."""
     import torch
     rows, cols = 1000, 2048
     raw = G.quantize(qt, seeded_weights(90, rows, cols))
@@ -329,13 +330,13 @@ def test_pinned_host_output_written_directly(qt):
         G.MatMulBuf(qt, y_pin, x_pin, buf, rows, cols)
         assert np.array_equal(y_pin.view(np.uint32), y_page.view(np.uint32))
         assert_parity(y_pin, O.matmul(qt, x, raw, rows, cols), what=f"pinned {qt}")
-        if qt != G.TYPE_Q8_0:  # batched prefill (tensor-core path for batch >= 16)
-            xb = np.stack([seeded_x(92 + b, cols) for b in range(16)])
-            yb_page = np.zeros(16 * rows, np.float32)
-            G.MatMulBatchBuf(qt, yb_page, xb.reshape(-1), buf, 16, rows, cols)
-            yb_pin = torch.zeros(16 * rows).pin_memory().numpy()
-            G.MatMulBatchBuf(qt, yb_pin, torch.from_numpy(xb.reshape(-1)).pin_memory().numpy(), buf, 16, rows, cols)
-            assert np.array_equal(yb_pin.view(np.uint32), yb_page.view(np.uint32))
+        for nb in (3, 16):  # per-token GEMVs, then the tensor-core prefill
+            xb = np.stack([seeded_x(92 + b, cols) for b in range(nb)])
+            yb_page = np.zeros(nb * rows, np.float32)
+            G.MatMulBatchBuf(qt, yb_page, xb.reshape(-1), buf, nb, rows, cols)
+            yb_pin = torch.zeros(nb * rows).pin_memory().numpy()
+            G.MatMulBatchBuf(qt, yb_pin, torch.from_numpy(xb.reshape(-1)).pin_memory().numpy(), buf, nb, rows, cols)
+            assert np.array_equal(yb_pin.view(np.uint32), yb_page.view(np.uint32)), f"batch {nb}"
     finally:
         G.ReleaseBuffer(buf)
 
