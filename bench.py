@@ -276,12 +276,23 @@ def decode_section(args, world, rank, local, pg):
         return float(t.item())
 
     def persistent_run(model, prompt, ids_ref):
-        """The same generation with every layer of a step in one persistent launch."""
-        model.set_persistent(True)
-        model.reset()
-        model.generate(prompt, 64)
-        model.reset()
-        ids_p, _l, ms_p = model.generate(prompt, 64)
+        """The same generation with every layer of a step in one persistent
+        launch.  A failure (a shape the plan does not take, a bounded wait
+        that gave up: the same on every rank) is reported in the line; the
+        per-layer numbers stand."""
+        try:
+            model.set_persistent(True)
+            model.reset()
+            model.generate(prompt, 64)
+            model.reset()
+            ids_p, _l, ms_p = model.generate(prompt, 64)
+        except G.GoInferCudaError as exc:
+            try:
+                model.set_persistent(False)
+            except G.GoInferCudaError:
+                pass
+            model.reset()
+            return {"error": str(exc)[:200]}
         ms_p = max_over_ranks(ms_p)
         model.set_persistent(False)
         return {"tok_s": round(63 / (ms_p / 1e3), 2), "ms_per_token": round(ms_p / 63, 4),
