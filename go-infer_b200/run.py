@@ -77,6 +77,8 @@ def prefill(args) -> None:
     y = torch.empty(args.batch, args.rows, device="cuda")
     st = torch.cuda.Stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    G.set_prefill_pair(args.pair)
+
     def run():
         G.gemm_dev(qt, y.data_ptr(), x.data_ptr(), wb.device_ptr, wb.nbytes, args.batch, args.rows, args.cols,
                    st.cuda_stream)
@@ -91,9 +93,10 @@ def prefill(args) -> None:
             e1.record()
         e1.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / args.reps
-        print(f"prefill {args.type} {args.batch}x{args.rows}x{args.cols}: {us:.1f} us "
-              f"({2 * args.batch * args.rows * args.cols / us / 1e6:.1f} TFLOP/s)")
+        print(f"prefill {args.type} {args.batch}x{args.rows}x{args.cols}{' (CTA pairs)' if args.pair else ''}: "
+              f"{us:.1f} us ({2 * args.batch * args.rows * args.cols / us / 1e6:.1f} TFLOP/s)")
     finally:
+        G.set_prefill_pair(False)
         G.ReleaseBuffer(wb)
 
 
@@ -157,6 +160,7 @@ def main() -> None:
     p.add_argument("--batch", type=int, default=512)
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--seed", type=int, default=8)
+    p.add_argument("--pair", action="store_true", help="CTA pairs (cta_group::2 MMAs) instead of single CTAs")
     v = sub.add_parser("gemv")
     v.add_argument("--type", choices=sorted(TYPES), default="q4_k")
     v.add_argument("--rows", type=int, default=11008)
