@@ -181,6 +181,7 @@ namespace gi {
 
 int gemv_prepare_device() { return 0; }
 int gemm_prepare_device() { return 0; }
+void gemm_tc_set_pair(bool) {}
 
 int64_t row_bytes(int qtype, int64_t cols) {
   switch (qtype) {
