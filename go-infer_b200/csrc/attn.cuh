@@ -17,19 +17,30 @@ inline size_t attn_smem_bytes(int kv_mul, int hd) {
   return sizeof(float) * ((size_t)kv_mul * hd + 2 * (size_t)kAttChunk * hd + (size_t)kv_mul * kAttChunk + 2 * kv_mul);
 }
 
+// Query heads per attention item: kv_mul halved while the items (kv heads x
+// chunks x head groups) number fewer than `target`.
+inline int attn_heads_per_item(int kv_mul, int n_kv_heads, int splits, int target) {
+  int hq = kv_mul;
+  while (hq > 1 && hq % 2 == 0 && (long long)n_kv_heads * splits * (kv_mul / hq) < target) hq /= 2;
+  return hq;
+}
+
 // ---- attention with GQA (forward.go:226-266), split over KV positions -------
-// CTA (kv head g, chunk c) handles the kv_mul query heads of g against the
-// cache slots [32c, 32c + 32) of the active context.  It applies RoPE
-// (kernels.go:22-36; rope[pos][i] = (cos, sin) of pos / theta^(2i/hd),
+// Item (kv head g, chunk c, head group hg) handles query heads hg*hq ..
+// hg*hq + hq - 1 of g's kv_mul heads against the cache slots [32c, 32c + 32)
+// of the active context (hq divides kv_mul; the callers pick it so that the
+// items fill the GPU: under tensor parallelism a rank holds few kv heads,
+// and each head's arithmetic is the same whatever the grouping).  It applies
+// RoPE (kernels.go:22-36; rope[pos][i] = (cos, sin) of pos / theta^(2i/hd),
 // computed in double on the host and rounded to float32) to its queries as
-// it stages them; the CTA whose chunk holds this step's slot also rotates
-// k, and writes k and v into the cache (forward.go:226-238) — no other CTA
-// reads that slot.  It stages the chunk's K and V rows in shared memory
-// (all loads in flight at once), then writes, per query head, (max, sum of
-// exp, unnormalised output) for attn_combine_kernel.  Scores use the float64
-// exp of kernels.go:60.
-// One (kv head g, chunk c) item, by every thread of the calling CTA; sm:
-// attn_smem_bytes(kv_mul, hd) of shared memory.
+// it stages them; the items whose chunk holds this step's slot also rotate
+// k, and the one of head group 0 writes k and v into the cache
+// (forward.go:226-238) — no other item reads that slot from the cache.  It
+// stages the chunk's K and V rows in shared memory (all loads in flight at
+// once), then writes, per query head, (max, sum of exp, unnormalised output)
+// for attn_combine_one.  Scores use the float64 exp of kernels.go:60.
+// One item, by every thread of the calling CTA; sm: attn_smem_bytes(hq, hd)
+// of shared memory.
 //
 // q, k, v and (in attn_combine_one) part may have been written earlier in the
 // same launch by other CTAs (the persistent decode-layer kernel rewrites them
@@ -38,25 +49,27 @@ inline size_t attn_smem_bytes(int kv_mul, int hd) {
 GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* q, const float* k, const float* v,
                                  const float2* __restrict__ rope, float* __restrict__ kc, float* __restrict__ vc,
                                  float* part, int kv_mul, int hd, int kv_dim, int splits, float scale,
-                                 uint32_t max_pos, int* error, int g, int c, float* sm) {
+                                 uint32_t max_pos, int* error, int g, int c, int hg, int hq, float* sm) {
   const uint32_t pos = st->pos, slot = st->slot;
   if (pos >= max_pos) {  // past the RoPE table: report, touch nothing
-    if (g == 0 && c == 0 && threadIdx.x == 0) atomicExch(error, 1);
+    if (g == 0 && c == 0 && hg == 0 && threadIdx.x == 0) atomicExch(error, 1);
     return;
   }
   const int active = (int)st->active;
   const int t0 = c * kAttChunk;
   const int nt = max(0, min(kAttChunk, active - t0));
   const int half = hd >> 1, hd4 = hd >> 2;
-  float* qs = sm;                          // [kv_mul][hd]
-  float* ks = qs + kv_mul * hd;            // [kAttChunk][hd]
+  float* qs = sm;                          // [hq][hd]
+  float* ks = qs + hq * hd;                // [kAttChunk][hd]
   float* vs = ks + kAttChunk * hd;         // [kAttChunk][hd]
-  float* sc = vs + kAttChunk * hd;         // [kv_mul][kAttChunk]
-  float* mx = sc + kv_mul * kAttChunk;     // [kv_mul][2]
+  float* sc = vs + kAttChunk * hd;         // [hq][kAttChunk]
+  float* mx = sc + hq * kAttChunk;         // [hq][2]
   const float2* cs = rope + (size_t)pos * half;
-  // queries of g's heads, rotated (r0 = v0 c - v1 s, r1 = v0 s + v1 c)
-  const float* qg = q + (size_t)g * kv_mul * hd;
-  for (int i = threadIdx.x; i < kv_mul * half; i += blockDim.x) {
+  // the item's queries (heads hg*hq .. hg*hq + hq - 1 of g's group), rotated
+  // (r0 = v0 c - v1 s, r1 = v0 s + v1 c)
+  const int h_first = g * kv_mul + hg * hq;  // the item's first query head
+  const float* qg = q + (size_t)h_first * hd;
+  for (int i = threadIdx.x; i < hq * half; i += blockDim.x) {
     const int h = i / half, j = i - h * half;
     const float2 r = cs[j];
     const float v0 = __ldcg(qg + h * hd + j), v1 = __ldcg(qg + h * hd + j + half);
@@ -83,18 +96,20 @@ GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* 
       const float r1 = __fadd_rn(__fmul_rn(v0, r.y), __fmul_rn(v1, r.x));
       ks[cur * hd + j] = r0;
       ks[cur * hd + j + half] = r1;
-      krow[j] = r0;
-      krow[j + half] = r1;
+      if (hg == 0) {  // one item of the chunk writes the cache
+        krow[j] = r0;
+        krow[j + half] = r1;
+      }
     }
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
       const float val = __ldcg(v + g * hd + d);
       vs[cur * hd + d] = val;
-      vrow[d] = val;
+      if (hg == 0) vrow[d] = val;
     }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int p = warp; p < kv_mul * nt; p += nw) {  // one warp per (head, position)
+  for (int p = warp; p < hq * nt; p += nw) {  // one warp per (head, position)
     const int h = p / nt, t = p - h * nt;
     float s = 0.f;
     for (int d = lane; d < hd; d += 32) s = fmaf(qs[h * hd + d], ks[t * hd + d], s);
@@ -102,7 +117,7 @@ GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* 
     if (lane == 0) sc[h * kAttChunk + t] = __fmul_rn(s, scale);
   }
   __syncthreads();
-  for (int h = warp; h < kv_mul; h += nw) {  // local softmax statistics per head
+  for (int h = warp; h < hq; h += nw) {  // local softmax statistics per head
     float m = -INFINITY;
     for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[h * kAttChunk + t]);
     m = warp_max(m);
@@ -119,7 +134,7 @@ GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* 
     }
   }
   __syncthreads();
-  for (int o = threadIdx.x; o < kv_mul * hd; o += blockDim.x) {  // thread per (head, d)
+  for (int o = threadIdx.x; o < hq * hd; o += blockDim.x) {  // thread per (head, d)
     const int h = o / hd, d = o - h * hd;
     float a0 = 0.f, a1 = 0.f;
     int t = 0;
@@ -128,7 +143,7 @@ GI_DEVINL void attn_partial_item(const StepState* __restrict__ st, const float* 
       a1 = fmaf(sc[h * kAttChunk + t + 1], vs[(t + 1) * hd + d], a1);
     }
     if (t < nt) a0 = fmaf(sc[h * kAttChunk + t], vs[t * hd + d], a0);
-    float* pp = part + ((size_t)(g * kv_mul + h) * splits + c) * (hd + 2);
+    float* pp = part + ((size_t)(h_first + h) * splits + c) * (hd + 2);
     pp[2 + d] = a0 + a1;
     if (d == 0) {
       pp[0] = nt > 0 ? mx[2 * h] : -INFINITY;

@@ -358,7 +358,8 @@ __global__ void __launch_bounds__(kLThreads, 1) layers_kernel(const LayersCfg a,
   // (RoPE, this step's cache write, scores and partial softmax sums per
   // (kv head, chunk), forward.go:226-266) and their combination.  One code
   // path for all four projections keeps a single copy of the GEMV inlined.
-  const int items = a.n_kv_heads * a.splits, nph = 4 * a.n_layers;
+  // attention items: (kv head, head group of hq query heads, chunk), chunk fastest
+  const int ng = a.kv_mul / a.hq, items = a.n_kv_heads * ng * a.splits, nph = 4 * a.n_layers;
   for (int k = 0; k < nph; ++k) {
     G.run(*p, smem);
     arrive();
@@ -372,8 +373,9 @@ __global__ void __launch_bounds__(kLThreads, 1) layers_kernel(const LayersCfg a,
       float* kc = a.kcache + (size_t)l * a.layer_kv;
       float* vc = a.vcache + (size_t)l * a.layer_kv;
       for (int it = c; it < items; it += (int)nct) {
+        const int gh = it / a.splits;  // g * ng + hg
         attn_partial_item(a.st, a.q, a.k, a.v, a.rope, kc, vc, a.part, a.kv_mul, a.hd, a.kv_dim, a.splits, a.scale,
-                          a.max_pos, a.error, it / a.splits, it % a.splits, att_sm);
+                          a.max_pos, a.error, gh / ng, it % a.splits, gh % ng, a.hq, att_sm);
         __syncthreads();
       }
       if (!sync()) break;

@@ -24,6 +24,7 @@ struct LayersCfg {
   const float2* rope = nullptr;
   size_t layer_kv = 0;  // floats of one layer's K (or V) cache
   int kv_mul = 1, hd = 0, kv_dim = 0, n_kv_heads = 0, n_heads = 0, splits = 1;
+  int hq = 1;  // query heads per attention item (divides kv_mul)
   float scale = 1.f;
   uint32_t max_pos = 0;
   unsigned* bar = nullptr;

@@ -128,12 +128,13 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const StepState* __re
                                                            const float2* __restrict__ rope, float* __restrict__ kc,
                                                            float* __restrict__ vc, float* __restrict__ part,
                                                            int kv_mul, int hd, int kv_dim, int splits, float scale,
-                                                           uint32_t max_pos, int* error) {
+                                                           uint32_t max_pos, int* error, int hq) {
   extern __shared__ __align__(16) float sm[];
   griddep_wait();
   griddep_launch_dependents();
-  attn_partial_item(st, q, k, v, rope, kc, vc, part, kv_mul, hd, kv_dim, splits, scale, max_pos, error, blockIdx.x,
-                    blockIdx.y, sm);
+  const int ng = kv_mul / hq;  // head groups per kv head: blockIdx.x = g * ng + hg
+  attn_partial_item(st, q, k, v, rope, kc, vc, part, kv_mul, hd, kv_dim, splits, scale, max_pos, error,
+                    blockIdx.x / ng, blockIdx.y, blockIdx.x % ng, hq, sm);
 }
 
 __global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ att, int hd, int splits) {
@@ -518,7 +519,6 @@ int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
     if (e != cudaSuccess) return -5;
   }
   const size_t layer_kv = (size_t)c.max_seq * kv_dim;
-  const size_t att_smem = attn_smem_bytes(kv_mul, hd);
   if (plan_) {  // every layer in one persistent launch
     LayersCfg a;
     a.n_layers = n_layers_;
@@ -529,6 +529,9 @@ int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
     a.layer_kv = layer_kv;
     a.kv_mul = kv_mul, a.hd = hd, a.kv_dim = kv_dim, a.n_kv_heads = c.n_kv_heads, a.n_heads = c.n_heads;
     a.splits = att_splits_;
+    // items split only while twice as many still run in one round of CTAs
+    // (one CTA per SM): one round of whole items beats two of halves
+    a.hq = attn_heads_per_item(kv_mul, c.n_kv_heads, att_splits_, sm_count_ / 2 + 1);
     a.scale = c.attn_scale;
     a.max_pos = (uint32_t)c.max_pos;
     a.error = scratch_.error;
@@ -564,9 +567,13 @@ int DecodeModel::enqueue_step(cudaStream_t s, bool embed, bool pdl) {
     if (Ly.bk && e == cudaSuccess) e = launch(pdl, blocks(kv_dim, 256), dim3(256), 0, s, add_kernel, k_, Ly.bk, kv_dim);
     if (Ly.bv && e == cudaSuccess) e = launch(pdl, blocks(kv_dim, 256), dim3(256), 0, s, add_kernel, v_, Ly.bv, kv_dim);
     if (e != cudaSuccess) return -5;
-    e = launch(pdl, dim3(c.n_kv_heads, att_splits_), dim3(256), att_smem, s, attn_partial_kernel,
+    // at least two items per SM: under tensor parallelism a rank's few kv
+    // heads are split by query-head groups
+    const int hq = attn_heads_per_item(kv_mul, c.n_kv_heads, att_splits_, 2 * sm_count_);
+    e = launch(pdl, dim3(c.n_kv_heads * (kv_mul / hq), att_splits_), dim3(256), attn_smem_bytes(hq, hd), s,
+               attn_partial_kernel,
                (const StepState*)st_, (const float*)q_, (const float*)k_, (const float*)v_, (const float2*)rope_, kc,
-               vc, part_, kv_mul, hd, kv_dim, att_splits_, c.attn_scale, (uint32_t)c.max_pos, scratch_.error);
+               vc, part_, kv_mul, hd, kv_dim, att_splits_, c.attn_scale, (uint32_t)c.max_pos, scratch_.error, hq);
     if (e != cudaSuccess) return -5;
     e = launch(pdl, dim3(c.n_heads), dim3(hd), 0, s, attn_combine_kernel, (const float*)part_, att_, hd, att_splits_);
     if (e != cudaSuccess) return -5;
