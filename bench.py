@@ -248,8 +248,8 @@ def run_reference(args):
         "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
-        "config": step_config(world),
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded)", "config": step_config(world),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample, "rows_sampled": round(frac, 4), "nproc": os.cpu_count(),
                          "cpu_model": cpu_model()},
