@@ -301,15 +301,9 @@ struct GemvPhase {
       for (int tl = warp; tl < ntl; tl += W) {
         const int row = (T0 + tl) * 16 + lane;
         if (lane < 16 && row < p.rows[0]) {
-          // rank by rank (tp_sum_ll's all-ranks-at-once loads cost this
-          // kernel registers: 3 % slower at TP2 on B200)
+          // four ranks' words at a time (eight cost this kernel registers)
           float sum = 0.f;
-          bool ok = true;
-          for (int r = 0; r < world && ok; ++r) {
-            float v = 0.f;
-            ok = tp_wait_ll(rv + (size_t)r * p.tp.max_dim + row, seq, p.tp.error, &v);
-            sum = r == 0 ? v : __fadd_rn(sum, v);
-          }
+          const bool ok = tp_sum_ll<4>(rv + row, p.tp.max_dim, world, seq, p.tp.error, &sum);
           if (ok)
             p.y[0][row] = __fadd_rn(p.y[0][row], sum);
           else

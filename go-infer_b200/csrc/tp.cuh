@@ -122,26 +122,34 @@ __device__ __forceinline__ bool tp_wait_ll(const unsigned long long* p, uint32_t
 }
 
 // The rank-ordered sum of one row's tagged partials (rank r's word at
-// rv + r * stride): every rank's word is loaded at once, a word not yet
-// tagged is then waited for as tp_wait_ll does, and the values are added in
-// rank order.  One round trip when the partials have arrived, instead of
-// one per rank.
+// rv + r * stride): the words of B ranks at a time are loaded at once, a
+// word not yet tagged is then waited for as tp_wait_ll does, and the values
+// are added in rank order.  One round trip per B ranks when the partials
+// have arrived, instead of one per rank (B = 8 in the stand-alone GEMV; the
+// persistent kernel, short of registers, takes 4).
+template <int B = kTpMaxWorld>
 __device__ __forceinline__ bool tp_sum_ll(const unsigned long long* rv, size_t stride, int world, uint32_t tag,
                                           const int* error, float* out) {
-  unsigned long long w[kTpMaxWorld];
-#pragma unroll
-  for (int r = 0; r < kTpMaxWorld; ++r)
-    if (r < world) w[r] = ld_ll(rv + (size_t)r * stride);
   float sum = 0.f;
 #pragma unroll
-  for (int r = 0; r < kTpMaxWorld; ++r) {
-    if (r < world) {
-      float v;
-      if ((uint32_t)(w[r] >> 32) == tag)
-        v = __uint_as_float((uint32_t)w[r]);
-      else if (!tp_wait_ll(rv + (size_t)r * stride, tag, error, &v))
-        return false;
-      sum = r == 0 ? v : __fadd_rn(sum, v);
+  for (int r0 = 0; r0 < kTpMaxWorld; r0 += B) {
+    if (r0 < world) {
+      unsigned long long w[B];
+#pragma unroll
+      for (int u = 0; u < B; ++u)
+        if (r0 + u < world) w[u] = ld_ll(rv + (size_t)(r0 + u) * stride);
+#pragma unroll
+      for (int u = 0; u < B; ++u) {
+        const int r = r0 + u;
+        if (r < world) {
+          float v;
+          if ((uint32_t)(w[u] >> 32) == tag)
+            v = __uint_as_float((uint32_t)w[u]);
+          else if (!tp_wait_ll(rv + (size_t)r * stride, tag, error, &v))
+            return false;
+          sum = r == 0 ? v : __fadd_rn(sum, v);
+        }
+      }
     }
   }
   *out = sum;
