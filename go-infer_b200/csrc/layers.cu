@@ -350,7 +350,8 @@ __global__ void __launch_bounds__(kLThreads, 1) layers_kernel(const LayersCfg a,
   // and up of RMSNorm(x) with SwiGLU (forward.go:275-283); x += Wdown h
   // (forward.go:284-287).  Between Q/K/V and O run the attention partials
   // (RoPE, this step's cache write, scores and partial softmax sums per
-  // (kv head, chunk), forward.go:226-266) and their combination.  One code
+  // (kv head, query-head group, chunk), forward.go:226-266) and their
+  // combination.  One code
   // path for all four projections keeps a single copy of the GEMV inlined.
   // attention items: (kv head, head group of hq query heads, chunk), chunk fastest
   const int ng = a.kv_mul / a.hq, items = a.n_kv_heads * ng * a.splits, nph = 4 * a.n_layers;
