@@ -51,7 +51,7 @@ namespace q4k {
 // epilogues) are compiled in; without them the kernel is the plain GEMV.
 template <int W, int S, bool F>
 __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_kernel(const Params p) {
-  constexpr int kWarps = W, kThreads = W * 32;
+  constexpr int kWarps = W;
   extern __shared__ __align__(16) uint8_t smem[];
   griddep_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -66,7 +66,9 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
   const uint32_t xs_s = smem_u32(xs);
   float* slots = reinterpret_cast<float*>(smem + p.slot_off);  // [ntl][kWarps][16]
   const uint64_t pol = l2_evict_first_policy();
-  for (int i = threadIdx.x; i < ntl * kWarps * 16; i += kThreads) slots[i] = 0.f;
+  // each warp zeroes its own partial slots (other warps read them only
+  // after the CTA barrier that ends the streaming loop)
+  for (int i = lane; i < ntl * 16; i += 32) slots[((i >> 4) * kWarps + warp) * 16 + (i & 15)] = 0.f;
 
   // Warp w takes the CTA's units w, w + kWarps, ...: at any moment the warps
   // stream neighbouring super-blocks of the same 16 rows (one long run of
@@ -133,8 +135,12 @@ __global__ void __launch_bounds__(W * 32, W == kWarpsSmall ? 2 : 1) gemv_q4k_ker
 #pragma unroll
   for (int s = 0; s < S; ++s) request(s);
   griddep_wait();
-  // ends with a CTA barrier (also orders the slot zeroing)
-  stage_x<W, F>(xs, reinterpret_cast<float*>(smem + p.red_off), p);
+  // When the column blocks are a multiple of the warps, warp w computes
+  // only the blocks w, w + kWarps, ... that it staged itself: no CTA
+  // barrier between staging and streaming.  (A runtime choice inside one
+  // kernel body: as a template parameter, two bodies, the decode step ran
+  // 1.5 % slower on B200 with the same stand-alone GEMV times.)
+  stage_x<W, F>(xs, reinterpret_cast<float*>(smem + p.red_off), p, p.nku % kWarps != 0);
 
   const uint32_t sh8 = 8u * (uint32_t)t;
   // byte selectors of this lane's sub-block scale (even / odd chunk c)

@@ -157,9 +157,11 @@ GI_DEVINL float4 ld_x4(const float4* p) {
 // Stage the activation vector: p.x, or in kXNorm mode RMSNorm(p.x) * p.x2
 // (pkg/math/kernels.go:9-19: float32 sum of squares, scale
 // float32(1 / sqrt(float64(mean + eps))), out = x * scale * w), computed by
-// every CTA from the same data in the same order.
+// every CTA from the same data in the same order.  Warp w stages the column
+// blocks w, w + W, ...; with cta_sync false it only waits for its own
+// stores, for a caller whose warps read nothing but the blocks they staged.
 template <int W, bool F, bool C = false>
-__device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
+__device__ void stage_x(uint8_t* xs, float* red, const Params& p, bool cta_sync = true) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int j = lane >> 2, q = lane & 3;
   const int offA = 64 * (j >> 1) + 32 * (j & 1) + 4 * q, offB = offA + 16;  // stage_unit's a, b
@@ -205,7 +207,10 @@ __device__ void stage_x(uint8_t* xs, float* red, const Params& p) {
       if (u < nku) stage_unit(xs + u * kUnitX, a[k], b[k], lane);
     }
   }
-  __syncthreads();
+  if (cta_sync)
+    __syncthreads();
+  else
+    __syncwarp();
 }
 
 // One unit: rows g and g+8 of a 16-row tile, 256 columns.  stage: the raw
