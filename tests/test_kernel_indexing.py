@@ -4,7 +4,8 @@ advances in place, across tiles of one matrix by dt * 15 rows, must equal
 the direct address of every unit (matrix, 16-row tile with clamped last
 rows, column block) for every CTA and warp, over matrix boundaries,
 ragged row counts, the interleaved SwiGLU tiles and warps-per-CTA both
-above and below the column-block count."""
+above and below the column-block count; and the warp-local activation
+staging and slot zeroing of the same kernel."""
 import pytest
 
 
@@ -135,3 +136,71 @@ def q6m_replay(rows, nku, W, ctas):
                                              (4100, 8, 8, 148), (40, 16, 8, 3)])
 def test_q6m_request_cursor(rows, nku, W, ctas):
     assert q6m_replay(rows, nku, W, ctas) > 0
+
+
+def staged_by(nku, W):
+    """stage_x (csrc/q4k.cuh): warp w stages the column blocks
+    u0 + k W, u0 = w, w + 4W, ..., k < 4 -- block u by warp u % W."""
+    owner = {}
+    for w in range(W):
+        for u0 in range(w, nku, 4 * W):
+            for k in range(4):
+                u = u0 + k * W
+                if u < nku:
+                    assert u not in owner
+                    owner[u] = w
+    assert sorted(owner) == list(range(nku))
+    return owner
+
+
+def computed_blocks(nku, W, ntl, warp):
+    """The compute cursor of gemv_q4k_kernel: units warp, warp + W, ... of
+    the CTA's ntl * nku units; (ctile, cku) advanced in place as the
+    kernel does.  Returns the (tile, column block) of each unit."""
+    ctile, cku = warp // nku, warp % nku
+    out = []
+    for i in range(warp, ntl * nku, W):
+        assert (ctile, cku) == divmod(i, nku)
+        out.append((ctile, cku))
+        cku += W
+        while cku >= nku:
+            cku -= nku
+            ctile += 1
+    return out
+
+
+@pytest.mark.parametrize("W", [8, 16])
+@pytest.mark.parametrize("nku", [1, 3, 4, 8, 16, 32, 43, 48, 112])
+def test_warp_local_staging(nku, W):
+    """The kernel skips the CTA barrier after staging exactly when
+    nku % W == 0; then every block a warp computes is one it staged itself
+    (on any number of tiles per CTA).  Otherwise some warp needs a block
+    another warp staged, and the barrier is required."""
+    owner = staged_by(nku, W)
+    foreign = False
+    for ntl in (1, 2, 3, 5):
+        for warp in range(W):
+            for _tile, cku in computed_blocks(nku, W, ntl, warp):
+                if owner[cku] != warp:
+                    foreign = True
+                    assert nku % W != 0, (nku, W, ntl, warp, cku)
+    assert foreign == (nku % W != 0)
+
+
+def test_warp_local_slot_zeroing():
+    """Each warp zeroes slots[(t * W + warp) * 16 + j] for its CTA's ntl
+    tiles: together the warps cover the whole [ntl][W][16] array once, and
+    every slot a warp writes at the end of a tile is one it zeroed."""
+    for W in (8, 16):
+        for ntl in (1, 2, 7):
+            seen = []
+            for warp in range(W):
+                mine = set()
+                for i in range(ntl * 16):  # lanes i = lane, lane + 32, ...
+                    s = ((i >> 4) * W + warp) * 16 + (i & 15)
+                    mine.add(s)
+                    seen.append(s)
+                for nku in (3, 16, 43):
+                    for tile, _ in computed_blocks(nku, W, ntl, warp):
+                        assert {(tile * W + warp) * 16 + j for j in range(16)} <= mine
+            assert sorted(seen) == list(range(ntl * W * 16))
