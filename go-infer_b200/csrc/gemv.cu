@@ -448,11 +448,16 @@ GI_DEVINL void stage_unit(uint8_t* xu, const float* xunit, int lane) {
   if (lane == 0) reinterpret_cast<float*>(xu + 1024)[0] = exp2i(-e);
 }
 
+// Warp w stages the column blocks w, w + W, ...; with cta_sync false it
+// waits only for its own stores (its caller's warps read no other blocks).
 template <int W>
-__device__ void stage_x(uint8_t* xs, const Params& p) {
+__device__ void stage_x(uint8_t* xs, const Params& p, bool cta_sync) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int u = warp; u < p.nku; u += W) stage_unit(xs + u * kUnitX, p.x + 256 * u, lane);
-  __syncthreads();
+  if (cta_sync)
+    __syncthreads();
+  else
+    __syncwarp();
 }
 
 GI_DEVINL float h2f(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
@@ -497,7 +502,7 @@ GI_DEVINL void compute_unit(uint32_t stage, uint32_t xu, int g, int t, float Wt,
 
 template <int W, int S>
 __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gemv_q80m_kernel(const Params p) {
-  constexpr int kWarps = W, kThreads = W * 32;
+  constexpr int kWarps = W;
   extern __shared__ __align__(16) uint8_t smem[];
   griddep_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -510,7 +515,9 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gemv_q80m_kernel(const
   const uint32_t xs_s = smem_u32(xs);
   float* slots = reinterpret_cast<float*>(smem + p.slot_off);  // [ntl][kWarps][16]
   const uint64_t pol = l2_evict_first_policy();
-  for (int i = threadIdx.x; i < ntl * kWarps * 16; i += kThreads) slots[i] = 0.f;
+  // each warp zeroes its own partial slots (other warps read them only
+  // after the CTA barrier that ends the streaming loop)
+  for (int i = lane; i < ntl * 16; i += 32) slots[((i >> 4) * kWarps + warp) * 16 + (i & 15)] = 0.f;
 
   // Request cursor: lane L copies row L/2 of the unit, chunks L%2, L%2 + 2,
   // ... (adjacent lanes fetch adjacent 16-byte chunks of a row).
@@ -546,7 +553,9 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gemv_q80m_kernel(const
 #pragma unroll
   for (int s = 0; s < S; ++s) request(s);
   griddep_wait();
-  stage_x<W>(xs, p);  // ends with a CTA barrier (also orders the slot zeroing)
+  // no CTA barrier when warp w computes only the blocks it staged (the
+  // column blocks a multiple of the warps), as in the Q4_K kernel
+  stage_x<W>(xs, p, p.nku % kWarps != 0);
 
   const float Wt = t == 0 ? 65536.f : (t == 1 ? 1.f : 0.f);
   int ctile = warp / p.nku, cku = warp - ctile * p.nku;
@@ -1205,11 +1214,16 @@ GI_DEVINL void stage_unit(uint8_t* xu, const float* xunit, int lane) {
   if (lane == 0) reinterpret_cast<float*>(xu + 1280)[0] = exp2i(-e);
 }
 
+// Warp w stages the column blocks w, w + W, ...; with cta_sync false it
+// waits only for its own stores (its caller's warps read no other blocks).
 template <int W>
-__device__ void stage_x(uint8_t* xs, const Params& p) {
+__device__ void stage_x(uint8_t* xs, const Params& p, bool cta_sync) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int u = warp; u < p.nku; u += W) stage_unit(xs + u * kUnitX, p.x + 256 * u, lane);
-  __syncthreads();
+  if (cta_sync)
+    __syncthreads();
+  else
+    __syncwarp();
 }
 
 // Word at a 2-byte-aligned shared address: one load, or (odd) two aligned
@@ -1280,7 +1294,7 @@ GI_DEVINL void compute_unit(uint32_t blk, uint32_t xu, int g, int t, float W0, f
 
 template <int W, int S>
 __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gemv_q6m_kernel(const Params p) {
-  constexpr int kWarps = W, kThreads = W * 32;
+  constexpr int kWarps = W;
   extern __shared__ __align__(16) uint8_t smem[];
   griddep_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1293,7 +1307,9 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gemv_q6m_kernel(const 
   const uint32_t xs_s = smem_u32(xs);
   float* slots = reinterpret_cast<float*>(smem + p.slot_off);  // [ntl][kWarps][16]
   const uint64_t pol = l2_evict_first_policy();
-  for (int i = threadIdx.x; i < ntl * kWarps * 16; i += kThreads) slots[i] = 0.f;
+  // each warp zeroes its own partial slots (other warps read them only
+  // after the CTA barrier that ends the streaming loop)
+  for (int i = lane; i < ntl * 16; i += 32) slots[((i >> 4) * kWarps + warp) * 16 + (i & 15)] = 0.f;
 
   // Request cursor: lane L copies row L/2 of the unit, chunks L%2, L%2 + 2,
   // ..., L%2 + 12 of the 14 that cover the row's block.
@@ -1328,7 +1344,9 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gemv_q6m_kernel(const 
 #pragma unroll
   for (int s = 0; s < S; ++s) request(s);
   griddep_wait();
-  stage_x<W>(xs, p);  // ends with a CTA barrier (also orders the slot zeroing)
+  // no CTA barrier when warp w computes only the blocks it staged (the
+  // column blocks a multiple of the warps), as in the Q4_K kernel
+  stage_x<W>(xs, p, p.nku % kWarps != 0);
 
   // limb weights of this lane's two columns: limbs 2(t&1), 2(t&1)+1
   const float W0 = (t & 1) ? 256.f : 16777216.f, W1 = (t & 1) ? 1.f : 65536.f;
