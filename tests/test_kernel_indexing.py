@@ -140,7 +140,9 @@ def test_q6m_request_cursor(rows, nku, W, ctas):
 
 def staged_by(nku, W):
     """stage_x (csrc/q4k.cuh): warp w stages the column blocks
-    u0 + k W, u0 = w, w + 4W, ..., k < 4 -- block u by warp u % W."""
+    u0 + k W, u0 = w, w + 4W, ..., k < 4 -- block u by warp u % W.  The
+    Q8_0 and Q6_K tensor-core kernels' stage_x (csrc/gemv.cu: u = w, w + W,
+    ...) assign the same owners."""
     owner = {}
     for w in range(W):
         for u0 in range(w, nku, 4 * W):
@@ -150,6 +152,7 @@ def staged_by(nku, W):
                     assert u not in owner
                     owner[u] = w
     assert sorted(owner) == list(range(nku))
+    assert owner == {u: w for w in range(W) for u in range(w, nku, W)}
     return owner
 
 
