@@ -207,3 +207,20 @@ def test_warp_local_slot_zeroing():
                     for tile, _ in computed_blocks(nku, W, ntl, warp):
                         assert {(tile * W + warp) * 16 + j for j in range(16)} <= mine
             assert sorted(seen) == list(range(ntl * W * 16))
+
+
+@pytest.mark.parametrize("nku,W", [(43, 16), (43, 8), (3, 8), (112, 16), (5, 16)])
+def test_single_tile_ctas_read_only_their_own_blocks(nku, W):
+    """A CTA with one tile computes unit i on block i, which warp i % W
+    staged -- for any column-block count -- and with two tiles of the
+    config-2 down shape (43 blocks, 16 warps) every warp first streams 2-3
+    units of its own blocks (the room a split barrier would have)."""
+    owner = staged_by(nku, W)
+    for warp in range(W):
+        assert all(owner[c] == warp for _t, c in computed_blocks(nku, W, 1, warp))
+    if (nku, W) == (43, 16):
+        lead = []
+        for warp in range(W):
+            blocks = computed_blocks(nku, W, 2, warp)
+            lead.append(next(i for i, (_t, c) in enumerate(blocks) if owner[c] != warp))
+        assert lead == [3] * 11 + [2] * 5
