@@ -44,3 +44,7 @@ func FFN(x []float32, norm, gate, up, down unsafe.Pointer, dim, hidden int, eps 
 
 func ConnectTP(rank, world, maxDim int, allGather func([]byte) [][]byte) error { return errUnsupported }
 func CloseTP() error                                                          { return errUnsupported }
+
+func SetPDL(on bool) error         { return errUnsupported }
+func SetQ6KMMA(on bool) error      { return errUnsupported }
+func SetPrefillPair(on bool) error { return errUnsupported }

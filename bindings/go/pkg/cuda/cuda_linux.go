@@ -320,3 +320,33 @@ func CloseTP() error {
 	}
 	return nil
 }
+
+// The launch switches of this library (no pkg/metal counterparts: each
+// chooses between two ways this library runs the same arithmetic).
+// SetPDL: programmatic dependent launch for stand-alone calls (off by
+// default; the decode graphs always use it).  SetQ6KMMA: Q6_K GEMVs on the
+// int8 tensor cores (on by default) or the CUDA cores.  SetPrefillPair:
+// batched GEMMs on CTA pairs (off by default, slower on B200, bit-identical).
+func SetPDL(on bool) error { return setSwitch("gi_cuda_set_pdl", C.gi_cuda_set_pdl(cBool(on))) }
+
+func SetQ6KMMA(on bool) error {
+	return setSwitch("gi_cuda_set_q6k_mma", C.gi_cuda_set_q6k_mma(cBool(on)))
+}
+
+func SetPrefillPair(on bool) error {
+	return setSwitch("gi_cuda_set_prefill_pair", C.gi_cuda_set_prefill_pair(cBool(on)))
+}
+
+func cBool(on bool) C.int {
+	if on {
+		return 1
+	}
+	return 0
+}
+
+func setSwitch(what string, rc C.int) error {
+	if rc != 0 {
+		return lastErr(what, rc)
+	}
+	return nil
+}
